@@ -1,0 +1,302 @@
+"""ctypes binding of libadai_b200.so (the C ABI declared in include/adai_b200.h).
+
+Error mapping follows the reference's exceptions on the same conditions:
+ADAI_B200_ERR_INVALID_ARGUMENT -> ValueError (std::invalid_argument),
+ADAI_B200_ERR_OUT_OF_RANGE -> IndexError (std::out_of_range), everything else -> RuntimeError
+(std::runtime_error), with DeviceTimeout / NonFiniteLogits / NoDevice as subclasses.
+
+There is no CPU fallback: if the library is missing, `load()` raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from .config import ModelConfig
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libadai_b200.so")
+
+OK, INVALID, OUT_OF_RANGE, CUDA, TIMEOUT, NONFINITE, STATE, NO_DEVICE = range(8)
+
+
+class AdaiError(RuntimeError):
+    pass
+
+
+class DeviceTimeout(AdaiError):
+    pass
+
+
+class NonFiniteLogits(AdaiError):
+    pass
+
+
+class NoDevice(AdaiError):
+    pass
+
+
+class StateError(AdaiError):
+    pass
+
+
+EXPORTS = [
+    "adai_b200_last_error", "adai_b200_ctx_create", "adai_b200_ctx_destroy",
+    "adai_b200_ctx_synchronize", "adai_b200_ctx_memory", "adai_b200_ctx_stream",
+    "adai_b200_model_tensor_count", "adai_b200_model_upload", "adai_b200_kv_create",
+    "adai_b200_kv_destroy", "adai_b200_kv_reset", "adai_b200_kv_length", "adai_b200_encode",
+    "adai_b200_decode_step", "adai_b200_generate", "adai_b200_sgemm", "adai_b200_weight_create",
+    "adai_b200_weight_destroy", "adai_b200_sgemm_prepared", "adai_b200_decode_attention",
+    "adai_b200_layernorm", "adai_b200_ctx_last_timing", "adai_b200_profile_step",
+    "adai_b200_kv_clear_self",
+]
+
+# Kernel classes of adai_b200_profile_step (adai_b200_kernel_class).
+KERNEL_CLASSES = ("gemm", "self_attention", "cross_attention", "norm", "lm_head", "other")
+
+
+class ModelDesc(C.Structure):
+    _fields_ = [(n, C.c_int) for n in
+                ("vocab", "d_model", "n_heads", "d_ff", "enc_layers", "dec_layers", "max_seq")]
+
+    @classmethod
+    def of(cls, cfg: ModelConfig) -> "ModelDesc":
+        return cls(*cfg.as_cfg())
+
+
+_lib = None
+_vp = C.c_void_p
+_ip = C.POINTER(C.c_int)
+
+
+def load() -> C.CDLL:
+    """Loads libadai_b200.so (built by `make -C adai_b200/csrc`); raises if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise FileNotFoundError(
+            f"{LIB_PATH} is not built; run `make -C adai_b200/csrc` (or __graft_entry__.build())")
+    lib = C.CDLL(LIB_PATH)
+    lib.adai_b200_last_error.restype = C.c_char_p
+    lib.adai_b200_ctx_create.argtypes = [C.c_int, C.c_float, C.POINTER(_vp)]
+    lib.adai_b200_ctx_destroy.argtypes = [_vp]
+    lib.adai_b200_ctx_synchronize.argtypes = [_vp, C.c_double]
+    lib.adai_b200_ctx_memory.argtypes = [_vp, C.POINTER(C.c_ulonglong)]
+    lib.adai_b200_ctx_stream.argtypes = [_vp]
+    lib.adai_b200_ctx_stream.restype = _vp
+    lib.adai_b200_model_tensor_count.argtypes = [C.POINTER(ModelDesc)]
+    lib.adai_b200_model_upload.argtypes = [_vp, C.POINTER(ModelDesc), C.POINTER(_vp), _vp]
+    lib.adai_b200_kv_create.argtypes = [_vp, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]
+    lib.adai_b200_kv_destroy.argtypes = [_vp, _vp]
+    lib.adai_b200_kv_reset.argtypes = [_vp, _vp, C.c_int]
+    lib.adai_b200_kv_clear_self.argtypes = [_vp, _vp, C.c_int]
+    lib.adai_b200_kv_length.argtypes = [_vp, _vp, C.c_int, _ip, _ip]
+    lib.adai_b200_encode.argtypes = [_vp, _vp, C.c_int, _vp, _vp, _vp, _vp]
+    lib.adai_b200_decode_step.argtypes = [_vp, _vp, C.c_int, _vp, _vp, _vp, _vp]
+    lib.adai_b200_generate.argtypes = [_vp, _vp, C.c_int, _vp, _vp, C.c_int, _vp]
+    lib.adai_b200_sgemm.argtypes = [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp]
+    lib.adai_b200_weight_create.argtypes = [_vp, _vp, C.c_int, C.c_int, C.POINTER(_vp)]
+    lib.adai_b200_weight_destroy.argtypes = [_vp, _vp]
+    lib.adai_b200_sgemm_prepared.argtypes = [_vp, C.c_int, _vp, _vp, _vp]
+    lib.adai_b200_decode_attention.argtypes = [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp,
+                                               _vp, _vp, _vp, C.c_int, _vp]
+    lib.adai_b200_layernorm.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int]
+    lib.adai_b200_ctx_last_timing.argtypes = [_vp, C.POINTER(C.c_double), _ip]
+    lib.adai_b200_profile_step.argtypes = [_vp, _vp, C.c_int, _vp, _vp, C.c_int, _vp, _vp, _vp,
+                                           _vp]
+    _lib = lib
+    return lib
+
+
+def check(rc: int) -> None:
+    if rc == OK:
+        return
+    msg = load().adai_b200_last_error().decode(errors="replace")
+    if rc == INVALID:
+        raise ValueError(msg)
+    if rc == OUT_OF_RANGE:
+        raise IndexError(msg)
+    if rc == TIMEOUT:
+        raise DeviceTimeout(msg)
+    if rc == NONFINITE:
+        raise NonFiniteLogits(msg)
+    if rc == NO_DEVICE:
+        raise NoDevice(msg)
+    if rc == STATE:
+        raise StateError(msg)
+    raise AdaiError(msg)
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.int32)
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+class Context:
+    """One GPU (the reference GPUManager's device + stream). Use one per device, one host thread
+    at a time."""
+
+    def __init__(self, device: int = 0, mem_fraction: float = 0.0):
+        self.lib = load()
+        h = _vp()
+        check(self.lib.adai_b200_ctx_create(device, mem_fraction, C.byref(h)))
+        self.h = h
+        self.device = device
+        self.cfg: ModelConfig | None = None
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            check(self.lib.adai_b200_ctx_destroy(self.h))
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def stream(self) -> int:
+        return self.lib.adai_b200_ctx_stream(self.h) or 0
+
+    def synchronize(self, timeout_s: float = 0.0) -> None:
+        check(self.lib.adai_b200_ctx_synchronize(self.h, timeout_s))
+
+    def memory_bytes(self) -> int:
+        v = C.c_ulonglong()
+        check(self.lib.adai_b200_ctx_memory(self.h, C.byref(v)))
+        return v.value
+
+    def upload(self, cfg: ModelConfig, weights, pe_table=None) -> None:
+        ws = [np.ascontiguousarray(w, np.float32) for w in weights]
+        desc = ModelDesc.of(cfg)
+        n = self.lib.adai_b200_model_tensor_count(C.byref(desc))
+        if n != len(ws):
+            raise ValueError(f"model needs {n} tensors, got {len(ws)}")
+        arr = (_vp * len(ws))(*[w.ctypes.data for w in ws])
+        pe = None if pe_table is None else np.ascontiguousarray(pe_table, np.float32)
+        check(self.lib.adai_b200_model_upload(self.h, C.byref(desc), arr, _ptr(pe)))
+        self.cfg = cfg
+
+    def kv_arena(self, max_slots: int, self_capacity: int, cross_capacity: int) -> "KVArena":
+        return KVArena(self, max_slots, self_capacity, cross_capacity)
+
+    # ---- op level (device pointers: ints, e.g. torch tensor .data_ptr()) ----
+    def sgemm(self, m, n, k, A_ptr, B_ptr, C_ptr) -> None:
+        check(self.lib.adai_b200_sgemm(self.h, m, n, k, A_ptr, B_ptr, C_ptr))
+
+    def weight(self, B_ptr, k, n) -> "PreparedWeight":
+        return PreparedWeight(self, B_ptr, k, n)
+
+    def decode_attention(self, B, H, capacity, q, k_new, v_new, k_cache, v_cache, lens, max_len,
+                         out) -> None:
+        check(self.lib.adai_b200_decode_attention(self.h, B, H, capacity, q, k_new, v_new,
+                                                  k_cache, v_cache, lens, max_len, out))
+
+    def layernorm(self, x, gamma, beta, out, rows, D) -> None:
+        check(self.lib.adai_b200_layernorm(self.h, x, gamma, beta, out, rows, D))
+
+    def last_timing(self) -> tuple[float, int]:
+        """(device ms of the last generate() decode loop, kernels launched per step)."""
+        ms, k = C.c_double(), C.c_int()
+        check(self.lib.adai_b200_ctx_last_timing(self.h, C.byref(ms), C.byref(k)))
+        return ms.value, k.value
+
+
+class PreparedWeight:
+    def __init__(self, ctx: Context, B_ptr, k, n):
+        self.ctx, self.k, self.n = ctx, k, n
+        h = _vp()
+        check(ctx.lib.adai_b200_weight_create(ctx.h, B_ptr, k, n, C.byref(h)))
+        self.h = h
+
+    def matmul(self, m, A_ptr, C_ptr) -> None:
+        check(self.ctx.lib.adai_b200_sgemm_prepared(self.ctx.h, m, A_ptr, self.h, C_ptr))
+
+    def close(self):
+        if getattr(self, "h", None):
+            check(self.ctx.lib.adai_b200_weight_destroy(self.ctx.h, self.h))
+            self.h = None
+
+
+class KVArena:
+    """Per-sequence self/cross caches for `max_slots` sequences (the reference DecoderKVCache,
+    one per slot), plus the decode entry points that use them."""
+
+    def __init__(self, ctx: Context, max_slots: int, self_capacity: int, cross_capacity: int):
+        self.ctx, self.lib = ctx, ctx.lib
+        self.max_slots = max_slots
+        self.self_capacity = self_capacity
+        self.cross_capacity = cross_capacity
+        h = _vp()
+        check(self.lib.adai_b200_kv_create(ctx.h, max_slots, self_capacity, cross_capacity,
+                                           C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None) and getattr(self.ctx, "h", None):
+            check(self.lib.adai_b200_kv_destroy(self.ctx.h, self.h))
+        self.h = None
+
+    def reset(self, slot: int) -> None:
+        check(self.lib.adai_b200_kv_reset(self.ctx.h, self.h, slot))
+
+    def clear_self(self, slot: int) -> None:
+        check(self.lib.adai_b200_kv_clear_self(self.ctx.h, self.h, slot))
+
+    def length(self, slot: int) -> tuple[int, int]:
+        a, b = C.c_int(), C.c_int()
+        check(self.lib.adai_b200_kv_length(self.ctx.h, self.h, slot, C.byref(a), C.byref(b)))
+        return a.value, b.value
+
+    def encode(self, slots, sources, want_output=False):
+        """Encoder prefill of each source (a list of id arrays) into its slot."""
+        slots = _i32(slots)
+        lens = _i32([len(s) for s in sources])
+        ids = _i32(np.concatenate([np.asarray(s, np.int32) for s in sources]))
+        out = (np.empty((int(lens.sum()), self.ctx.cfg.d_model), np.float32)
+               if want_output else None)
+        check(self.lib.adai_b200_encode(self.ctx.h, self.h, len(slots), _ptr(slots), _ptr(ids),
+                                        _ptr(lens), _ptr(out)))
+        return out
+
+    def decode_step(self, slots, ids, want_logits=False):
+        slots, ids = _i32(slots), _i32(ids)
+        B = slots.size
+        nxt = np.empty(B, np.int32)
+        lg = np.empty((B, self.ctx.cfg.vocab), np.float32) if want_logits else None
+        check(self.lib.adai_b200_decode_step(self.ctx.h, self.h, B, _ptr(slots), _ptr(ids),
+                                             _ptr(nxt), _ptr(lg)))
+        return nxt, lg
+
+    def profile_step(self, slots, ids) -> dict:
+        """One eager decode step with CUDA events around every kernel; per kernel class:
+        ms, algorithmic bytes, flops, launches."""
+        slots, ids = _i32(slots), _i32(ids)
+        n = len(KERNEL_CLASSES)
+        ms, by, fl = (np.zeros(n, np.float64) for _ in range(3))
+        ln = np.zeros(n, np.int32)
+        check(self.lib.adai_b200_profile_step(self.ctx.h, self.h, slots.size, _ptr(slots),
+                                              _ptr(ids), n, _ptr(ms), _ptr(by), _ptr(fl),
+                                              _ptr(ln)))
+        return {k: dict(ms=float(ms[i]), bytes=float(by[i]), flops=float(fl[i]),
+                        launches=int(ln[i])) for i, k in enumerate(KERNEL_CLASSES)}
+
+    def generate(self, slots, first_ids, steps):
+        slots, first = _i32(slots), _i32(first_ids)
+        out = np.empty((slots.size, steps), np.int32)
+        check(self.lib.adai_b200_generate(self.ctx.h, self.h, slots.size, _ptr(slots),
+                                          _ptr(first), steps, _ptr(out)))
+        return out

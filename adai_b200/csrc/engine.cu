@@ -1,0 +1,1478 @@
+// engine.cu — host runtime behind the C ABI (include/adai_b200.h): per-GPU context, model
+// upload, KV-cache arena, encoder prefill, the stacked decode step and its CUDA-graph replay.
+//
+// Reference behaviour this mirrors:
+//   GPUManager (src/gpu/GPUUtils.hpp:98-530): one device, one stream, a memory budget.
+//   GPUDecoderKVCache (src/gpu/MatrixGPU.hpp:563-623): fixed-capacity per-layer caches.
+//   LLMDecoder::gpu_decode_step (src/Decoder.cpp:566-608) / forward_with_cache (:210-287), for B
+//   stacked sequences instead of one: embed + PE, L pre-LN blocks, final LN, LM head, argmax.
+//   LLMEncoder::encode_with_mask (src/LLMEncoder.cpp:120-142) + CrossAttention's first-call K/V.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <set>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <tuple>
+#include <vector>
+
+#include "../../include/adai_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace adai_b200;
+
+namespace adai_b200 {
+bool layernorm_width_supported(int D);
+}
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct Status : std::runtime_error {
+    int code;
+    Status(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+[[noreturn]] void fail(int code, const std::string& msg) { throw Status(code, msg); }
+
+void cuda_ok(cudaError_t e, const char* what) {
+    if (e != cudaSuccess)
+        fail(ADAI_B200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+void launch_ok(int e, const char* what) {
+    if (e != 0) fail(ADAI_B200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(static_cast<cudaError_t>(e)));
+}
+
+template <class Fn>
+int guarded(Fn&& fn) {
+    try {
+        fn();
+        g_last_error.clear();
+        return ADAI_B200_OK;
+    } catch (const Status& s) {
+        g_last_error = s.what();
+        return s.code;
+    } catch (const std::bad_alloc&) {
+        g_last_error = "host allocation failed";
+        return ADAI_B200_ERR_CUDA;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return ADAI_B200_ERR_CUDA;
+    }
+}
+
+inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+double wait_timeout_seconds() {
+    const char* s = std::getenv("ADAI_B200_WAIT_TIMEOUT_SECONDS");
+    if (s && *s) {
+        const double v = std::atof(s);
+        if (v > 0) return v;
+    }
+    return 120.0;
+}
+
+constexpr int kEncRows = 16384;  // encoder prefill rows per chunk
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------
+struct EncLayerW {
+    const float *ln1g, *ln1b, *ln2g, *ln2b, *b1, *b2;
+    TcWeight qkv, o, w1, w2;
+};
+struct DecLayerW {
+    const float *ln1g, *ln1b, *ln2g, *ln2b, *ln3g, *ln3b, *b1, *b2;
+    TcWeight qkv, o, cq, ckv, co, w1, w2;
+};
+
+struct Model {
+    adai_b200_model_desc d{};
+    float* pe = nullptr;
+    float* enc_embed = nullptr;
+    float* dec_embed = nullptr;
+    const float *enc_lnf_g = nullptr, *enc_lnf_b = nullptr, *dec_lnf_g = nullptr,
+                *dec_lnf_b = nullptr, *head_b = nullptr;
+    std::vector<EncLayerW> enc;
+    std::vector<DecLayerW> dec;
+    TcWeight head;
+    std::vector<void*> owned;
+};
+
+struct StepBufs {
+    int rows = 0;  // allocated rows (multiple of 128)
+    float *x = nullptr, *nrm_hi = nullptr, *nrm_lo = nullptr, *qkv = nullptr, *attn_hi = nullptr,
+          *attn_lo = nullptr, *qc = nullptr, *h_hi = nullptr, *h_lo = nullptr,
+          *logits = nullptr;
+    int *ids = nullptr, *next = nullptr, *slots = nullptr, *nonfinite = nullptr,
+        *nonfinite_any = nullptr;
+};
+
+struct EncBufs {
+    int rows = 0;
+    float *x = nullptr, *nrm_hi = nullptr, *nrm_lo = nullptr, *qkv = nullptr, *attn_hi = nullptr,
+          *attn_lo = nullptr, *h_hi = nullptr, *h_lo = nullptr, *out = nullptr;
+    int *ids = nullptr, *row_slot = nullptr, *row_pos = nullptr, *offsets = nullptr,
+        *lens = nullptr;
+};
+
+struct adai_b200_kv {
+    int max_slots = 0, self_cap = 0, cross_cap = 0, L = 0, H = 0;
+    float *self_k = nullptr, *self_v = nullptr, *cross_k = nullptr, *cross_v = nullptr;
+    int *d_self_len = nullptr, *d_cross_len = nullptr;
+    int* d_hist = nullptr;  // [max_slots][self_cap]: the argmax produced at each position
+    std::vector<int> self_len, cross_len;
+    long long self_slot_stride() const { return static_cast<long long>(H) * self_cap * 64; }
+    long long cross_slot_stride() const { return static_cast<long long>(H) * cross_cap * 64; }
+    float* self_k_layer(int l) const { return self_k + static_cast<size_t>(l) * max_slots * self_slot_stride(); }
+    float* self_v_layer(int l) const { return self_v + static_cast<size_t>(l) * max_slots * self_slot_stride(); }
+    float* cross_k_layer(int l) const { return cross_k + static_cast<size_t>(l) * max_slots * cross_slot_stride(); }
+    float* cross_v_layer(int l) const { return cross_v + static_cast<size_t>(l) * max_slots * cross_slot_stride(); }
+};
+
+struct adai_b200_weight {
+    TcWeight w;
+    int K = 0;     // the caller's inner dimension
+    int Kpad = 0;  // K rounded up to a multiple of 4 (16-byte rows for TMA)
+};
+
+struct GraphKey {
+    const adai_b200_kv* kv;
+    int B;
+    int flags;
+    bool operator<(const GraphKey& o) const {
+        return std::tie(kv, B, flags) < std::tie(o.kv, o.B, o.flags);
+    }
+};
+
+enum StepFlags { kStepLogits = 1, kStepAdvanceIds = 2 };
+
+// Per-launch CUDA-event spans of a profiled (eager) decode step, with the algorithmic bytes and
+// flops of each launch, grouped by kernel class (adai_b200_kernel_class in the header).
+struct Span {
+    cudaEvent_t a, b;
+    int cls;
+    double bytes, flops;
+};
+struct Profiler {
+    std::vector<Span> spans;
+    double sum_self_rows = 0;   // sum over the batch of rows attended by self-attention
+    double sum_cross_rows = 0;  // ... by cross-attention
+};
+
+struct adai_b200_ctx {
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    size_t mem_cap = 0, mem_used = 0;
+    std::map<void*, size_t> allocs;
+    int* d_err = nullptr;
+    bool unusable = false;
+    std::unique_ptr<Model> model;
+    std::set<adai_b200_kv*> kvs;
+    StepBufs sb;
+    EncBufs eb;
+    GemmScratch gs;
+    float* attn_ws = nullptr;
+    size_t attn_ws_floats = 0;
+    int* attn_tickets = nullptr;
+    int attn_n_tickets = 0;
+    float *op_a_hi = nullptr, *op_a_lo = nullptr;
+    size_t op_a_floats = 0;
+    int* h_pin = nullptr;  // pinned staging for ids / slots / lengths
+    size_t h_pin_ints = 0;
+    std::map<GraphKey, cudaGraphExec_t> graphs;
+    std::map<GraphKey, int> graph_kernels;
+    Profiler* prof = nullptr;
+    double last_decode_ms = 0.0;
+    int last_kernels_per_step = 0;
+
+    void* dalloc(size_t bytes) {
+        if (bytes == 0) bytes = 16;
+        if (mem_cap && mem_used + bytes > mem_cap)
+            fail(ADAI_B200_ERR_CUDA, "device memory budget (mem_fraction) exceeded: need " +
+                                         std::to_string(bytes) + " more bytes, " +
+                                         std::to_string(mem_cap - mem_used) + " left");
+        void* p = nullptr;
+        cuda_ok(cudaMalloc(&p, bytes), "cudaMalloc");
+        allocs[p] = bytes;
+        mem_used += bytes;
+        return p;
+    }
+    template <class T>
+    T* dalloc_t(size_t n) {
+        return static_cast<T*>(dalloc(n * sizeof(T)));
+    }
+    template <class T>
+    T* dzalloc_t(size_t n) {
+        T* p = dalloc_t<T>(n);
+        cuda_ok(cudaMemsetAsync(p, 0, n * sizeof(T), stream), "cudaMemset");
+        return p;
+    }
+    void dfree(void* p) {
+        if (!p) return;
+        auto it = allocs.find(p);
+        if (it != allocs.end()) {
+            mem_used -= it->second;
+            allocs.erase(it);
+        }
+        cudaFree(p);
+    }
+    void clear_graphs() {
+        for (auto& kvp : graphs) cudaGraphExecDestroy(kvp.second);
+        graphs.clear();
+        graph_kernels.clear();
+    }
+    void check_usable() const {
+        if (unusable)
+            fail(ADAI_B200_ERR_STATE, "context is unusable after an earlier device timeout or fault");
+    }
+    int* pinned(size_t n) {
+        if (n > h_pin_ints) {
+            // copies queued from the old buffer must finish before it is released
+            cuda_ok(cudaStreamSynchronize(stream), "sync before staging growth");
+            if (h_pin) cudaFreeHost(h_pin);
+            h_pin = nullptr;
+            h_pin_ints = 0;
+            cuda_ok(cudaMallocHost(&h_pin, n * sizeof(int)), "cudaMallocHost");
+            h_pin_ints = n;
+        }
+        return h_pin;
+    }
+    // Bounded host wait (GPU_WAIT_TIMEOUT_SECONDS semantics), then the device error word.
+    void sync(double timeout_s) {
+        cudaEvent_t ev;
+        cuda_ok(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "cudaEventCreate");
+        cuda_ok(cudaEventRecord(ev, stream), "cudaEventRecord");
+        const auto t0 = std::chrono::steady_clock::now();
+        while (true) {
+            const cudaError_t q = cudaEventQuery(ev);
+            if (q == cudaSuccess) break;
+            if (q != cudaErrorNotReady) {
+                cudaEventDestroy(ev);
+                unusable = true;
+                fail(ADAI_B200_ERR_CUDA, std::string("device error: ") + cudaGetErrorString(q));
+            }
+            const double el =
+                std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+            if (el > timeout_s) {
+                cudaEventDestroy(ev);
+                unusable = true;
+                fail(ADAI_B200_ERR_TIMEOUT,
+                     "device wait exceeded " + std::to_string(timeout_s) + " s");
+            }
+            std::this_thread::yield();
+        }
+        cudaEventDestroy(ev);
+        int herr = 0;
+        cuda_ok(cudaMemcpy(&herr, d_err, sizeof(int), cudaMemcpyDeviceToHost), "read error word");
+        if (herr != 0) {
+            cuda_ok(cudaMemset(d_err, 0, sizeof(int)), "clear error word");
+            if (herr >= 101 && herr <= 103) {
+                unusable = true;
+                fail(ADAI_B200_ERR_TIMEOUT,
+                     "a kernel gave up waiting (code " + std::to_string(herr) + ")");
+            }
+            fail(ADAI_B200_ERR_OUT_OF_RANGE,
+                 "a kernel rejected its input (code " + std::to_string(herr) + ")");
+        }
+    }
+
+    // ------------------------------------------------------------------------------------------
+    void ensure_gemm_scratch(const GemmPlan& p) {
+        const size_t ws = gemm_ws_floats(p);
+        const int tk = p.m_tiles * p.n_tiles;
+        const size_t ae = gemm_arg_entries(p);
+        if (ws > gs.ws_floats || tk > gs.n_tickets || ae > gs.arg_entries) {
+            cuda_ok(cudaStreamSynchronize(stream), "sync before scratch growth");
+            clear_graphs();
+            if (ws > gs.ws_floats) {
+                dfree(gs.ws);
+                gs.ws_floats = std::max(ws, gs.ws_floats * 2);
+                gs.ws = dalloc_t<float>(gs.ws_floats);
+            }
+            if (tk > gs.n_tickets) {
+                dfree(gs.tickets);
+                gs.n_tickets = std::max(tk, 1024);
+                gs.tickets = dzalloc_t<int>(gs.n_tickets);
+            }
+            if (ae > gs.arg_entries) {
+                dfree(gs.arg_val);
+                dfree(gs.arg_idx);
+                gs.arg_entries = std::max(ae, gs.arg_entries * 2);
+                gs.arg_val = dalloc_t<float>(gs.arg_entries);
+                gs.arg_idx = dalloc_t<int>(gs.arg_entries);
+            }
+        }
+    }
+    void ensure_attn_scratch(int B, int H, int max_len) {
+        const size_t f = decode_attn_ws_floats(B, H, max_len);
+        const int tk = B * H;
+        if (f > attn_ws_floats || tk > attn_n_tickets) {
+            cuda_ok(cudaStreamSynchronize(stream), "sync before scratch growth");
+            clear_graphs();
+            if (f > attn_ws_floats) {
+                dfree(attn_ws);
+                attn_ws_floats = f;
+                attn_ws = dalloc_t<float>(f);
+            }
+            if (tk > attn_n_tickets) {
+                dfree(attn_tickets);
+                attn_n_tickets = tk;
+                attn_tickets = dzalloc_t<int>(tk);
+            }
+        }
+    }
+
+    void gemm(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e) {
+        const GemmPlan p = gemm_plan(M, w.N, w.K, e.flags, num_sms);
+        ensure_gemm_scratch(p);
+        launch_ok(gemm_launch(a, M, w, e, p, gs, d_err, stream), "gemm launch");
+    }
+};
+
+namespace {
+
+// Runs `fn` (which enqueues launches on the context stream) between two recorded events when a
+// profiled step is being recorded; otherwise just runs it.
+template <class Fn>
+void timed(adai_b200_ctx* c, int cls, double bytes, double flops, Fn&& fn) {
+    if (!c->prof) {
+        fn();
+        return;
+    }
+    Span sp{};
+    sp.cls = cls;
+    sp.bytes = bytes;
+    sp.flops = flops;
+    cuda_ok(cudaEventCreate(&sp.a), "cudaEventCreate");
+    cuda_ok(cudaEventCreate(&sp.b), "cudaEventCreate");
+    cuda_ok(cudaEventRecord(sp.a, c->stream), "cudaEventRecord");
+    fn();
+    cuda_ok(cudaEventRecord(sp.b, c->stream), "cudaEventRecord");
+    c->prof->spans.push_back(sp);
+}
+
+double gemm_bytes(double M, double N, double K) { return 4.0 * (M * K + K * N + M * N); }
+double gemm_flops(double M, double N, double K) { return 2.0 * M * N * K; }
+
+// ---------------------------------------------------------------------------------------------
+// Model upload
+TcWeight make_tc_weight(adai_b200_ctx* c, std::vector<void*>& owned, int K, int N) {
+    TcWeight w;
+    w.K = K;
+    w.N = N;
+    const size_t rows = static_cast<size_t>(round_up(N, 256));
+    w.hi = c->dzalloc_t<float>(rows * K);
+    w.lo = c->dzalloc_t<float>(rows * K);
+    owned.push_back(w.hi);
+    owned.push_back(w.lo);
+    return w;
+}
+
+// Transposes + splits host W [K, Nsub] into rows [row0, row0+Nsub) of w (W^T layout).
+void fill_tc_weight(adai_b200_ctx* c, float* staging, const TcWeight& w, int row0, const float* host,
+                    int K, int Nsub) {
+    const size_t bytes = static_cast<size_t>(K) * Nsub * sizeof(float);
+    cuda_ok(cudaMemcpyAsync(staging, host, bytes, cudaMemcpyHostToDevice, c->stream), "upload");
+    launch_transpose_split(staging, K, Nsub, w.hi + static_cast<size_t>(row0) * K,
+                           w.lo + static_cast<size_t>(row0) * K, c->stream);
+    cuda_ok(cudaGetLastError(), "transpose-split");
+    cuda_ok(cudaStreamSynchronize(c->stream), "upload sync");  // staging is reused
+}
+
+float* upload_vec(adai_b200_ctx* c, std::vector<void*>& owned, const float* host, size_t n) {
+    float* d = c->dalloc_t<float>(n);
+    owned.push_back(d);
+    cuda_ok(cudaMemcpyAsync(d, host, n * sizeof(float), cudaMemcpyHostToDevice, c->stream),
+            "upload");
+    return d;
+}
+
+void free_model(adai_b200_ctx* c) {
+    if (!c->model) return;
+    cudaStreamSynchronize(c->stream);
+    for (void* p : c->model->owned) c->dfree(p);
+    c->model.reset();
+    c->clear_graphs();
+}
+
+void validate_desc(const adai_b200_model_desc* d) {
+    if (!d) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null model description");
+    if (d->vocab <= 0 || d->d_model <= 0 || d->n_heads <= 0 || d->d_ff <= 0 ||
+        d->enc_layers < 0 || d->dec_layers <= 0 || d->max_seq <= 0)
+        fail(ADAI_B200_ERR_INVALID_ARGUMENT, "model dimensions must be positive");
+    if (d->d_model % d->n_heads || d->d_model / d->n_heads != 64)
+        fail(ADAI_B200_ERR_INVALID_ARGUMENT, "d_model / n_heads must be 64 (head width of the kernels)");
+    if (!layernorm_width_supported(d->d_model))
+        fail(ADAI_B200_ERR_INVALID_ARGUMENT, "d_model must be 128 * {1,2,3,4,6,8,12,16}");
+    if (d->d_ff % 16 || d->vocab % 4)
+        fail(ADAI_B200_ERR_INVALID_ARGUMENT, "d_ff must be a multiple of 16 and vocab of 4");
+}
+
+int tensor_count(const adai_b200_model_desc* d) {
+    return 1 + 12 * d->enc_layers + 2 + 1 + 18 * d->dec_layers + 2 + 2;
+}
+
+// PositionalEncoding table, src/PositionalEncoding.cpp:13-32.
+std::vector<float> pe_table_host(int max_len, int D) {
+    std::vector<float> t(static_cast<size_t>(max_len) * D);
+    for (int pos = 0; pos < max_len; ++pos)
+        for (int i = 0; i < D; ++i) {
+            const float angle = static_cast<float>(pos) /
+                                std::pow(10000.0f, (2.0f * static_cast<float>(i / 2)) / static_cast<float>(D));
+            t[static_cast<size_t>(pos) * D + i] = (i % 2 == 0) ? std::sin(angle) : std::cos(angle);
+        }
+    return t;
+}
+
+// ---------------------------------------------------------------------------------------------
+void ensure_step_bufs(adai_b200_ctx* c, int rows_needed) {
+    const Model& m = *c->model;
+    const int R = round_up(std::max(rows_needed, 1), 128);
+    if (c->sb.rows >= R) return;
+    cuda_ok(cudaStreamSynchronize(c->stream), "sync");
+    c->clear_graphs();
+    StepBufs& s = c->sb;
+    for (void* p : {(void*)s.x, (void*)s.nrm_hi, (void*)s.nrm_lo, (void*)s.qkv, (void*)s.attn_hi,
+                    (void*)s.attn_lo, (void*)s.qc, (void*)s.h_hi, (void*)s.h_lo, (void*)s.logits,
+                    (void*)s.ids, (void*)s.next, (void*)s.slots, (void*)s.nonfinite,
+                    (void*)s.nonfinite_any})
+        c->dfree(p);
+    const size_t D = m.d.d_model, F = m.d.d_ff, V = m.d.vocab;
+    s.rows = R;
+    s.x = c->dzalloc_t<float>(R * D);
+    s.nrm_hi = c->dzalloc_t<float>(R * D);
+    s.nrm_lo = c->dzalloc_t<float>(R * D);
+    s.qkv = c->dzalloc_t<float>(R * 3 * D);
+    s.attn_hi = c->dzalloc_t<float>(R * D);
+    s.attn_lo = c->dzalloc_t<float>(R * D);
+    s.qc = c->dzalloc_t<float>(R * D);
+    s.h_hi = c->dzalloc_t<float>(R * F);
+    s.h_lo = c->dzalloc_t<float>(R * F);
+    s.logits = c->dzalloc_t<float>(R * V);
+    s.ids = c->dzalloc_t<int>(R);
+    s.next = c->dzalloc_t<int>(R);
+    s.slots = c->dzalloc_t<int>(R);
+    s.nonfinite = c->dzalloc_t<int>(R);
+    s.nonfinite_any = c->dzalloc_t<int>(1);
+}
+
+void ensure_enc_bufs(adai_b200_ctx* c) {
+    if (c->eb.rows) return;
+    const Model& m = *c->model;
+    const int R = kEncRows;
+    EncBufs& e = c->eb;
+    const size_t D = m.d.d_model, F = m.d.d_ff;
+    e.rows = R;
+    e.x = c->dzalloc_t<float>(R * D);
+    e.nrm_hi = c->dzalloc_t<float>(R * D);
+    e.nrm_lo = c->dzalloc_t<float>(R * D);
+    e.qkv = c->dzalloc_t<float>(R * 3 * D);
+    e.attn_hi = c->dzalloc_t<float>(R * D);
+    e.attn_lo = c->dzalloc_t<float>(R * D);
+    e.h_hi = c->dzalloc_t<float>(R * F);
+    e.h_lo = c->dzalloc_t<float>(R * F);
+    e.out = c->dzalloc_t<float>(R * D);
+    e.ids = c->dzalloc_t<int>(R);
+    e.row_slot = c->dzalloc_t<int>(R);
+    e.row_pos = c->dzalloc_t<int>(R);
+    e.offsets = c->dzalloc_t<int>(R);
+    e.lens = c->dzalloc_t<int>(R);
+}
+
+void free_enc_bufs(adai_b200_ctx* c) {
+    EncBufs& e = c->eb;
+    for (void* p : {(void*)e.x, (void*)e.nrm_hi, (void*)e.nrm_lo, (void*)e.qkv, (void*)e.attn_hi,
+                    (void*)e.attn_lo, (void*)e.h_hi, (void*)e.h_lo, (void*)e.out, (void*)e.ids,
+                    (void*)e.row_slot, (void*)e.row_pos, (void*)e.offsets, (void*)e.lens})
+        c->dfree(p);
+    e = EncBufs{};
+}
+
+void free_step_bufs(adai_b200_ctx* c) {
+    StepBufs& s = c->sb;
+    for (void* p : {(void*)s.x, (void*)s.nrm_hi, (void*)s.nrm_lo, (void*)s.qkv, (void*)s.attn_hi,
+                    (void*)s.attn_lo, (void*)s.qc, (void*)s.h_hi, (void*)s.h_lo, (void*)s.logits,
+                    (void*)s.ids, (void*)s.next, (void*)s.slots, (void*)s.nonfinite,
+                    (void*)s.nonfinite_any})
+        c->dfree(p);
+    s = StepBufs{};
+}
+
+TcActs acts(const float* hi, const float* lo, int K, int rows_alloc) {
+    TcActs a;
+    a.hi = hi;
+    a.lo = lo;
+    a.K = K;
+    a.rows_alloc = rows_alloc;
+    return a;
+}
+
+// Enqueues one stacked decode step for rows 0..B-1 of the step buffers (ids in sb.ids, slots in
+// sb.slots). The graph captured from this is replayed by decode_step / generate.
+void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
+    const Model& m = *c->model;
+    StepBufs& s = c->sb;
+    const int D = m.d.d_model, F = m.d.d_ff, H = m.d.n_heads, L = m.d.dec_layers;
+    const int R = s.rows;
+    const float scale = 1.0f / std::sqrt(64.0f);
+    cudaStream_t st = c->stream;
+    const double Bd = B, Dd = D, Fd = F;
+    const double ln_bytes = 2.0 * Bd * Dd * 4.0;
+    timed(c, ADAI_B200_KC_NORM, ln_bytes, 0, [&] {
+        launch_embed_ln(m.dec_embed, s.ids, m.pe, m.d.max_seq, s.slots, kv->d_self_len, nullptr,
+                        s.x, m.dec[0].ln1g, m.dec[0].ln1b, s.nrm_hi, s.nrm_lo, B, D, m.d.vocab,
+                        c->d_err, st);
+    });
+    const double self_bytes = c->prof ? (2.0 * c->prof->sum_self_rows * Dd * 4.0 + 4.0 * Bd * Dd * 4.0) : 0;
+    const double cross_bytes = c->prof ? (2.0 * c->prof->sum_cross_rows * Dd * 4.0 + 2.0 * Bd * Dd * 4.0) : 0;
+    const TcActs a_nrm = acts(s.nrm_hi, s.nrm_lo, D, R);
+    const TcActs a_attn = acts(s.attn_hi, s.attn_lo, D, R);
+    const TcActs a_h = acts(s.h_hi, s.h_lo, F, R);
+    for (int l = 0; l < L; ++l) {
+        const DecLayerW& w = m.dec[l];
+        {  // Q|K|V of the new token
+            GemmEpilogue e;
+            e.flags = kEpiStore;
+            e.out = s.qkv;
+            e.ldo = 3 * D;
+            timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, 3 * Dd, Dd), gemm_flops(Bd, 3 * Dd, Dd),
+                  [&] { c->gemm(a_nrm, B, w.qkv, e); });
+        }
+        {  // masked self-attention over the cache, the new K/V appended first
+            DecodeAttnArgs a;
+            a.q = s.qkv;
+            a.ldq = 3 * D;
+            a.k_new = s.qkv + D;
+            a.v_new = s.qkv + 2 * D;
+            a.ldkv = 3 * D;
+            a.kc = kv->self_k_layer(l);
+            a.vc = kv->self_v_layer(l);
+            a.slot_stride = kv->self_slot_stride();
+            a.cap = kv->self_cap;
+            a.slots = s.slots;
+            a.len_by_slot = kv->d_self_len;
+            a.len_add = 1;
+            a.out_hi = s.attn_hi;
+            a.out_lo = s.attn_lo;
+            a.ldo = D;
+            a.B = B;
+            a.H = H;
+            a.max_len = kv->self_cap;
+            a.scale = scale;
+            a.ws = c->attn_ws;
+            a.tickets = c->attn_tickets;
+            timed(c, ADAI_B200_KC_SELF_ATTN, self_bytes, 0,
+                  [&] { launch_decode_attention(a, c->d_err, st); });
+        }
+        {  // x = x + attn W_o
+            GemmEpilogue e;
+            e.flags = kEpiStore | kEpiResid;
+            e.resid = s.x;
+            e.ldr = D;
+            e.out = s.x;
+            e.ldo = D;
+            timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Dd, Dd), gemm_flops(Bd, Dd, Dd),
+                  [&] { c->gemm(a_attn, B, w.o, e); });
+        }
+        timed(c, ADAI_B200_KC_NORM, ln_bytes, 0, [&] {
+            launch_layernorm(s.x, D, w.ln2g, w.ln2b, nullptr, s.nrm_hi, s.nrm_lo, B, D, st);
+        });
+        {  // cross-attention query
+            GemmEpilogue e;
+            e.flags = kEpiStore;
+            e.out = s.qc;
+            e.ldo = D;
+            timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Dd, Dd), gemm_flops(Bd, Dd, Dd),
+                  [&] { c->gemm(a_nrm, B, w.cq, e); });
+        }
+        {
+            DecodeAttnArgs a;
+            a.q = s.qc;
+            a.ldq = D;
+            a.kc = kv->cross_k_layer(l);
+            a.vc = kv->cross_v_layer(l);
+            a.slot_stride = kv->cross_slot_stride();
+            a.cap = kv->cross_cap;
+            a.slots = s.slots;
+            a.len_by_slot = kv->d_cross_len;
+            a.len_add = 0;
+            a.out_hi = s.attn_hi;
+            a.out_lo = s.attn_lo;
+            a.ldo = D;
+            a.B = B;
+            a.H = H;
+            a.max_len = kv->cross_cap;
+            a.scale = scale;
+            a.ws = c->attn_ws;
+            a.tickets = c->attn_tickets;
+            timed(c, ADAI_B200_KC_CROSS_ATTN, cross_bytes, 0,
+                  [&] { launch_decode_attention(a, c->d_err, st); });
+        }
+        {
+            GemmEpilogue e;
+            e.flags = kEpiStore | kEpiResid;
+            e.resid = s.x;
+            e.ldr = D;
+            e.out = s.x;
+            e.ldo = D;
+            timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Dd, Dd), gemm_flops(Bd, Dd, Dd),
+                  [&] { c->gemm(a_attn, B, w.co, e); });
+        }
+        timed(c, ADAI_B200_KC_NORM, ln_bytes, 0, [&] {
+            launch_layernorm(s.x, D, w.ln3g, w.ln3b, nullptr, s.nrm_hi, s.nrm_lo, B, D, st);
+        });
+        {  // h = GELU(x W1 + b1), written as its tf32 split for the next GEMM
+            GemmEpilogue e;
+            e.flags = kEpiBias | kEpiGelu | kEpiSplit;
+            e.bias = w.b1;
+            e.out_hi = s.h_hi;
+            e.out_lo = s.h_lo;
+            e.lds = F;
+            timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Fd, Dd), gemm_flops(Bd, Fd, Dd),
+                  [&] { c->gemm(a_nrm, B, w.w1, e); });
+        }
+        {  // x = x + (h W2 + b2)
+            GemmEpilogue e;
+            e.flags = kEpiBias | kEpiResid | kEpiStore;
+            e.bias = w.b2;
+            e.resid = s.x;
+            e.ldr = D;
+            e.out = s.x;
+            e.ldo = D;
+            timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Dd, Fd), gemm_flops(Bd, Dd, Fd),
+                  [&] { c->gemm(a_h, B, w.w2, e); });
+        }
+        const bool last = (l + 1 == L);
+        timed(c, ADAI_B200_KC_NORM, ln_bytes, 0, [&] {
+            launch_layernorm(s.x, D, last ? m.dec_lnf_g : m.dec[l + 1].ln1g,
+                             last ? m.dec_lnf_b : m.dec[l + 1].ln1b, nullptr, s.nrm_hi, s.nrm_lo,
+                             B, D, st);
+        });
+    }
+    {  // logits = x W_out + b, first maximum per row
+        GemmEpilogue e;
+        e.flags = kEpiBias | kEpiArgmax | ((flags & kStepLogits) ? kEpiStore : 0);
+        e.bias = m.head_b;
+        e.out = s.logits;
+        e.ldo = m.d.vocab;
+        e.next_ids = s.next;
+        e.nonfinite = s.nonfinite;
+        const double Vd = m.d.vocab;
+        timed(c, ADAI_B200_KC_HEAD, 4.0 * (Bd * Dd + Dd * Vd), gemm_flops(Bd, Vd, Dd),
+              [&] { c->gemm(a_nrm, B, m.head, e); });
+    }
+}
+
+__global__ void record_and_advance_kernel(const int* __restrict__ next, int* __restrict__ ids,
+                                          const int* __restrict__ slots, int* __restrict__ self_len,
+                                          int* __restrict__ hist, int hist_ld,
+                                          const int* __restrict__ nonfinite, int* __restrict__ nf_any,
+                                          int B, int feed_back) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    const int slot = slots[b];
+    const int pos = self_len[slot];
+    if (hist) hist[static_cast<size_t>(slot) * hist_ld + pos] = next[b];
+    if (nonfinite[b]) atomicOr(nf_any, 1);
+    if (feed_back) ids[b] = next[b];
+    self_len[slot] = pos + 1;
+}
+
+// Sizes the scratch a decode step of B rows needs (allocation cannot happen inside a capture).
+void presize_step_scratch(adai_b200_ctx* c, adai_b200_kv* kv, int B) {
+    const Model& m = *c->model;
+    const int D = m.d.d_model, F = m.d.d_ff;
+    for (const auto& sh : {std::make_tuple(3 * D, D, 0), std::make_tuple(D, D, 0),
+                           std::make_tuple(F, D, 0), std::make_tuple(D, F, 0),
+                           std::make_tuple(m.d.vocab, D, (int)kEpiArgmax)})
+        c->ensure_gemm_scratch(gemm_plan(B, std::get<0>(sh), std::get<1>(sh), std::get<2>(sh), c->num_sms));
+    c->ensure_attn_scratch(B, m.d.n_heads, std::max(kv->self_cap, kv->cross_cap));
+}
+
+cudaGraphExec_t get_graph(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
+    const GraphKey key{kv, B, flags};
+    auto it = c->graphs.find(key);
+    if (it != c->graphs.end()) return it->second;
+    presize_step_scratch(c, kv, B);
+    cuda_ok(cudaStreamSynchronize(c->stream), "sync before capture");
+    cudaGraph_t g;
+    cuda_ok(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+        record_step(c, kv, B, flags);
+        record_and_advance_kernel<<<(B + 127) / 128, 128, 0, c->stream>>>(
+            c->sb.next, c->sb.ids, c->sb.slots, kv->d_self_len, kv->d_hist, kv->self_cap,
+            c->sb.nonfinite, c->sb.nonfinite_any, B, (flags & kStepAdvanceIds) ? 1 : 0);
+    } catch (...) {
+        cudaGraph_t dummy;
+        cudaStreamEndCapture(c->stream, &dummy);
+        if (dummy) cudaGraphDestroy(dummy);
+        throw;
+    }
+    cuda_ok(cudaStreamEndCapture(c->stream, &g), "end capture");
+    size_t n_nodes = 0;
+    cuda_ok(cudaGraphGetNodes(g, nullptr, &n_nodes), "graph nodes");
+    c->graph_kernels[key] = static_cast<int>(n_nodes);
+    cudaGraphExec_t ge;
+    cuda_ok(cudaGraphInstantiate(&ge, g, 0), "graph instantiate");
+    cudaGraphDestroy(g);
+    c->graphs[key] = ge;
+    return ge;
+}
+
+void check_ctx(adai_b200_ctx* c) {
+    if (!c) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null context");
+    c->check_usable();
+    cuda_ok(cudaSetDevice(c->device), "cudaSetDevice");
+}
+
+void check_kv(adai_b200_ctx* c, adai_b200_kv* kv) {
+    if (!kv || !c->kvs.count(kv)) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "unknown KV arena");
+}
+
+void check_model(adai_b200_ctx* c) {
+    if (!c->model) fail(ADAI_B200_ERR_STATE, "no model uploaded");
+}
+
+// Validates the batch of a decode step and stages slots/ids into the step buffers.
+void stage_batch(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slots, const int* ids,
+                 int steps) {
+    if (B <= 0 || B > kv->max_slots)
+        fail(ADAI_B200_ERR_INVALID_ARGUMENT, "batch must be in [1, max_slots]");
+    if (!slots || !ids) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null slots or ids");
+    std::vector<char> seen(kv->max_slots, 0);
+    for (int b = 0; b < B; ++b) {
+        const int s = slots[b];
+        if (s < 0 || s >= kv->max_slots)
+            fail(ADAI_B200_ERR_OUT_OF_RANGE, "slot " + std::to_string(s) + " out of range");
+        if (seen[s]) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "slot " + std::to_string(s) + " repeated in one batch");
+        seen[s] = 1;
+        if (kv->cross_len[s] <= 0)
+            fail(ADAI_B200_ERR_STATE, "slot " + std::to_string(s) + " has no encoder output (call adai_b200_encode first)");
+        if (kv->self_len[s] + steps > kv->self_cap)
+            fail(ADAI_B200_ERR_OUT_OF_RANGE, "self-attention cache of slot " + std::to_string(s) +
+                                                 " full (capacity " + std::to_string(kv->self_cap) + ")");
+        if (ids[b] < 0 || ids[b] >= c->model->d.vocab)
+            fail(ADAI_B200_ERR_OUT_OF_RANGE, "Token ID " + std::to_string(ids[b]) + " out of range [0, " +
+                                                 std::to_string(c->model->d.vocab) + ")");
+    }
+    ensure_step_bufs(c, B);
+    int* pin = c->pinned(2 * static_cast<size_t>(B));
+    std::memcpy(pin, slots, B * sizeof(int));
+    std::memcpy(pin + B, ids, B * sizeof(int));
+    cuda_ok(cudaMemcpyAsync(c->sb.slots, pin, B * sizeof(int), cudaMemcpyHostToDevice, c->stream), "H2D slots");
+    cuda_ok(cudaMemcpyAsync(c->sb.ids, pin + B, B * sizeof(int), cudaMemcpyHostToDevice, c->stream), "H2D ids");
+}
+
+}  // namespace
+
+// =============================================================================================
+// C ABI
+extern "C" {
+
+const char* adai_b200_last_error(void) { return g_last_error.c_str(); }
+
+int adai_b200_ctx_create(int device, float mem_fraction, adai_b200_ctx** out) {
+    return guarded([&] {
+        if (!out) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null output handle");
+        *out = nullptr;
+        int n = 0;
+        if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0)
+            fail(ADAI_B200_ERR_NO_DEVICE, "no CUDA device");
+        if (device < 0 || device >= n) fail(ADAI_B200_ERR_OUT_OF_RANGE, "device index out of range");
+        if (mem_fraction < 0.f || mem_fraction > 1.f)
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "mem_fraction must be in [0, 1]");
+        cudaDeviceProp prop;
+        cuda_ok(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+        if (prop.major != 10)
+            fail(ADAI_B200_ERR_NO_DEVICE, std::string("device ") + prop.name +
+                                              " is not sm_100 (this library is built for sm_100a only)");
+        if (!tensor_map_api_available())
+            fail(ADAI_B200_ERR_NO_DEVICE, "cuTensorMapEncodeTiled unavailable in the driver");
+        cuda_ok(cudaSetDevice(device), "cudaSetDevice");
+        auto c = std::make_unique<adai_b200_ctx>();
+        c->device = device;
+        c->num_sms = prop.multiProcessorCount;
+        if (mem_fraction > 0.f) c->mem_cap = static_cast<size_t>(static_cast<double>(prop.totalGlobalMem) * mem_fraction);
+        cuda_ok(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+        c->d_err = c->dzalloc_t<int>(1);
+        cuda_ok(cudaStreamSynchronize(c->stream), "sync");
+        *out = c.release();
+    });
+}
+
+int adai_b200_ctx_destroy(adai_b200_ctx* c) {
+    return guarded([&] {
+        if (!c) return;
+        cudaSetDevice(c->device);
+        cudaStreamSynchronize(c->stream);
+        c->clear_graphs();
+        for (auto& kvp : c->allocs) cudaFree(kvp.first);
+        c->allocs.clear();
+        for (adai_b200_kv* kv : c->kvs) delete kv;
+        c->kvs.clear();
+        if (c->h_pin) cudaFreeHost(c->h_pin);
+        cudaStreamDestroy(c->stream);
+        delete c;
+    });
+}
+
+int adai_b200_ctx_synchronize(adai_b200_ctx* c, double timeout_seconds) {
+    return guarded([&] {
+        check_ctx(c);
+        c->sync(timeout_seconds > 0 ? timeout_seconds : wait_timeout_seconds());
+    });
+}
+
+int adai_b200_ctx_memory(adai_b200_ctx* c, unsigned long long* bytes) {
+    return guarded([&] {
+        if (!c || !bytes) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null argument");
+        *bytes = c->mem_used;
+    });
+}
+
+void* adai_b200_ctx_stream(adai_b200_ctx* c) { return c ? static_cast<void*>(c->stream) : nullptr; }
+
+int adai_b200_model_tensor_count(const adai_b200_model_desc* d) { return d ? tensor_count(d) : -1; }
+
+int adai_b200_model_upload(adai_b200_ctx* c, const adai_b200_model_desc* d,
+                           const float* const* t, const float* pe_table) {
+    return guarded([&] {
+        check_ctx(c);
+        validate_desc(d);
+        if (!t) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null tensor list");
+        for (int i = 0; i < tensor_count(d); ++i)
+            if (!t[i]) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "tensor " + std::to_string(i) + " is null");
+        for (adai_b200_kv* kv : c->kvs)
+            if (kv->L != d->dec_layers || kv->H != d->n_heads)
+                fail(ADAI_B200_ERR_STATE, "an existing KV arena does not match this model");
+        free_model(c);
+        free_enc_bufs(c);
+        free_step_bufs(c);
+        auto m = std::make_unique<Model>();
+        m->d = *d;
+        const int V = d->vocab, D = d->d_model, F = d->d_ff;
+        auto& own = m->owned;
+        const size_t max_mat = std::max<size_t>({static_cast<size_t>(V) * D, static_cast<size_t>(D) * F});
+        float* staging = c->dalloc_t<float>(max_mat);
+        try {
+            int k = 0;
+            m->enc_embed = upload_vec(c, own, t[k++], static_cast<size_t>(V) * D);
+            m->enc.resize(d->enc_layers);
+            for (int i = 0; i < d->enc_layers; ++i) {
+                EncLayerW& e = m->enc[i];
+                e.ln1g = upload_vec(c, own, t[k++], D);
+                e.ln1b = upload_vec(c, own, t[k++], D);
+                e.qkv = make_tc_weight(c, own, D, 3 * D);
+                fill_tc_weight(c, staging, e.qkv, 0, t[k++], D, D);
+                fill_tc_weight(c, staging, e.qkv, D, t[k++], D, D);
+                fill_tc_weight(c, staging, e.qkv, 2 * D, t[k++], D, D);
+                e.o = make_tc_weight(c, own, D, D);
+                fill_tc_weight(c, staging, e.o, 0, t[k++], D, D);
+                e.ln2g = upload_vec(c, own, t[k++], D);
+                e.ln2b = upload_vec(c, own, t[k++], D);
+                e.w1 = make_tc_weight(c, own, D, F);
+                fill_tc_weight(c, staging, e.w1, 0, t[k++], D, F);
+                e.b1 = upload_vec(c, own, t[k++], F);
+                e.w2 = make_tc_weight(c, own, F, D);
+                fill_tc_weight(c, staging, e.w2, 0, t[k++], F, D);
+                e.b2 = upload_vec(c, own, t[k++], D);
+            }
+            m->enc_lnf_g = upload_vec(c, own, t[k++], D);
+            m->enc_lnf_b = upload_vec(c, own, t[k++], D);
+            m->dec_embed = upload_vec(c, own, t[k++], static_cast<size_t>(V) * D);
+            m->dec.resize(d->dec_layers);
+            for (int i = 0; i < d->dec_layers; ++i) {
+                DecLayerW& w = m->dec[i];
+                w.ln1g = upload_vec(c, own, t[k++], D);
+                w.ln1b = upload_vec(c, own, t[k++], D);
+                w.qkv = make_tc_weight(c, own, D, 3 * D);
+                fill_tc_weight(c, staging, w.qkv, 0, t[k++], D, D);
+                fill_tc_weight(c, staging, w.qkv, D, t[k++], D, D);
+                fill_tc_weight(c, staging, w.qkv, 2 * D, t[k++], D, D);
+                w.o = make_tc_weight(c, own, D, D);
+                fill_tc_weight(c, staging, w.o, 0, t[k++], D, D);
+                w.ln2g = upload_vec(c, own, t[k++], D);
+                w.ln2b = upload_vec(c, own, t[k++], D);
+                w.cq = make_tc_weight(c, own, D, D);
+                fill_tc_weight(c, staging, w.cq, 0, t[k++], D, D);
+                w.ckv = make_tc_weight(c, own, D, 2 * D);
+                fill_tc_weight(c, staging, w.ckv, 0, t[k++], D, D);
+                fill_tc_weight(c, staging, w.ckv, D, t[k++], D, D);
+                w.co = make_tc_weight(c, own, D, D);
+                fill_tc_weight(c, staging, w.co, 0, t[k++], D, D);
+                w.ln3g = upload_vec(c, own, t[k++], D);
+                w.ln3b = upload_vec(c, own, t[k++], D);
+                w.w1 = make_tc_weight(c, own, D, F);
+                fill_tc_weight(c, staging, w.w1, 0, t[k++], D, F);
+                w.b1 = upload_vec(c, own, t[k++], F);
+                w.w2 = make_tc_weight(c, own, F, D);
+                fill_tc_weight(c, staging, w.w2, 0, t[k++], F, D);
+                w.b2 = upload_vec(c, own, t[k++], D);
+            }
+            m->dec_lnf_g = upload_vec(c, own, t[k++], D);
+            m->dec_lnf_b = upload_vec(c, own, t[k++], D);
+            m->head = make_tc_weight(c, own, D, V);
+            fill_tc_weight(c, staging, m->head, 0, t[k++], D, V);
+            m->head_b = upload_vec(c, own, t[k++], V);
+            std::vector<float> pe;
+            if (!pe_table) {
+                pe = pe_table_host(d->max_seq, D);
+                pe_table = pe.data();
+            }
+            m->pe = upload_vec(c, own, pe_table, static_cast<size_t>(d->max_seq) * D);
+            cuda_ok(cudaStreamSynchronize(c->stream), "upload sync");
+        } catch (...) {
+            c->dfree(staging);
+            for (void* p : own) c->dfree(p);
+            throw;
+        }
+        c->dfree(staging);
+        c->model = std::move(m);
+    });
+}
+
+int adai_b200_kv_create(adai_b200_ctx* c, int max_slots, int self_cap, int cross_cap,
+                        adai_b200_kv** out) {
+    return guarded([&] {
+        check_ctx(c);
+        check_model(c);
+        if (!out) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null output handle");
+        if (max_slots <= 0 || self_cap <= 0 || cross_cap <= 0)
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "KV arena sizes must be positive");
+        const Model& m = *c->model;
+        auto kv = std::make_unique<adai_b200_kv>();
+        kv->max_slots = max_slots;
+        kv->self_cap = self_cap;
+        kv->cross_cap = cross_cap;
+        kv->L = m.d.dec_layers;
+        kv->H = m.d.n_heads;
+        const size_t self_n = static_cast<size_t>(kv->L) * max_slots * kv->self_slot_stride();
+        const size_t cross_n = static_cast<size_t>(kv->L) * max_slots * kv->cross_slot_stride();
+        std::vector<void*> got;
+        try {
+            kv->self_k = c->dalloc_t<float>(self_n);
+            got.push_back(kv->self_k);
+            kv->self_v = c->dalloc_t<float>(self_n);
+            got.push_back(kv->self_v);
+            kv->cross_k = c->dalloc_t<float>(cross_n);
+            got.push_back(kv->cross_k);
+            kv->cross_v = c->dalloc_t<float>(cross_n);
+            got.push_back(kv->cross_v);
+            kv->d_self_len = c->dzalloc_t<int>(max_slots);
+            got.push_back(kv->d_self_len);
+            kv->d_cross_len = c->dzalloc_t<int>(max_slots);
+            got.push_back(kv->d_cross_len);
+            kv->d_hist = c->dzalloc_t<int>(static_cast<size_t>(max_slots) * self_cap);
+            got.push_back(kv->d_hist);
+        } catch (...) {
+            for (void* p : got) c->dfree(p);
+            throw;
+        }
+        kv->self_len.assign(max_slots, 0);
+        kv->cross_len.assign(max_slots, 0);
+        cuda_ok(cudaStreamSynchronize(c->stream), "sync");
+        c->kvs.insert(kv.get());
+        *out = kv.release();
+    });
+}
+
+int adai_b200_kv_destroy(adai_b200_ctx* c, adai_b200_kv* kv) {
+    return guarded([&] {
+        if (!c) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null context");
+        check_kv(c, kv);
+        cudaSetDevice(c->device);
+        cudaStreamSynchronize(c->stream);
+        c->clear_graphs();
+        for (void* p : {(void*)kv->self_k, (void*)kv->self_v, (void*)kv->cross_k,
+                        (void*)kv->cross_v, (void*)kv->d_self_len, (void*)kv->d_cross_len,
+                        (void*)kv->d_hist})
+            c->dfree(p);
+        c->kvs.erase(kv);
+        delete kv;
+    });
+}
+
+int adai_b200_kv_reset(adai_b200_ctx* c, adai_b200_kv* kv, int slot) {
+    return guarded([&] {
+        check_ctx(c);
+        check_kv(c, kv);
+        if (slot < 0 || slot >= kv->max_slots) fail(ADAI_B200_ERR_OUT_OF_RANGE, "slot out of range");
+        kv->self_len[slot] = 0;
+        kv->cross_len[slot] = 0;
+        cuda_ok(cudaMemsetAsync(kv->d_self_len + slot, 0, sizeof(int), c->stream), "memset");
+        cuda_ok(cudaMemsetAsync(kv->d_cross_len + slot, 0, sizeof(int), c->stream), "memset");
+        c->sync(wait_timeout_seconds());
+    });
+}
+
+int adai_b200_kv_clear_self(adai_b200_ctx* c, adai_b200_kv* kv, int slot) {
+    return guarded([&] {
+        check_ctx(c);
+        check_kv(c, kv);
+        if (slot < 0 || slot >= kv->max_slots) fail(ADAI_B200_ERR_OUT_OF_RANGE, "slot out of range");
+        kv->self_len[slot] = 0;
+        cuda_ok(cudaMemsetAsync(kv->d_self_len + slot, 0, sizeof(int), c->stream), "memset");
+        c->sync(wait_timeout_seconds());
+    });
+}
+
+int adai_b200_kv_length(adai_b200_ctx* c, adai_b200_kv* kv, int slot, int* self_len,
+                        int* cross_len) {
+    return guarded([&] {
+        if (!c) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null context");
+        check_kv(c, kv);
+        if (slot < 0 || slot >= kv->max_slots) fail(ADAI_B200_ERR_OUT_OF_RANGE, "slot out of range");
+        if (self_len) *self_len = kv->self_len[slot];
+        if (cross_len) *cross_len = kv->cross_len[slot];
+    });
+}
+
+int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots, const int* ids,
+                     const int* src_lens, float* enc_out) {
+    return guarded([&] {
+        check_ctx(c);
+        check_model(c);
+        check_kv(c, kv);
+        const Model& m = *c->model;
+        if (n <= 0 || !slots || !ids || !src_lens) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "empty or null request list");
+        std::vector<char> seen(kv->max_slots, 0);
+        long long total = 0;
+        for (int i = 0; i < n; ++i) {
+            if (slots[i] < 0 || slots[i] >= kv->max_slots) fail(ADAI_B200_ERR_OUT_OF_RANGE, "slot out of range");
+            if (seen[slots[i]]) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "slot repeated in one encode call");
+            seen[slots[i]] = 1;
+            if (src_lens[i] <= 0) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "empty source sequence");
+            // LLMEncoder::encode_with_mask refuses more than max_seq_length ids (src/LLMEncoder.cpp:106-116)
+            if (src_lens[i] > m.d.max_seq)
+                fail(ADAI_B200_ERR_INVALID_ARGUMENT, std::to_string(src_lens[i]) + " tokens exceed max_seq_length " + std::to_string(m.d.max_seq));
+            if (src_lens[i] > kv->cross_cap) fail(ADAI_B200_ERR_OUT_OF_RANGE, "source longer than the cross-attention cache");
+            total += src_lens[i];
+        }
+        for (long long r = 0; r < total; ++r)
+            if (ids[r] < 0 || ids[r] >= m.d.vocab)
+                fail(ADAI_B200_ERR_OUT_OF_RANGE, "Token ID " + std::to_string(ids[r]) + " out of range [0, " + std::to_string(m.d.vocab) + ")");
+        ensure_enc_bufs(c);
+        EncBufs& e = c->eb;
+        const int D = m.d.d_model, F = m.d.d_ff, H = m.d.n_heads;
+        const float scale = 1.0f / std::sqrt(64.0f);
+        cudaStream_t st = c->stream;
+        long long row_base = 0;
+        int i0 = 0;
+        while (i0 < n) {
+            int i1 = i0, rows = 0;
+            while (i1 < n && rows + src_lens[i1] <= e.rows) rows += src_lens[i1++];
+            const int nseq = i1 - i0;
+            int max_len = 0;
+            int* pin = c->pinned(static_cast<size_t>(rows) * 3 + 2 * static_cast<size_t>(nseq));
+            int* p_ids = pin;
+            int* p_slot = pin + rows;
+            int* p_pos = pin + 2 * rows;
+            int* p_off = pin + 3 * rows;
+            int* p_len = p_off + nseq;
+            int r = 0;
+            for (int i = i0; i < i1; ++i) {
+                p_off[i - i0] = r;
+                p_len[i - i0] = src_lens[i];
+                max_len = std::max(max_len, src_lens[i]);
+                for (int t = 0; t < src_lens[i]; ++t, ++r) {
+                    p_ids[r] = ids[row_base + r];
+                    p_slot[r] = slots[i];
+                    p_pos[r] = t;
+                }
+            }
+            cuda_ok(cudaMemcpyAsync(e.ids, p_ids, rows * sizeof(int), cudaMemcpyHostToDevice, st), "H2D");
+            cuda_ok(cudaMemcpyAsync(e.row_slot, p_slot, rows * sizeof(int), cudaMemcpyHostToDevice, st), "H2D");
+            cuda_ok(cudaMemcpyAsync(e.row_pos, p_pos, rows * sizeof(int), cudaMemcpyHostToDevice, st), "H2D");
+            cuda_ok(cudaMemcpyAsync(e.offsets, p_off, nseq * sizeof(int), cudaMemcpyHostToDevice, st), "H2D");
+            cuda_ok(cudaMemcpyAsync(e.lens, p_len, nseq * sizeof(int), cudaMemcpyHostToDevice, st), "H2D");
+            const int Le = m.d.enc_layers;
+            launch_embed_ln(m.enc_embed, e.ids, m.pe, m.d.max_seq, nullptr, nullptr, e.row_pos, e.x,
+                            Le ? m.enc[0].ln1g : m.enc_lnf_g, Le ? m.enc[0].ln1b : m.enc_lnf_b,
+                            e.nrm_hi, e.nrm_lo, rows, D, m.d.vocab, c->d_err, st);
+            if (Le == 0)  // the embedding row LayerNorm'd by final_norm is the encoder output
+                launch_layernorm(e.x, D, m.enc_lnf_g, m.enc_lnf_b, e.out, e.nrm_hi, e.nrm_lo, rows, D, st);
+            const TcActs a_nrm = acts(e.nrm_hi, e.nrm_lo, D, e.rows);
+            const TcActs a_attn = acts(e.attn_hi, e.attn_lo, D, e.rows);
+            const TcActs a_h = acts(e.h_hi, e.h_lo, F, e.rows);
+            for (int l = 0; l < Le; ++l) {
+                const EncLayerW& w = m.enc[l];
+                GemmEpilogue q;
+                q.flags = kEpiStore;
+                q.out = e.qkv;
+                q.ldo = 3 * D;
+                c->gemm(a_nrm, rows, w.qkv, q);
+                launch_prefill_attention(e.qkv, D, H, e.offsets, e.lens, nseq, max_len, e.attn_hi,
+                                         e.attn_lo, scale, st);
+                GemmEpilogue o;
+                o.flags = kEpiStore | kEpiResid;
+                o.resid = e.x;
+                o.ldr = D;
+                o.out = e.x;
+                o.ldo = D;
+                c->gemm(a_attn, rows, w.o, o);
+                launch_layernorm(e.x, D, w.ln2g, w.ln2b, nullptr, e.nrm_hi, e.nrm_lo, rows, D, st);
+                GemmEpilogue f1;
+                f1.flags = kEpiBias | kEpiGelu | kEpiSplit;
+                f1.bias = w.b1;
+                f1.out_hi = e.h_hi;
+                f1.out_lo = e.h_lo;
+                f1.lds = F;
+                c->gemm(a_nrm, rows, w.w1, f1);
+                GemmEpilogue f2;
+                f2.flags = kEpiBias | kEpiResid | kEpiStore;
+                f2.bias = w.b2;
+                f2.resid = e.x;
+                f2.ldr = D;
+                f2.out = e.x;
+                f2.ldo = D;
+                c->gemm(a_h, rows, w.w2, f2);
+                const bool last = l + 1 == Le;
+                launch_layernorm(e.x, D, last ? m.enc_lnf_g : m.enc[l + 1].ln1g,
+                                 last ? m.enc_lnf_b : m.enc[l + 1].ln1b, last ? e.out : nullptr,
+                                 e.nrm_hi, e.nrm_lo, rows, D, st);
+            }
+            // Cross-attention K/V of every decoder layer, scattered into the slot's cache rows.
+            for (int l = 0; l < m.d.dec_layers; ++l) {
+                GemmEpilogue s;
+                s.flags = kEpiKvScatter;
+                s.kc = kv->cross_k_layer(l);
+                s.vc = kv->cross_v_layer(l);
+                s.slot_stride = kv->cross_slot_stride();
+                s.cap = kv->cross_cap;
+                s.heads = H;
+                s.d_model = D;
+                s.row_slot = e.row_slot;
+                s.row_pos = e.row_pos;
+                c->gemm(a_nrm, rows, m.dec[l].ckv, s);
+            }
+            if (enc_out)
+                cuda_ok(cudaMemcpyAsync(enc_out + row_base * D, e.out, static_cast<size_t>(rows) * D * sizeof(float),
+                                        cudaMemcpyDeviceToHost, st), "D2H encoder output");
+            for (int i = i0; i < i1; ++i) {
+                kv->cross_len[slots[i]] = src_lens[i];
+                kv->self_len[slots[i]] = 0;
+            }
+            c->sync(wait_timeout_seconds());
+            row_base += rows;
+            i0 = i1;
+        }
+        // Device copies of the per-slot lengths.
+        int* pin = c->pinned(2 * static_cast<size_t>(kv->max_slots));
+        std::memcpy(pin, kv->self_len.data(), kv->max_slots * sizeof(int));
+        std::memcpy(pin + kv->max_slots, kv->cross_len.data(), kv->max_slots * sizeof(int));
+        cuda_ok(cudaMemcpyAsync(kv->d_self_len, pin, kv->max_slots * sizeof(int), cudaMemcpyHostToDevice, st), "H2D");
+        cuda_ok(cudaMemcpyAsync(kv->d_cross_len, pin + kv->max_slots, kv->max_slots * sizeof(int), cudaMemcpyHostToDevice, st), "H2D");
+        c->sync(wait_timeout_seconds());
+    });
+}
+
+int adai_b200_decode_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slots,
+                          const int* ids, int* next_ids, float* logits) {
+    return guarded([&] {
+        check_ctx(c);
+        check_model(c);
+        check_kv(c, kv);
+        if (!next_ids) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null next_ids");
+        stage_batch(c, kv, B, slots, ids, 1);
+        const int flags = logits ? kStepLogits : 0;
+        cudaGraphExec_t g = get_graph(c, kv, B, flags);
+        cuda_ok(cudaMemsetAsync(c->sb.nonfinite_any, 0, sizeof(int), c->stream), "memset");
+        cuda_ok(cudaGraphLaunch(g, c->stream), "graph launch");
+        int* pin = c->pinned(static_cast<size_t>(B) + 1);
+        cuda_ok(cudaMemcpyAsync(pin, c->sb.next, B * sizeof(int), cudaMemcpyDeviceToHost, c->stream), "D2H ids");
+        cuda_ok(cudaMemcpyAsync(pin + B, c->sb.nonfinite_any, sizeof(int), cudaMemcpyDeviceToHost, c->stream), "D2H flag");
+        if (logits)
+            cuda_ok(cudaMemcpyAsync(logits, c->sb.logits, static_cast<size_t>(B) * c->model->d.vocab * sizeof(float),
+                                    cudaMemcpyDeviceToHost, c->stream), "D2H logits");
+        c->sync(wait_timeout_seconds());
+        for (int b = 0; b < B; ++b) kv->self_len[slots[b]] += 1;
+        std::memcpy(next_ids, pin, B * sizeof(int));
+        if (pin[B]) fail(ADAI_B200_ERR_NONFINITE, "the model returned non-finite logits");
+    });
+}
+
+int adai_b200_generate(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slots,
+                       const int* first_ids, int steps, int* out_ids) {
+    return guarded([&] {
+        check_ctx(c);
+        check_model(c);
+        check_kv(c, kv);
+        if (steps <= 0 || !out_ids) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "steps must be positive, out_ids non-null");
+        stage_batch(c, kv, B, slots, first_ids, steps);
+        std::vector<int> pos0(B);
+        for (int b = 0; b < B; ++b) pos0[b] = kv->self_len[slots[b]];
+        cudaGraphExec_t g = get_graph(c, kv, B, kStepAdvanceIds);
+        cuda_ok(cudaMemsetAsync(c->sb.nonfinite_any, 0, sizeof(int), c->stream), "memset");
+        cudaEvent_t e0, e1;
+        cuda_ok(cudaEventCreate(&e0), "cudaEventCreate");
+        cuda_ok(cudaEventCreate(&e1), "cudaEventCreate");
+        cuda_ok(cudaEventRecord(e0, c->stream), "cudaEventRecord");
+        for (int s = 0; s < steps; ++s) cuda_ok(cudaGraphLaunch(g, c->stream), "graph launch");
+        cuda_ok(cudaEventRecord(e1, c->stream), "cudaEventRecord");
+        c->sync(wait_timeout_seconds() + 1e-3 * steps);
+        float ms = 0.f;
+        cuda_ok(cudaEventElapsedTime(&ms, e0, e1), "cudaEventElapsedTime");
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        c->last_decode_ms = ms;
+        c->last_kernels_per_step = c->graph_kernels[GraphKey{kv, B, kStepAdvanceIds}];
+        for (int b = 0; b < B; ++b) kv->self_len[slots[b]] += steps;
+        int nf = 0;
+        cuda_ok(cudaMemcpy(&nf, c->sb.nonfinite_any, sizeof(int), cudaMemcpyDeviceToHost), "D2H flag");
+        for (int b = 0; b < B; ++b)
+            cuda_ok(cudaMemcpy(out_ids + static_cast<size_t>(b) * steps,
+                               kv->d_hist + static_cast<size_t>(slots[b]) * kv->self_cap + pos0[b],
+                               steps * sizeof(int), cudaMemcpyDeviceToHost), "D2H ids");
+        if (nf) fail(ADAI_B200_ERR_NONFINITE, "the model returned non-finite logits");
+    });
+}
+
+// ---- op level ----------------------------------------------------------------------------------
+namespace {
+__global__ void split_pad_kernel(const float* __restrict__ x, int rows, int k, float* __restrict__ hi,
+                                 float* __restrict__ lo, int kpad, int rows_alloc) {
+    const size_t n = static_cast<size_t>(rows_alloc) * kpad;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int r = static_cast<int>(i / kpad), cc = static_cast<int>(i % kpad);
+        const float v = (r < rows && cc < k) ? x[static_cast<size_t>(r) * k + cc] : 0.f;
+        float h, l;
+        split_tf32(v, h, l);
+        hi[i] = h;
+        lo[i] = l;
+    }
+}
+__global__ void transpose_split_pad_kernel(const float* __restrict__ w, int K, int N, int Kpad,
+                                           float* __restrict__ hi_t, float* __restrict__ lo_t) {
+    __shared__ float tile[32][33];
+    const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int k = k0 + i, nn = n0 + threadIdx.x;
+        tile[i][threadIdx.x] = (k < K && nn < N) ? w[static_cast<size_t>(k) * N + nn] : 0.f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int nn = n0 + i, k = k0 + threadIdx.x;
+        if (nn < N && k < Kpad) {
+            float h, l;
+            split_tf32(tile[threadIdx.x][i], h, l);
+            hi_t[static_cast<size_t>(nn) * Kpad + k] = h;
+            lo_t[static_cast<size_t>(nn) * Kpad + k] = l;
+        }
+    }
+}
+
+adai_b200_weight* prepare_weight(adai_b200_ctx* c, const float* B, int k, int n) {
+    if (!B || k <= 0 || n <= 0) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad weight shape");
+    auto w = std::make_unique<adai_b200_weight>();
+    const int kpad = round_up(k, 4);
+    const size_t rows = static_cast<size_t>(round_up(n, 256));
+    w->K = k;
+    w->Kpad = kpad;
+    w->w.K = kpad;
+    w->w.N = n;
+    w->w.hi = c->dzalloc_t<float>(rows * kpad);
+    w->w.lo = c->dzalloc_t<float>(rows * kpad);
+    dim3 grid((n + 31) / 32, (kpad + 31) / 32);
+    transpose_split_pad_kernel<<<grid, dim3(32, 8), 0, c->stream>>>(B, k, n, kpad, w->w.hi, w->w.lo);
+    cuda_ok(cudaGetLastError(), "transpose-split");
+    return w.release();
+}
+
+void free_weight(adai_b200_ctx* c, adai_b200_weight* w) {
+    c->dfree(w->w.hi);
+    c->dfree(w->w.lo);
+    delete w;
+}
+
+void sgemm_prepared(adai_b200_ctx* c, int m, const float* A, const adai_b200_weight* w, float* C, int k) {
+    if (m <= 0 || !A || !C) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad GEMM arguments");
+    const int kpad = w->Kpad;
+    const int rows_alloc = round_up(m, 128);
+    const size_t need = static_cast<size_t>(rows_alloc) * kpad;
+    if (need > c->op_a_floats) {
+        cuda_ok(cudaStreamSynchronize(c->stream), "sync");
+        c->dfree(c->op_a_hi);
+        c->dfree(c->op_a_lo);
+        c->op_a_hi = nullptr;
+        c->op_a_lo = nullptr;
+        c->op_a_floats = 0;
+        c->op_a_hi = c->dalloc_t<float>(need);
+        c->op_a_lo = c->dalloc_t<float>(need);
+        c->op_a_floats = need;
+    }
+    const size_t n = need;
+    const int blocks = static_cast<int>(std::min<size_t>((n + 255) / 256, 148 * 16));
+    split_pad_kernel<<<blocks, 256, 0, c->stream>>>(A, m, k, c->op_a_hi, c->op_a_lo, kpad, rows_alloc);
+    cuda_ok(cudaGetLastError(), "split");
+    GemmEpilogue e;
+    e.flags = kEpiStore;
+    e.out = C;
+    e.ldo = w->w.N;
+    c->gemm(acts(c->op_a_hi, c->op_a_lo, kpad, rows_alloc), m, w->w, e);
+}
+}  // namespace
+
+int adai_b200_weight_create(adai_b200_ctx* c, const float* B, int k, int n, adai_b200_weight** out) {
+    return guarded([&] {
+        check_ctx(c);
+        if (!out) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null output handle");
+        *out = prepare_weight(c, B, k, n);
+    });
+}
+
+int adai_b200_weight_destroy(adai_b200_ctx* c, adai_b200_weight* w) {
+    return guarded([&] {
+        if (!c || !w) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null argument");
+        cudaSetDevice(c->device);
+        cudaStreamSynchronize(c->stream);
+        free_weight(c, w);
+    });
+}
+
+int adai_b200_sgemm_prepared(adai_b200_ctx* c, int m, const float* A, const adai_b200_weight* w, float* C) {
+    return guarded([&] {
+        check_ctx(c);
+        if (!w) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null weight");
+        sgemm_prepared(c, m, A, w, C, w->K);
+    });
+}
+
+int adai_b200_sgemm(adai_b200_ctx* c, int m, int n, int k, const float* A, const float* B, float* C) {
+    return guarded([&] {
+        check_ctx(c);
+        adai_b200_weight* w = prepare_weight(c, B, k, n);
+        try {
+            sgemm_prepared(c, m, A, w, C, k);
+        } catch (...) {
+            cudaStreamSynchronize(c->stream);
+            free_weight(c, w);
+            throw;
+        }
+        cuda_ok(cudaStreamSynchronize(c->stream), "sync");
+        free_weight(c, w);
+    });
+}
+
+int adai_b200_decode_attention(adai_b200_ctx* c, int B, int H, int capacity, const float* q,
+                               const float* k_new, const float* v_new, float* k_cache,
+                               float* v_cache, const int* lens, int max_len, float* out) {
+    return guarded([&] {
+        check_ctx(c);
+        if (B <= 0 || H <= 0 || capacity <= 0 || !q || !k_cache || !v_cache || !lens || !out)
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad attention arguments");
+        if ((k_new == nullptr) != (v_new == nullptr))
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "k_new and v_new must both be given or both be null");
+        const int add = k_new ? 1 : 0;
+        if (max_len + add > capacity) fail(ADAI_B200_ERR_OUT_OF_RANGE, "max_len exceeds the cache capacity");
+        c->ensure_attn_scratch(B, H, max_len + add);
+        DecodeAttnArgs a;
+        a.q = q;
+        a.ldq = H * 64;
+        a.k_new = k_new;
+        a.v_new = v_new;
+        a.ldkv = H * 64;
+        a.kc = k_cache;
+        a.vc = v_cache;
+        a.slot_stride = static_cast<long long>(H) * capacity * 64;
+        a.cap = capacity;
+        a.slots = nullptr;
+        a.len_by_slot = lens;
+        a.len_add = add;
+        a.out = out;
+        a.ldo = H * 64;
+        a.B = B;
+        a.H = H;
+        a.max_len = max_len + add;
+        a.scale = 1.0f / std::sqrt(64.0f);
+        a.ws = c->attn_ws;
+        a.tickets = c->attn_tickets;
+        launch_decode_attention(a, c->d_err, c->stream);
+        cuda_ok(cudaGetLastError(), "attention launch");
+    });
+}
+
+int adai_b200_ctx_last_timing(adai_b200_ctx* c, double* decode_ms, int* kernels_per_step) {
+    return guarded([&] {
+        if (!c) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null context");
+        if (decode_ms) *decode_ms = c->last_decode_ms;
+        if (kernels_per_step) *kernels_per_step = c->last_kernels_per_step;
+    });
+}
+
+int adai_b200_profile_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slots,
+                           const int* ids, int n_classes, double* ms, double* bytes,
+                           double* flops, int* launches) {
+    return guarded([&] {
+        check_ctx(c);
+        check_model(c);
+        check_kv(c, kv);
+        if (n_classes < ADAI_B200_KC_COUNT || !ms || !bytes || !flops || !launches)
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "need ADAI_B200_KC_COUNT entries in every output array");
+        stage_batch(c, kv, B, slots, ids, 1);
+        presize_step_scratch(c, kv, B);
+        Profiler prof;
+        for (int b = 0; b < B; ++b) {
+            prof.sum_self_rows += kv->self_len[slots[b]] + 1;
+            prof.sum_cross_rows += kv->cross_len[slots[b]];
+        }
+        c->prof = &prof;
+        try {
+            record_step(c, kv, B, 0);
+            timed(c, ADAI_B200_KC_OTHER, 0, 0, [&] {
+                record_and_advance_kernel<<<(B + 127) / 128, 128, 0, c->stream>>>(
+                    c->sb.next, c->sb.ids, c->sb.slots, kv->d_self_len, kv->d_hist, kv->self_cap,
+                    c->sb.nonfinite, c->sb.nonfinite_any, B, 0);
+            });
+            c->prof = nullptr;
+            c->sync(wait_timeout_seconds());
+        } catch (...) {
+            c->prof = nullptr;
+            cudaStreamSynchronize(c->stream);
+            for (auto& sp : prof.spans) {
+                cudaEventDestroy(sp.a);
+                cudaEventDestroy(sp.b);
+            }
+            throw;
+        }
+        for (int k = 0; k < n_classes; ++k) {
+            ms[k] = bytes[k] = flops[k] = 0;
+            launches[k] = 0;
+        }
+        for (auto& sp : prof.spans) {
+            float t = 0.f;
+            cuda_ok(cudaEventElapsedTime(&t, sp.a, sp.b), "cudaEventElapsedTime");
+            ms[sp.cls] += t;
+            bytes[sp.cls] += sp.bytes;
+            flops[sp.cls] += sp.flops;
+            launches[sp.cls] += 1;
+            cudaEventDestroy(sp.a);
+            cudaEventDestroy(sp.b);
+        }
+        for (int b = 0; b < B; ++b) kv->self_len[slots[b]] += 1;
+    });
+}
+
+int adai_b200_layernorm(adai_b200_ctx* c, const float* x, const float* gamma, const float* beta,
+                        float* out, int rows, int D) {
+    return guarded([&] {
+        check_ctx(c);
+        if (!x || !gamma || !beta || !out || rows <= 0) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad LayerNorm arguments");
+        if (!layernorm_width_supported(D)) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "D must be 128 * {1,2,3,4,6,8,12,16}");
+        launch_layernorm(x, D, gamma, beta, out, nullptr, nullptr, rows, D, c->stream);
+        cuda_ok(cudaGetLastError(), "layernorm launch");
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,151 @@
+// kernels.h — host-side launch interface of the sm_100a kernels (internal to libadai_b200.so).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace adai_b200 {
+
+// ------------------------------------------------------------------------------------------
+// 3xTF32 tcgen05 GEMM: out[M,N] = epilogue(A[M,K] * W[K,N]) with A given as its tf32 split
+// (A_hi, A_lo, row-major [M,K]) and W given transposed and split (W_hi, W_lo, row-major [N,K]).
+enum GemmFlags : int {
+    kEpiBias = 1,       // + bias[n]
+    kEpiGelu = 2,       // GELU-tanh after the bias
+    kEpiResid = 4,      // resid[m,n] + (...)
+    kEpiStore = 8,      // write fp32 out[m,n]
+    kEpiSplit = 16,     // write the tf32 split of the result to out_hi / out_lo
+    kEpiArgmax = 32,    // per-row first maximum -> next_ids (and the non-finite flag)
+    kEpiKvScatter = 64, // columns [0,D) -> K cache, [D,2D) -> V cache at (row_slot, row_pos)
+};
+
+struct GemmEpilogue {
+    int flags = 0;
+    const float* bias = nullptr;
+    const float* resid = nullptr;
+    int ldr = 0;
+    float* out = nullptr;
+    int ldo = 0;
+    float* out_hi = nullptr;
+    float* out_lo = nullptr;
+    int lds = 0;
+    // argmax
+    int* next_ids = nullptr;
+    int* nonfinite = nullptr;
+    // kv scatter
+    float* kc = nullptr;
+    float* vc = nullptr;
+    long long slot_stride = 0;  // floats between slots
+    int cap = 0;                // rows per (slot, head)
+    int heads = 0;
+    int d_model = 0;
+    const int* row_slot = nullptr;
+    const int* row_pos = nullptr;
+};
+
+// A prepared right-hand operand: W^T split into hi/lo, [N, K] row-major, device memory.
+struct TcWeight {
+    int K = 0, N = 0;
+    float* hi = nullptr;
+    float* lo = nullptr;
+};
+
+// A left-hand operand: the tf32 split of A, [rows_alloc, K] row-major, device memory.
+struct TcActs {
+    int K = 0, rows_alloc = 0;
+    const float* hi = nullptr;
+    const float* lo = nullptr;
+};
+
+struct GemmPlan {
+    int bn = 128;
+    int splits = 1;
+    int stages = 3;
+    int kb_per_split = 0;
+    int m_tiles = 1, n_tiles = 1;
+    size_t smem_bytes = 0;
+};
+
+// Scratch a GEMM launch may use: split-K partial tiles and per-tile tickets (zeroed at creation;
+// every launch leaves them zero again), argmax partials.
+struct GemmScratch {
+    float* ws = nullptr;
+    size_t ws_floats = 0;
+    int* tickets = nullptr;
+    int n_tickets = 0;
+    float* arg_val = nullptr;
+    int* arg_idx = nullptr;
+    size_t arg_entries = 0;
+};
+
+GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms);
+size_t gemm_ws_floats(const GemmPlan& p);
+size_t gemm_arg_entries(const GemmPlan& p);
+
+// Encodes (or reuses) the tensor maps and launches. Returns a cudaError_t-style code: 0 ok,
+// cudaErrorInvalidValue for shapes the kernel cannot take.
+int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& epi,
+                const GemmPlan& plan, const GemmScratch& scratch, int* err, cudaStream_t st);
+
+bool tensor_map_api_available();
+
+// ------------------------------------------------------------------------------------------
+// Row kernels
+void launch_split_tf32(const float* x, float* hi, float* lo, size_t n, cudaStream_t st);
+void launch_transpose_split(const float* w, int K, int N, float* hi_t, float* lo_t,
+                            cudaStream_t st);
+// LayerNorm (two-pass, eps 1e-5) of `rows` rows of x (row stride ldx); writes any of out / the
+// split (out_hi, out_lo), row stride D.
+void launch_layernorm(const float* x, int ldx, const float* g, const float* b, float* out,
+                      float* out_hi, float* out_lo, int rows, int D, cudaStream_t st);
+// x[r] = table[ids[r]] + pe[pos(r)] (no positional row when pos >= pe_rows), then LayerNorm.
+// pos(r) = pos_by_slot ? pos_by_slot[slots[r]] : pos_direct[r].
+void launch_embed_ln(const float* table, const int* ids, const float* pe, int pe_rows,
+                     const int* slots, const int* pos_by_slot, const int* pos_direct, float* x,
+                     const float* g, const float* b, float* out_hi, float* out_lo, int rows,
+                     int D, int vocab, int* err, cudaStream_t st);
+
+// ------------------------------------------------------------------------------------------
+// Attention
+struct DecodeAttnArgs {
+    const float* q = nullptr;  // row b at q + b*ldq; head h at + h*64
+    int ldq = 0;
+    const float* k_new = nullptr;  // self-attention append source (null: no append)
+    const float* v_new = nullptr;
+    int ldkv = 0;
+    float* kc = nullptr;  // this layer's cache: [slot][H][cap][64]
+    float* vc = nullptr;
+    long long slot_stride = 0;
+    int cap = 0;
+    const int* slots = nullptr;        // [B] slot of each batch row (null: row b is slot b)
+    const int* len_by_slot = nullptr;  // rows already cached per slot
+    int len_add = 0;                   // 1 for self-attention (the appended row)
+    float* out = nullptr;              // optional fp32 [B, ldo]
+    float* out_hi = nullptr;           // optional split
+    float* out_lo = nullptr;
+    int ldo = 0;
+    int B = 0, H = 0;
+    int max_len = 0;  // upper bound of len over the batch (sizes the grid)
+    float scale = 0.f;
+    float* ws = nullptr;  // split-KV partials
+    int* tickets = nullptr;
+};
+constexpr int kAttnChunk = 256;  // cached rows per CTA
+constexpr int kAttnPartial = 68; // floats per (b, h, chunk) partial: m, l, 64 acc, 2 pad
+size_t decode_attn_ws_floats(int B, int H, int max_len);
+void launch_decode_attention(const DecodeAttnArgs& a, int* err, cudaStream_t st);
+
+// Encoder self-attention over ragged sequences: qkv [rows, 3D]; sequence s holds rows
+// [offsets[s], offsets[s] + lens[s]); out split [rows, D].
+void launch_prefill_attention(const float* qkv, int D, int H, const int* offsets, const int* lens,
+                              int nseq, int max_len, float* out_hi, float* out_lo, float scale,
+                              cudaStream_t st);
+
+// Decode-loop bookkeeping: ids[b] = next[b]; len_by_slot[slots[b]] += 1.
+void launch_advance(const int* next, int* ids, const int* slots, int* len_by_slot, int B,
+                    cudaStream_t st);
+
+}  // namespace adai_b200

@@ -1,0 +1,203 @@
+/*
+ * adai_b200.h — C ABI of the B200 (sm_100a) batched KV-cached decode step.
+ *
+ * Drop-in target: the GPU decode path of kerfbit/adai (paths below are inside that source tree).
+ * Plain C types only (pointers, ints, floats); no CUDA or C++ types cross this boundary except
+ * the opaque handles. Every call returns an adai_b200_status; adai_b200_last_error() gives the
+ * message of the last failure on the calling thread.
+ *
+ * Threading: one context per GPU, used by one host thread at a time (the reference serialises its
+ * GPU path the same way: EncoderDecoderModel::model_mutex_, src/EncoderDecoderModel.cpp:366 and
+ * :1476, and the cuBLAS mutex, src/gpu/MatrixGPU.cu:356). Several contexts on several GPUs may be
+ * driven from several threads at once; nothing is shared between contexts.
+ *
+ * Layouts: host tensors are row-major fp32 exactly as the reference Matrix holds them
+ * (src/Matrix.hpp:32); weights are W[in, out] as the reference setters take them.
+ */
+#ifndef ADAI_B200_H
+#define ADAI_B200_H
+
+#if defined(__GNUC__)
+#define ADAI_B200_API __attribute__((visibility("default")))
+#else
+#define ADAI_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    ADAI_B200_OK = 0,
+    ADAI_B200_ERR_INVALID_ARGUMENT = 1, /* std::invalid_argument in the reference */
+    ADAI_B200_ERR_OUT_OF_RANGE = 2,     /* std::out_of_range (capacity, token id, slot) */
+    ADAI_B200_ERR_CUDA = 3,             /* a CUDA runtime error (std::runtime_error, CUDA_CHECK) */
+    ADAI_B200_ERR_TIMEOUT = 4,          /* a bounded wait expired; the context is marked unusable */
+    ADAI_B200_ERR_NONFINITE = 5,        /* NaN/+inf logits (TextGenerator::next_logits throws) */
+    ADAI_B200_ERR_STATE = 6,            /* call order (no model, context unusable, ...) */
+    ADAI_B200_ERR_NO_DEVICE = 7         /* no sm_100 device / the tensor-map API is missing */
+} adai_b200_status;
+
+typedef struct adai_b200_ctx adai_b200_ctx;
+typedef struct adai_b200_kv adai_b200_kv;
+typedef struct adai_b200_weight adai_b200_weight;
+
+/* Model shape: the constructor arguments of LLMEncoder (src/encoder.hpp:90), LLMDecoder
+ * (src/Decoder.hpp:125) and LanguageModelHead. */
+typedef struct {
+    int vocab;
+    int d_model;
+    int n_heads;    /* d_model / n_heads must be 64 */
+    int d_ff;
+    int enc_layers;
+    int dec_layers;
+    int max_seq;    /* positional-encoding table rows (PositionalEncoding(max_seq, d_model)) */
+} adai_b200_model_desc;
+
+/* Message of the last failed call on this thread ("" if none). */
+ADAI_B200_API const char* adai_b200_last_error(void);
+
+/* ---- context (replaces GPUManager: one device, one stream; src/gpu/GPUUtils.hpp:98-530) ---- */
+
+/* Creates a context on `device`. mem_fraction in (0, 1] caps the device memory the context will
+ * allocate (GPU_MEMORY_FRACTION, config.conf:262-300); 0 means no cap. */
+ADAI_B200_API int adai_b200_ctx_create(int device, float mem_fraction, adai_b200_ctx** out);
+ADAI_B200_API int adai_b200_ctx_destroy(adai_b200_ctx* ctx);
+/* Bounded host wait for all queued work (GPUDebugSync wait with GPU_WAIT_TIMEOUT_SECONDS,
+ * src/gpu/GPUDebugSync.cpp:236-244). On expiry returns ADAI_B200_ERR_TIMEOUT and marks the
+ * context unusable (the reference marks the device lost). */
+ADAI_B200_API int adai_b200_ctx_synchronize(adai_b200_ctx* ctx, double timeout_seconds);
+/* Device bytes this context holds. */
+ADAI_B200_API int adai_b200_ctx_memory(adai_b200_ctx* ctx, unsigned long long* bytes);
+/* The CUDA stream (as void*) the context launches on. */
+ADAI_B200_API void* adai_b200_ctx_stream(adai_b200_ctx* ctx);
+
+/* ---- model weights ---- */
+
+/* Number of tensors adai_b200_model_upload expects for `desc`. */
+ADAI_B200_API int adai_b200_model_tensor_count(const adai_b200_model_desc* desc);
+
+/* Copies the model to the device (host fp32 row-major). Tensor order:
+ *   enc.embed[V,D]
+ *   per encoder layer: ln1.g[D] ln1.b[D] wq wk wv wo[D,D] ln2.g ln2.b w1[D,F] b1[F] w2[F,D] b2[D]
+ *   enc.lnf.g enc.lnf.b
+ *   dec.embed[V,D]
+ *   per decoder layer: ln1.g ln1.b sa.wq sa.wk sa.wv sa.wo ln2.g ln2.b ca.wq ca.wk ca.wv ca.wo
+ *                      ln3.g ln3.b w1 b1 w2 b2
+ *   dec.lnf.g dec.lnf.b head.w[D,V] head.b[V]
+ * i.e. the setters MultiHeadAttention::set_W* (src/MultiHeadAttention.cpp:630-652),
+ * CrossAttention::set_W* (src/CrossAttention.cpp:717-739), FeedForward::set_W1/b1/W2/b2
+ * (src/FeedForward.hpp:201-212), LayerNorm::set_gamma/set_beta (src/LayerNorm.cpp:218-234),
+ * TokenEmbedding::set_embeddings (src/TokenEmbedding.hpp:259), LanguageModelHead::set_W_output /
+ * set_bias (src/LanguageModelHead.cpp:145-160). Weights are copied; a later change on the host
+ * needs a new upload (the reference's refresh_gpu_mirror, src/MultiHeadAttention.cpp:654-660).
+ * pe_table [max_seq, d_model] may be NULL: the table of src/PositionalEncoding.cpp:13-32 is then
+ * computed on the host. Replaces the previous model, if any. */
+ADAI_B200_API int adai_b200_model_upload(adai_b200_ctx* ctx, const adai_b200_model_desc* desc,
+                           const float* const* tensors, const float* pe_table);
+
+/* ---- KV cache arena (replaces GPUDecoderKVCache, src/gpu/MatrixGPU.hpp:563-623, and the CPU
+ * DecoderKVCache, src/KVCache.hpp:155-245) ----
+ * `max_slots` sequences, each with dec_layers self caches of `self_capacity` rows and cross
+ * caches of `cross_capacity` rows (fixed capacity, as GPUKVCache's max_seq_length). */
+ADAI_B200_API int adai_b200_kv_create(adai_b200_ctx* ctx, int max_slots, int self_capacity, int cross_capacity,
+                        adai_b200_kv** out);
+ADAI_B200_API int adai_b200_kv_destroy(adai_b200_ctx* ctx, adai_b200_kv* kv);
+/* DecoderKVCache::clear() for one slot (self and cross). */
+ADAI_B200_API int adai_b200_kv_reset(adai_b200_ctx* ctx, adai_b200_kv* kv, int slot);
+/* DecoderKVCache::clear_self_attention() for one slot (src/KVCache.hpp:190-196): the decoder
+ * restarts at position 0 over the same encoder output. */
+ADAI_B200_API int adai_b200_kv_clear_self(adai_b200_ctx* ctx, adai_b200_kv* kv, int slot);
+/* Rows currently cached for a slot (DecoderKVCache::current_length, src/KVCache.hpp:235-244). */
+ADAI_B200_API int adai_b200_kv_length(adai_b200_ctx* ctx, adai_b200_kv* kv, int slot, int* self_len,
+                        int* cross_len);
+
+/* ---- encoder prefill + cross K/V (LLMEncoder::encode_with_mask, src/LLMEncoder.cpp:120-142,
+ * with CrossAttention's first-call K/V projection, src/CrossAttention.cpp:388-413) ----
+ * n requests; request i has src_lens[i] source ids (concatenated in ids) and is placed in slot
+ * slots[i], whose self cache is cleared. Host arrays. Optionally returns the encoder output
+ * [sum(src_lens), d_model] (enc_out may be NULL). */
+ADAI_B200_API int adai_b200_encode(adai_b200_ctx* ctx, adai_b200_kv* kv, int n, const int* slots,
+                     const int* ids, const int* src_lens, float* enc_out);
+
+/* ---- one stacked decode step (LLMDecoder::forward_with_cache, src/Decoder.cpp:210-287, for B
+ * sequences at once; LanguageModelHead::forward, src/LanguageModelHead.cpp:49-69; greedy
+ * TextGenerator::argmax, src/TextGenerator.cpp:151-153) ----
+ * Feeds ids[b] to sequence slots[b], appends one row to its self caches and returns the first
+ * maximum of its logits in next_ids[b]. logits [B, vocab] may be NULL. Host arrays; the call
+ * waits for the result. Fails with ADAI_B200_ERR_NONFINITE where the reference's
+ * TextGenerator::next_logits would throw (NaN or +inf logit, or every logit -inf). */
+ADAI_B200_API int adai_b200_decode_step(adai_b200_ctx* ctx, adai_b200_kv* kv, int B, const int* slots,
+                          const int* ids, int* next_ids, float* logits);
+
+/* Greedy decode of `steps` tokens for B sequences, all on the device: the step is captured once
+ * in a CUDA graph and replayed, the argmax fed back on the device. first_ids[b] is the first
+ * token fed (BOS = 2 for a fresh request); out_ids [B, steps] receives step s's argmax in column
+ * s. Host arrays. The same arithmetic as `steps` calls of adai_b200_decode_step. */
+ADAI_B200_API int adai_b200_generate(adai_b200_ctx* ctx, adai_b200_kv* kv, int B, const int* slots,
+                       const int* first_ids, int steps, int* out_ids);
+
+/* ---- op level: stacked GEMM (Matrix::operator*, src/Matrix.cpp:212-277; matrix_multiply_gpu,
+ * src/gpu/MatrixGPU.hpp:100 and src/gpu/MatrixGPU.cu:351-370) ----
+ * C[m,n] = A[m,k] B[k,n], fp32 in and out, 3xTF32 on the tensor cores. Device pointers on the
+ * context's stream; asynchronous. B is prepared (transposed and split) on every call; use
+ * adai_b200_weight_create + adai_b200_sgemm_prepared to prepare it once. */
+ADAI_B200_API int adai_b200_sgemm(adai_b200_ctx* ctx, int m, int n, int k, const float* A, const float* B,
+                    float* C);
+/* Prepares B [k, n] (device pointer) once for repeated products. */
+ADAI_B200_API int adai_b200_weight_create(adai_b200_ctx* ctx, const float* B, int k, int n,
+                            adai_b200_weight** out);
+ADAI_B200_API int adai_b200_weight_destroy(adai_b200_ctx* ctx, adai_b200_weight* w);
+ADAI_B200_API int adai_b200_sgemm_prepared(adai_b200_ctx* ctx, int m, const float* A, const adai_b200_weight* w,
+                             float* C);
+
+/* ---- op level: single-token attention over a KV cache with the append fused in
+ * (MultiHeadAttention::forward_with_cache, src/MultiHeadAttention.cpp:278-395, per-head math
+ * :336-367; KVCache::append, src/KVCache.hpp:99-128) ----
+ * B sequences, H heads of width 64. Cache layout [B][H][capacity][64] (K and V), device
+ * pointers. lens[b] rows are cached for sequence b; when k_new/v_new [B, H*64] are non-NULL they
+ * are appended at row lens[b] first and attention runs over lens[b] + 1 rows (lens is not
+ * updated). q [B, H*64]; out [B, H*64]. Asynchronous on the context's stream. */
+ADAI_B200_API int adai_b200_decode_attention(adai_b200_ctx* ctx, int B, int H, int capacity, const float* q,
+                               const float* k_new, const float* v_new, float* k_cache,
+                               float* v_cache, const int* lens, int max_len, float* out);
+
+/* ---- op level: LayerNorm (LayerNorm::forward, src/LayerNorm.cpp:56-109; the reference GPU
+ * kernel matrix_layer_norm_fwd_gpu, src/gpu/MatrixGPU.hpp:140) ----
+ * out[rows, D] = gamma * (x - mean) / sqrt(var + 1e-5) + beta. Device pointers; D a multiple of
+ * 128 up to 2048. */
+ADAI_B200_API int adai_b200_layernorm(adai_b200_ctx* ctx, const float* x, const float* gamma, const float* beta,
+                        float* out, int rows, int D);
+
+/* ---- measurement ----
+ * Device time (CUDA events on the context stream, around the graph replays) of the decode loop
+ * of the last adai_b200_generate call, and the kernels one replayed step launches. The reference
+ * reports the same figure as ms/token from its decode benchmark
+ * (benchmarks/GpuDecodeBenchmark.cpp:383-420). */
+ADAI_B200_API int adai_b200_ctx_last_timing(adai_b200_ctx* ctx, double* decode_ms,
+                                            int* kernels_per_step);
+
+typedef enum {
+    ADAI_B200_KC_GEMM = 0,       /* stacked projections: Q|K|V, W_o, cross W_q / W_o, FFN */
+    ADAI_B200_KC_SELF_ATTN = 1,  /* decode self-attention with the fused KV append */
+    ADAI_B200_KC_CROSS_ATTN = 2, /* decode cross-attention over the encoder K/V */
+    ADAI_B200_KC_NORM = 3,       /* LayerNorms, embedding + positional row */
+    ADAI_B200_KC_HEAD = 4,       /* LM head GEMM with the fused argmax */
+    ADAI_B200_KC_OTHER = 5,      /* step bookkeeping */
+    ADAI_B200_KC_COUNT = 6
+} adai_b200_kernel_class;
+
+/* Runs one decode step like adai_b200_decode_step (ids fed, one row appended per sequence) but
+ * launched eagerly with a CUDA event pair around every kernel, and returns per kernel class the
+ * summed device time (ms), the algorithmic bytes and flops the launches had to move / compute
+ * (GEMM: 4(MK+KN+MN) bytes, 2MNK flops; attention: the K/V rows read, q read, output written)
+ * and the launch count. Arrays hold n_classes >= ADAI_B200_KC_COUNT entries. */
+ADAI_B200_API int adai_b200_profile_step(adai_b200_ctx* ctx, adai_b200_kv* kv, int B,
+                                         const int* slots, const int* ids, int n_classes,
+                                         double* ms, double* bytes, double* flops,
+                                         int* launches);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ADAI_B200_H */

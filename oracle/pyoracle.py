@@ -1,0 +1,275 @@
+"""ctypes wrappers over the two CPU oracles. TEST INFRASTRUCTURE ONLY.
+
+* `Port`  — oracle/liboracle_port.so, the plain-C restatement (oracle/adai_oracle.c).
+* `Ref`   — oracle/_ref/libadai_ref.so, the reference's own sources built by oracle/Makefile
+            with our driver (oracle/ref_driver.cpp). Present wherever it was built (it travels
+            with the repository snapshot as a built file); `Ref.available()` says whether it is.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this module.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PORT_SO = os.path.join(HERE, "liboracle_port.so")
+REF_SO = os.path.join(HERE, "_ref", "libadai_ref.so")
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+
+
+def build_port() -> None:
+    subprocess.run(["make", "-s", "-C", HERE, "port"], check=True)
+
+
+def _ptr_array(ws):
+    arr = (C.c_void_p * len(ws))()
+    for i, w in enumerate(ws):
+        assert w.dtype == np.float32 and w.flags.c_contiguous
+        arr[i] = w.ctypes.data
+    return arr
+
+
+class _Base:
+    lib: C.CDLL
+
+    def matmul(self, A, B):
+        A = np.ascontiguousarray(A, np.float32)
+        B = np.ascontiguousarray(B, np.float32)
+        M, K = A.shape
+        K2, N = B.shape
+        assert K == K2
+        out = np.empty((M, N), np.float32)
+        self._check(getattr(self.lib, self._p + "matmul")(A, B, out, M, K, N))
+        return out
+
+    def _check(self, rc):
+        if rc not in (None, 0):
+            raise RuntimeError(f"oracle call failed: {self._err()}")
+
+    def _err(self):
+        return "error"
+
+
+class Port(_Base):
+    _p = "orc_"
+
+    def __init__(self):
+        if not os.path.exists(PORT_SO):
+            build_port()
+        lib = C.CDLL(PORT_SO)
+        lib.orc_matmul.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int, C.c_int]
+        lib.orc_matmul.restype = None
+        lib.orc_layernorm.argtypes = [_f32p, _f32p, _f32p, _f32p, C.c_int, C.c_int]
+        lib.orc_gelu.argtypes = [_f32p, _f32p, C.c_int]
+        lib.orc_softmax_row.argtypes = [_f32p, _f32p, C.c_int]
+        lib.orc_pe_table.argtypes = [C.c_int, C.c_int, _f32p]
+        lib.orc_attention_single.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int, C.c_int,
+                                             _f32p]
+        lib.orc_argmax.argtypes = [_f32p, C.c_int]
+        lib.orc_argmax.restype = C.c_int
+        lib.orc_model_create.argtypes = [_i32p, C.c_void_p]
+        lib.orc_model_create.restype = C.c_void_p
+        lib.orc_model_destroy.argtypes = [C.c_void_p]
+        lib.orc_encode.argtypes = [C.c_void_p, _i32p, C.c_int, _f32p]
+        lib.orc_generate.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                     _i32p, C.c_void_p]
+        self.lib = lib
+
+    def layernorm(self, x, g, b):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        self.lib.orc_layernorm(x, np.ascontiguousarray(g, np.float32),
+                               np.ascontiguousarray(b, np.float32), out, x.shape[0], x.shape[1])
+        return out
+
+    def gelu(self, x):
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        out = np.empty_like(x)
+        self.lib.orc_gelu(x, out, x.size)
+        return out
+
+    def softmax_rows(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        for i in range(x.shape[0]):
+            r = np.ascontiguousarray(x[i])
+            o = np.empty_like(r)
+            self.lib.orc_softmax_row(r, o, r.size)
+            out[i] = o
+        return out
+
+    def pe_table(self, max_len, D):
+        out = np.empty((max_len, D), np.float32)
+        self.lib.orc_pe_table(max_len, D, out)
+        return out
+
+    def attention_single(self, q, K, V, H):
+        q = np.ascontiguousarray(q, np.float32)
+        K = np.ascontiguousarray(K, np.float32)
+        V = np.ascontiguousarray(V, np.float32)
+        out = np.empty_like(q)
+        self.lib.orc_attention_single(q, K, V, K.shape[0], K.shape[1], H, out)
+        return out
+
+    def model(self, cfg, weights):
+        return _PortModel(self, cfg, weights)
+
+
+class _PortModel:
+    def __init__(self, port, cfg, weights):
+        self.port, self.cfg = port, cfg
+        self.weights = [np.ascontiguousarray(w, np.float32) for w in weights]
+        self._ptrs = _ptr_array(self.weights)
+        self.h = port.lib.orc_model_create(np.asarray(cfg.as_cfg(), np.int32), self._ptrs)
+        if not self.h:
+            raise ValueError("bad model config")
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.port.lib.orc_model_destroy(self.h)
+            self.h = None
+
+    def encode(self, ids):
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.empty((ids.size, self.cfg.d_model), np.float32)
+        if self.port.lib.orc_encode(self.h, ids, ids.size, out) != 0:
+            raise ValueError("encode failed")
+        return out
+
+    def generate(self, src, steps, bos=2, forced=None, want_logits=False):
+        src = np.ascontiguousarray(src, np.int32)
+        ids = np.empty(steps, np.int32)
+        lg = np.empty((steps, self.cfg.vocab), np.float32) if want_logits else None
+        fz = np.ascontiguousarray(forced, np.int32) if forced is not None else None
+        rc = self.port.lib.orc_generate(self.h, src, src.size, bos, steps,
+                                        fz.ctypes.data if fz is not None else None, ids,
+                                        lg.ctypes.data if lg is not None else None)
+        if rc != 0:
+            raise ValueError("generate failed")
+        return ids, lg
+
+
+class Ref(_Base):
+    _p = "ref_"
+
+    @staticmethod
+    def available() -> bool:
+        return os.path.exists(REF_SO)
+
+    def __init__(self):
+        if not self.available():
+            raise FileNotFoundError(REF_SO)
+        lib = C.CDLL(REF_SO)
+        lib.ref_last_error.restype = C.c_char_p
+        lib.ref_matmul_kernel.restype = C.c_char_p
+        lib.ref_matmul.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int, C.c_int]
+        lib.ref_layernorm.argtypes = [_f32p, _f32p, _f32p, _f32p, C.c_int, C.c_int]
+        lib.ref_gelu.argtypes = [_f32p, _f32p, C.c_int]
+        lib.ref_softmax_rows.argtypes = [_f32p, _f32p, C.c_int, C.c_int]
+        lib.ref_pe_table.argtypes = [C.c_int, C.c_int, _f32p]
+        lib.ref_attention_single.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int, C.c_int,
+                                             _f32p]
+        lib.ref_model_create.argtypes = [_i32p, C.c_void_p, C.POINTER(C.c_void_p)]
+        lib.ref_model_destroy.argtypes = [C.c_void_p]
+        lib.ref_generate_timed.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, C.c_int, _i32p,
+                                           np.ctypeslib.ndpointer(np.float64,
+                                                                  flags="C_CONTIGUOUS"),
+                                           C.POINTER(C.c_double)]
+        lib.ref_encode.argtypes = [C.c_void_p, _i32p, C.c_int, _f32p]
+        lib.ref_generate.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                     _i32p, C.c_void_p, C.POINTER(C.c_double),
+                                     C.POINTER(C.c_double)]
+        self.lib = lib
+
+    def _err(self):
+        return self.lib.ref_last_error().decode()
+
+    def matmul_kernel(self) -> str:
+        return self.lib.ref_matmul_kernel().decode()
+
+    def layernorm(self, x, g, b):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        self._check(self.lib.ref_layernorm(x, np.ascontiguousarray(g, np.float32),
+                                           np.ascontiguousarray(b, np.float32), out,
+                                           x.shape[0], x.shape[1]))
+        return out
+
+    def gelu(self, x):
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        out = np.empty_like(x)
+        self._check(self.lib.ref_gelu(x, out, x.size))
+        return out
+
+    def softmax_rows(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        self._check(self.lib.ref_softmax_rows(x, out, x.shape[0], x.shape[1]))
+        return out
+
+    def pe_table(self, max_len, D):
+        out = np.empty((max_len, D), np.float32)
+        self._check(self.lib.ref_pe_table(max_len, D, out))
+        return out
+
+    def attention_single(self, q, K, V, H):
+        q = np.ascontiguousarray(q, np.float32)
+        K = np.ascontiguousarray(K, np.float32)
+        V = np.ascontiguousarray(V, np.float32)
+        out = np.empty_like(q)
+        self._check(self.lib.ref_attention_single(q, K, V, K.shape[0], K.shape[1], H, out))
+        return out
+
+    def model(self, cfg, weights):
+        return _RefModel(self, cfg, weights)
+
+
+class _RefModel:
+    def __init__(self, ref, cfg, weights):
+        self.ref, self.cfg = ref, cfg
+        ws = [np.ascontiguousarray(w, np.float32) for w in weights]
+        h = C.c_void_p()
+        ref._check(ref.lib.ref_model_create(np.asarray(cfg.as_cfg(), np.int32), _ptr_array(ws),
+                                            C.byref(h)))
+        self.h = h
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.ref.lib.ref_model_destroy(self.h)
+            self.h = None
+
+    def encode(self, ids):
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.empty((ids.size, self.cfg.d_model), np.float32)
+        self.ref._check(self.ref.lib.ref_encode(self.h, ids, ids.size, out))
+        return out
+
+    def generate_timed(self, src, steps, bos=2):
+        """Greedy decode; returns (ids, per-step wall seconds, encoder seconds)."""
+        src = np.ascontiguousarray(src, np.int32)
+        ids = np.empty(steps, np.int32)
+        st = np.empty(steps, np.float64)
+        te = C.c_double()
+        self.ref._check(self.ref.lib.ref_generate_timed(self.h, src, src.size, bos, steps, ids,
+                                                        st, C.byref(te)))
+        return ids, st, te.value
+
+    def generate(self, src, steps, bos=2, forced=None, want_logits=False, timings=None):
+        src = np.ascontiguousarray(src, np.int32)
+        ids = np.empty(steps, np.int32)
+        lg = np.empty((steps, self.cfg.vocab), np.float32) if want_logits else None
+        fz = np.ascontiguousarray(forced, np.int32) if forced is not None else None
+        te, td = C.c_double(), C.c_double()
+        self.ref._check(self.ref.lib.ref_generate(
+            self.h, src, src.size, bos, steps, fz.ctypes.data if fz is not None else None, ids,
+            lg.ctypes.data if lg is not None else None, C.byref(te), C.byref(td)))
+        if timings is not None:
+            timings["encode_s"] = te.value
+            timings["decode_s"] = td.value
+        return ids, lg

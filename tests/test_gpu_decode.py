@@ -1,0 +1,164 @@
+"""The stacked decode step end to end through the C ABI, against the CPU oracle.
+
+The bar (from the decode-path specification): greedy token ids identical to the reference CPU
+path, logits within |gpu - cpu| <= 1e-5 + 1e-4 |cpu|. Checked in lockstep (each step fed the
+oracle's own token, as benchmarks/GpuDecodeBenchmark.cpp:347-375 does) so that one near-tie
+cannot cascade, and free-running (greedy, ids fed back on the device) for whole generations.
+"""
+import numpy as np
+import pytest
+
+from adai_b200.api import Context, StateError
+from adai_b200.config import LARGE, MID, TINY
+from adai_b200.synth import make_sources, make_weights
+from tests.conftest import tol_ratio
+from tests.golden.make_golden import DECODE_LOGIT_STEPS, DECODE_SEQS, DECODE_SRC, DECODE_STEPS
+
+pytestmark = pytest.mark.gpu
+
+BOS = 2
+
+
+def near_tie(logits_row, tol_abs):
+    top2 = np.sort(logits_row)[-2:]
+    return (top2[1] - top2[0]) <= 2 * tol_abs
+
+
+def lockstep(kv, cfg, model, slots, srcs, steps):
+    """Feeds every sequence the oracle's greedy tokens; returns the worst tolerance ratio over
+    all logits and the list of (seq, step) where the argmax differed."""
+    want = [model.generate(s, steps, want_logits=True) for s in srcs]
+    kv.encode(slots, srcs)
+    worst, mismatch = 0.0, []
+    feed = np.full(len(srcs), BOS, np.int32)
+    for t in range(steps):
+        nxt, lg = kv.decode_step(slots, feed, want_logits=True)
+        for i in range(len(srcs)):
+            wid, wlg = want[i][0][t], want[i][1][t]
+            worst = max(worst, tol_ratio(lg[i], wlg))
+            if nxt[i] != wid:
+                mismatch.append((i, t, near_tie(wlg, np.abs(lg[i] - wlg).max())))
+            feed[i] = wid
+    return worst, mismatch
+
+
+@pytest.fixture(scope="module")
+def tiny(ctx):
+    w = make_weights(TINY, 0, affine=True)
+    ctx.upload(TINY, w)
+    return w
+
+
+def test_encoder_output_matches_oracle(ctx, port, tiny, golden):
+    kv = ctx.kv_arena(4, 64, 64)
+    srcs = make_sources(TINY, DECODE_SEQS, (DECODE_SRC, DECODE_SRC), 0)
+    out = kv.encode([0, 1, 2], srcs, want_output=True)
+    assert tol_ratio(out[:DECODE_SRC], golden["tiny_enc0"]) <= 1.0
+    m = port.model(TINY, tiny)
+    for i, s in enumerate(srcs):
+        assert tol_ratio(out[i * DECODE_SRC:(i + 1) * DECODE_SRC], m.encode(s)) <= 1.0
+    kv.close()
+
+
+def test_tiny_lockstep_against_golden(ctx, tiny, golden):
+    kv = ctx.kv_arena(DECODE_SEQS, 32, 32)
+    srcs = make_sources(TINY, DECODE_SEQS, (DECODE_SRC, DECODE_SRC), 0)
+    kv.encode(list(range(DECODE_SEQS)), srcs)
+    feed = np.full(DECODE_SEQS, BOS, np.int32)
+    for t in range(DECODE_STEPS):
+        nxt, lg = kv.decode_step(list(range(DECODE_SEQS)), feed, want_logits=True)
+        np.testing.assert_array_equal(nxt, golden["tiny_ids"][:, t])
+        if t < DECODE_LOGIT_STEPS:
+            assert tol_ratio(lg, golden["tiny_logits"][:, t]) <= 1.0
+        feed = golden["tiny_ids"][:, t].astype(np.int32)
+    kv.close()
+
+
+def test_tiny_workload_free_running_greedy(ctx, port, tiny):
+    # The tiny encoder-decoder workload: batch 8, source length 64, 32 greedy tokens.
+    srcs = make_sources(TINY, 8, (64, 64), 0)
+    kv = ctx.kv_arena(8, 40, 64)
+    kv.encode(list(range(8)), srcs)
+    got = kv.generate(list(range(8)), [BOS] * 8, 32)
+    m = port.model(TINY, tiny)
+    for i, s in enumerate(srcs):
+        np.testing.assert_array_equal(got[i], m.generate(s, 32)[0])
+    assert kv.length(3) == (32, 64)
+    kv.close()
+
+
+def test_generate_equals_repeated_decode_step(ctx, tiny):
+    srcs = make_sources(TINY, 5, (10, 40), 9)
+    slots = [4, 0, 7, 2, 5]   # non-contiguous slots, ragged sources
+    kv1 = ctx.kv_arena(8, 24, 64)
+    kv1.encode(slots, srcs)
+    g = kv1.generate(slots, [BOS] * 5, 20)
+    kv2 = ctx.kv_arena(8, 24, 64)
+    kv2.encode(slots, srcs)
+    feed = np.full(5, BOS, np.int32)
+    for t in range(20):
+        nxt, _ = kv2.decode_step(slots, feed)
+        np.testing.assert_array_equal(nxt, g[:, t])
+        feed = nxt
+    kv1.close()
+    kv2.close()
+
+
+def test_ragged_batch_lockstep_with_random_affine(ctx, port, tiny):
+    srcs = make_sources(TINY, 6, (1, 64), 21)
+    kv = ctx.kv_arena(6, 16, 64)
+    worst, mism = lockstep(kv, TINY, port.model(TINY, tiny), [5, 3, 1, 0, 2, 4], srcs, 16)
+    assert worst <= 1.0, worst
+    assert all(tie for _, _, tie in mism), mism
+    kv.close()
+
+
+def test_mid_model_lockstep(port):
+    # Mid encoder-decoder (d_model 512, 8 heads, 6+6 layers, d_ff 2048, vocab 16000); 4 of the
+    # workload's 64 sequences (source length 256), 12 steps.
+    with Context(0) as c:
+        w = make_weights(MID, 1)
+        c.upload(MID, w)
+        srcs = make_sources(MID, 4, (256, 256), 1)
+        kv = c.kv_arena(4, 16, 256)
+        worst, mism = lockstep(kv, MID, port.model(MID, w), [0, 1, 2, 3], srcs, 12)
+        assert worst <= 1.0, worst
+        assert all(tie for _, _, tie in mism), mism
+        kv.close()
+
+
+def test_large_model_lockstep(port):
+    # Large encoder-decoder (d_model 1024, 16 heads, 12+12 layers, d_ff 4096, vocab 32000); two
+    # sequences with sources of 130 and 300 ids (the workload's range is 128-1024), 4 steps.
+    with Context(0) as c:
+        w = make_weights(LARGE, 2)
+        c.upload(LARGE, w)
+        srcs = make_sources(LARGE, 2, (128, 300), 2)
+        kv = c.kv_arena(2, 8, 1024)
+        worst, mism = lockstep(kv, LARGE, port.model(LARGE, w), [0, 1], srcs, 4)
+        assert worst <= 1.0, worst
+        assert all(tie for _, _, tie in mism), mism
+        kv.close()
+
+
+def test_errors_follow_reference_exceptions(ctx, tiny):
+    kv = ctx.kv_arena(2, 2, 16)
+    with pytest.raises(StateError):          # no encoder output yet
+        kv.decode_step([0], [BOS])
+    src = make_sources(TINY, 1, (8, 8), 0)
+    kv.encode([0], src)
+    with pytest.raises(IndexError):          # TokenEmbedding: id out of range
+        kv.decode_step([0], [TINY.vocab])
+    with pytest.raises(IndexError):          # slot out of range
+        kv.decode_step([2], [BOS])
+    with pytest.raises(ValueError):          # one slot twice in a batch
+        kv.encode([1, 1], src * 2)
+    with pytest.raises(ValueError):          # encoder input longer than max_seq_length
+        kv.encode([1], [np.arange(4, 4 + TINY.max_seq + 1) % TINY.vocab])
+    kv.decode_step([0], [BOS])
+    kv.decode_step([0], [BOS])
+    with pytest.raises(IndexError):          # self-attention cache full
+        kv.decode_step([0], [BOS])
+    kv.reset(0)
+    assert kv.length(0) == (0, 0)
+    kv.close()
