@@ -101,7 +101,7 @@ def load() -> C.CDLL:
     lib.adai_b200_weight_create.argtypes = [_vp, _vp, C.c_int, C.c_int, C.POINTER(_vp)]
     lib.adai_b200_weight_destroy.argtypes = [_vp, _vp]
     lib.adai_b200_sgemm_prepared.argtypes = [_vp, C.c_int, _vp, _vp, _vp]
-    lib.adai_b200_decode_attention.argtypes = [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp,
+    lib.adai_b200_decode_attention.argtypes = [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp,
                                                _vp, _vp, _vp, C.c_int, _vp]
     lib.adai_b200_layernorm.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int]
     lib.adai_b200_ctx_last_timing.argtypes = [_vp, C.POINTER(C.c_double), _ip]
@@ -201,9 +201,9 @@ class Context:
         return PreparedWeight(self, B_ptr, k, n)
 
     def decode_attention(self, B, H, capacity, q, k_new, v_new, k_cache, v_cache, lens, max_len,
-                         out) -> None:
-        check(self.lib.adai_b200_decode_attention(self.h, B, H, capacity, q, k_new, v_new,
-                                                  k_cache, v_cache, lens, max_len, out))
+                         out, head_dim=64) -> None:
+        check(self.lib.adai_b200_decode_attention(self.h, B, H, head_dim, capacity, q, k_new,
+                                                  v_new, k_cache, v_cache, lens, max_len, out))
 
     def layernorm(self, x, gamma, beta, out, rows, D) -> None:
         check(self.lib.adai_b200_layernorm(self.h, x, gamma, beta, out, rows, D))

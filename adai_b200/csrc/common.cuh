@@ -69,7 +69,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.
+// Bounded wait for the phase with the given parity to complete. Gives up after kSpinTimeoutNs
+// (recording `code`), or at once when another thread of the context has already recorded an
+// error, so one failure does not make every later wait run to its deadline.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, parity)) return true;
@@ -77,11 +79,42 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     while (true) {
         for (int i = 0; i < 256; ++i)
             if (mbar_try_wait(addr, parity)) return true;
+        if (err && *reinterpret_cast<volatile int*>(err) != 0) return false;
         if (globaltimer_ns() - t0 > kSpinTimeoutNs) {
             record_error(err, code);
             return false;
         }
     }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Thread-block clusters: rank, barrier, and loads from a peer CTA's shared memory (DSMEM).
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Every thread of every CTA of the cluster must execute this (warp-converged).
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+                 "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t local_smem_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(cluster_addr)
+                 : "memory");
+    return v;
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -126,13 +126,13 @@ struct EncBufs {
 };
 
 struct adai_b200_kv {
-    int max_slots = 0, self_cap = 0, cross_cap = 0, L = 0, H = 0;
+    int max_slots = 0, self_cap = 0, cross_cap = 0, L = 0, H = 0, dh = 64;
     float *self_k = nullptr, *self_v = nullptr, *cross_k = nullptr, *cross_v = nullptr;
     int *d_self_len = nullptr, *d_cross_len = nullptr;
     int* d_hist = nullptr;  // [max_slots][self_cap]: the argmax produced at each position
     std::vector<int> self_len, cross_len;
-    long long self_slot_stride() const { return static_cast<long long>(H) * self_cap * 64; }
-    long long cross_slot_stride() const { return static_cast<long long>(H) * cross_cap * 64; }
+    long long self_slot_stride() const { return static_cast<long long>(H) * self_cap * dh; }
+    long long cross_slot_stride() const { return static_cast<long long>(H) * cross_cap * dh; }
     float* self_k_layer(int l) const { return self_k + static_cast<size_t>(l) * max_slots * self_slot_stride(); }
     float* self_v_layer(int l) const { return self_v + static_cast<size_t>(l) * max_slots * self_slot_stride(); }
     float* cross_k_layer(int l) const { return cross_k + static_cast<size_t>(l) * max_slots * cross_slot_stride(); }
@@ -314,8 +314,8 @@ struct adai_b200_ctx {
             }
         }
     }
-    void ensure_attn_scratch(int B, int H, int max_len) {
-        const size_t f = decode_attn_ws_floats(B, H, max_len);
+    void ensure_attn_scratch(int B, int H, int max_len, int dh) {
+        const size_t f = decode_attn_ws_floats(B, H, max_len, dh);
         const int tk = B * H;
         if (f > attn_ws_floats || tk > attn_n_tickets) {
             cuda_ok(cudaStreamSynchronize(stream), "sync before scratch growth");
@@ -411,8 +411,8 @@ void validate_desc(const adai_b200_model_desc* d) {
     if (d->vocab <= 0 || d->d_model <= 0 || d->n_heads <= 0 || d->d_ff <= 0 ||
         d->enc_layers < 0 || d->dec_layers <= 0 || d->max_seq <= 0)
         fail(ADAI_B200_ERR_INVALID_ARGUMENT, "model dimensions must be positive");
-    if (d->d_model % d->n_heads || d->d_model / d->n_heads != 64)
-        fail(ADAI_B200_ERR_INVALID_ARGUMENT, "d_model / n_heads must be 64 (head width of the kernels)");
+    if (d->d_model % d->n_heads || !attention_head_dim_supported(d->d_model / d->n_heads))
+        fail(ADAI_B200_ERR_INVALID_ARGUMENT, "d_model / n_heads must be 32 or 64 (head widths of the attention kernels)");
     if (!layernorm_width_supported(d->d_model))
         fail(ADAI_B200_ERR_INVALID_ARGUMENT, "d_model must be 128 * {1,2,3,4,6,8,12,16}");
     if (d->d_ff % 16 || d->vocab % 4)
@@ -525,7 +525,7 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
     StepBufs& s = c->sb;
     const int D = m.d.d_model, F = m.d.d_ff, H = m.d.n_heads, L = m.d.dec_layers;
     const int R = s.rows;
-    const float scale = 1.0f / std::sqrt(64.0f);
+    const float scale = 1.0f / std::sqrt(static_cast<float>(D / H));
     cudaStream_t st = c->stream;
     const double Bd = B, Dd = D, Fd = F;
     const double ln_bytes = 2.0 * Bd * Dd * 4.0;
@@ -568,6 +568,7 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             a.ldo = D;
             a.B = B;
             a.H = H;
+            a.head_dim = D / H;
             a.max_len = kv->self_cap;
             a.scale = scale;
             a.ws = c->attn_ws;
@@ -612,6 +613,7 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             a.ldo = D;
             a.B = B;
             a.H = H;
+            a.head_dim = D / H;
             a.max_len = kv->cross_cap;
             a.scale = scale;
             a.ws = c->attn_ws;
@@ -697,7 +699,7 @@ void presize_step_scratch(adai_b200_ctx* c, adai_b200_kv* kv, int B) {
                            std::make_tuple(F, D, 0), std::make_tuple(D, F, 0),
                            std::make_tuple(m.d.vocab, D, (int)kEpiArgmax)})
         c->ensure_gemm_scratch(gemm_plan(B, std::get<0>(sh), std::get<1>(sh), std::get<2>(sh), c->num_sms));
-    c->ensure_attn_scratch(B, m.d.n_heads, std::max(kv->self_cap, kv->cross_cap));
+    c->ensure_attn_scratch(B, m.d.n_heads, std::max(kv->self_cap, kv->cross_cap), kv->dh);
 }
 
 cudaGraphExec_t get_graph(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
@@ -957,6 +959,7 @@ int adai_b200_kv_create(adai_b200_ctx* c, int max_slots, int self_cap, int cross
         kv->cross_cap = cross_cap;
         kv->L = m.d.dec_layers;
         kv->H = m.d.n_heads;
+        kv->dh = m.d.d_model / m.d.n_heads;
         const size_t self_n = static_cast<size_t>(kv->L) * max_slots * kv->self_slot_stride();
         const size_t cross_n = static_cast<size_t>(kv->L) * max_slots * kv->cross_slot_stride();
         std::vector<void*> got;
@@ -1065,7 +1068,7 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
         ensure_enc_bufs(c);
         EncBufs& e = c->eb;
         const int D = m.d.d_model, F = m.d.d_ff, H = m.d.n_heads;
-        const float scale = 1.0f / std::sqrt(64.0f);
+        const float scale = 1.0f / std::sqrt(static_cast<float>(D / H));
         cudaStream_t st = c->stream;
         long long row_base = 0;
         int i0 = 0;
@@ -1150,7 +1153,7 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
                 s.vc = kv->cross_v_layer(l);
                 s.slot_stride = kv->cross_slot_stride();
                 s.cap = kv->cross_cap;
-                s.heads = H;
+                s.head_dim = D / H;
                 s.d_model = D;
                 s.row_slot = e.row_slot;
                 s.row_pos = e.row_pos;
@@ -1365,37 +1368,43 @@ int adai_b200_sgemm(adai_b200_ctx* c, int m, int n, int k, const float* A, const
     });
 }
 
-int adai_b200_decode_attention(adai_b200_ctx* c, int B, int H, int capacity, const float* q,
-                               const float* k_new, const float* v_new, float* k_cache,
-                               float* v_cache, const int* lens, int max_len, float* out) {
+int adai_b200_decode_attention(adai_b200_ctx* c, int B, int H, int head_dim, int capacity,
+                               const float* q, const float* k_new, const float* v_new,
+                               float* k_cache, float* v_cache, const int* lens, int max_len,
+                               float* out) {
     return guarded([&] {
         check_ctx(c);
         if (B <= 0 || H <= 0 || capacity <= 0 || !q || !k_cache || !v_cache || !lens || !out)
             fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad attention arguments");
+        if (!attention_head_dim_supported(head_dim))
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "head_dim must be 32 or 64");
         if ((k_new == nullptr) != (v_new == nullptr))
             fail(ADAI_B200_ERR_INVALID_ARGUMENT, "k_new and v_new must both be given or both be null");
         const int add = k_new ? 1 : 0;
-        if (max_len + add > capacity) fail(ADAI_B200_ERR_OUT_OF_RANGE, "max_len exceeds the cache capacity");
-        c->ensure_attn_scratch(B, H, max_len + add);
+        if (max_len < 0 || max_len + add > capacity)
+            fail(ADAI_B200_ERR_OUT_OF_RANGE, "max_len exceeds the cache capacity");
+        c->ensure_attn_scratch(B, H, max_len + add, head_dim);
+        const int D = H * head_dim;
         DecodeAttnArgs a;
         a.q = q;
-        a.ldq = H * 64;
+        a.ldq = D;
         a.k_new = k_new;
         a.v_new = v_new;
-        a.ldkv = H * 64;
+        a.ldkv = D;
         a.kc = k_cache;
         a.vc = v_cache;
-        a.slot_stride = static_cast<long long>(H) * capacity * 64;
+        a.slot_stride = static_cast<long long>(H) * capacity * head_dim;
         a.cap = capacity;
         a.slots = nullptr;
         a.len_by_slot = lens;
         a.len_add = add;
         a.out = out;
-        a.ldo = H * 64;
+        a.ldo = D;
         a.B = B;
         a.H = H;
+        a.head_dim = head_dim;
         a.max_len = max_len + add;
-        a.scale = 1.0f / std::sqrt(64.0f);
+        a.scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
         a.ws = c->attn_ws;
         a.tickets = c->attn_tickets;
         launch_decode_attention(a, c->d_err, c->stream);

@@ -11,13 +11,17 @@
 // within a few fp32 ulps of an fp32 GEMM. The weights are split once at upload (stored W^T,
 // K-major, hi and lo planes); activations arrive already split by the kernel that produced them.
 //
-// Structure (one CTA = one 128 x BN output tile, or one K-slice of it):
+// One CTA computes one 128 x BN output tile over one K-slice:
 //   warp 0    TMA producer: 4 boxes per stage (A_hi, A_lo 128x32; W_hi, W_lo BNx32), 128B swizzle
 //   warp 1    TMEM allocator + single-thread tcgen05.mma issuer (3 MMAs per K=8 step)
-//   warps 2-5 epilogue: tcgen05.ld 32 rows x 16 columns per warp, fused bias / GELU / residual /
-//             tf32 split of the output / KV-cache scatter / first-maximum argmax partials.
-// Split-K writes fp32 partial tiles to scratch; the last CTA of a tile (ticket counter) sums the
-// partials in split order 0..S-1 — deterministic — and runs the epilogue. No cluster multicast.
+//   warps 2-5 drain the TMEM accumulator (tcgen05.ld, 32 rows x 16 columns per warp) into a
+//             padded shared-memory tile.
+// Split-K: the S K-slices of a tile are the S CTAs of one thread-block cluster. After a cluster
+// barrier every CTA reduces its 128/S rows of the tile by reading the S partial tiles over
+// distributed shared memory in rank order 0..S-1 (deterministic, no global scratch), then all six
+// warps run the fused epilogue one row per warp, so every store is a coalesced float4 run:
+// bias / GELU / residual / fp32 store / tf32 split of the output / KV-cache scatter /
+// first-maximum argmax partials (the LM head). No TMA multicast anywhere.
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
@@ -33,17 +37,19 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 32;  // fp32 elements per 128-byte swizzled row
 constexpr int kThreads = 192;
+constexpr int kWarps = kThreads / 32;
 constexpr int kATileBytes = kBM * kBK * 4;  // 16 KB
 constexpr size_t kSmemLimit = 227 * 1024;
 constexpr size_t kSmemReserve = 1024 /*alignment slack*/ + 256 /*barriers*/;
 
+constexpr int kMaxCluster = 8;
+
 struct __align__(64) GemmKParams {
     CUtensorMap a_hi, a_lo, b_hi, b_lo;
     int M, N, K;
-    int bn, stages, kb_per_split, splits, n_tiles, m_tiles, total_kb;
+    int bn, stages, kb_per_split, splits, n_tiles, m_tiles, total_kb, chunk_kb;
     uint32_t idesc, tmem_cols;
     GemmEpilogue epi;
-    float* ws;
     int* tickets;
     float* arg_val;
     int* arg_idx;
@@ -58,115 +64,144 @@ struct ArgState {
     int nf;
 };
 
-__device__ __forceinline__ void st4(float* p, float a, float b, float c, float d) {
-    *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+__device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+
+__device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
 }
 
-// Epilogue on 16 consecutive accumulator columns [col, col+16) of one output row.
-__device__ __forceinline__ void epilogue16(const GemmKParams& p, int row, int col, float (&v)[16],
-                                           ArgState& as) {
+__device__ __forceinline__ void st_shared_f4(uint32_t addr, float a, float b, float c, float d) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c),
+                 "f"(d)
+                 : "memory");
+}
+
+// Epilogue on 4 consecutive output columns [col, col+4) of one row (col % 4 == 0, col < N).
+__device__ __forceinline__ void epilogue4(const GemmKParams& p, int row, int col, float4 acc,
+                                          ArgState& as) {
     const GemmEpilogue& e = p.epi;
     const int N = p.N;
-    const bool full = col + 16 <= N;
+    const int nv = min(4, N - col);
+    float v[4] = {acc.x, acc.y, acc.z, acc.w};
     if (e.flags & kEpiBias) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-            if (full || col + j < N) v[j] += __ldg(e.bias + col + j);
+        for (int j = 0; j < 4; ++j)
+            if (j < nv) v[j] += __ldg(e.bias + col + j);
     }
     if (e.flags & kEpiGelu) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = gelu_tanh(v[j]);
+        for (int j = 0; j < 4; ++j) v[j] = gelu_tanh(v[j]);
     }
     if (e.flags & kEpiResid) {
         const float* r = e.resid + static_cast<size_t>(row) * e.ldr + col;
+        if (nv == 4 && (e.ldr & 3) == 0) {
+            const float4 rv = *reinterpret_cast<const float4*>(r);
+            v[0] = rv.x + v[0];
+            v[1] = rv.y + v[1];
+            v[2] = rv.z + v[2];
+            v[3] = rv.w + v[3];
+        } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-            if (full || col + j < N) v[j] = r[j] + v[j];
+            for (int j = 0; j < 4; ++j)
+                if (j < nv) v[j] = r[j] + v[j];
+        }
     }
     if (e.flags & kEpiArgmax) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            if (full || col + j < N) {
+        for (int j = 0; j < 4; ++j) {
+            if (j < nv) {
                 const float x = v[j];
                 if (isnan(x) || x == INFINITY) as.nf = 1;
-                if (x > as.best) {
+                if (x > as.best) {  // strictly greater: the first maximum in column order wins
                     as.best = x;
                     as.idx = col + j;
                 }
             }
         }
     }
-    const bool vec = full && ((col & 3) == 0);
     if (e.flags & kEpiStore) {
         float* o = e.out + static_cast<size_t>(row) * e.ldo + col;
-        if (vec && ((e.ldo & 3) == 0)) {
-#pragma unroll
-            for (int j = 0; j < 16; j += 4) st4(o + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+        if (nv == 4 && (e.ldo & 3) == 0) {
+            st4(o, make_float4(v[0], v[1], v[2], v[3]));
         } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (col + j < N) o[j] = v[j];
+            for (int j = 0; j < 4; ++j)
+                if (j < nv) o[j] = v[j];
         }
     }
     if (e.flags & kEpiSplit) {
+        float h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) split_tf32(v[j], h[j], l[j]);
         float* oh = e.out_hi + static_cast<size_t>(row) * e.lds + col;
         float* ol = e.out_lo + static_cast<size_t>(row) * e.lds + col;
-        float h[16], l[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) split_tf32(v[j], h[j], l[j]);
-        if (vec && ((e.lds & 3) == 0)) {
-#pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-                st4(oh + j, h[j], h[j + 1], h[j + 2], h[j + 3]);
-                st4(ol + j, l[j], l[j + 1], l[j + 2], l[j + 3]);
-            }
+        if (nv == 4 && (e.lds & 3) == 0) {
+            st4(oh, make_float4(h[0], h[1], h[2], h[3]));
+            st4(ol, make_float4(l[0], l[1], l[2], l[3]));
         } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (col + j < N) {
+            for (int j = 0; j < 4; ++j)
+                if (j < nv) {
                     oh[j] = h[j];
                     ol[j] = l[j];
                 }
         }
     }
     if (e.flags & kEpiKvScatter) {
-        // 16-column chunks never straddle a head (head width 64) nor the K/V boundary (d_model).
+        // columns [0, D) are K, [D, 2D) are V; a 4-column group never straddles a head.
         const int kv = col / e.d_model;
         const int cc = col - kv * e.d_model;
-        const int h = cc >> 6, j0 = cc & 63;
+        const int h = cc / e.head_dim, j0 = cc - h * e.head_dim;
         const int slot = e.row_slot[row], t = e.row_pos[row];
         float* dst = (kv ? e.vc : e.kc) + static_cast<long long>(slot) * e.slot_stride +
-                     (static_cast<long long>(h) * e.cap + t) * 64 + j0;
-#pragma unroll
-        for (int j = 0; j < 16; j += 4) st4(dst + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+                     (static_cast<long long>(h) * e.cap + t) * e.head_dim + j0;
+        st4(dst, make_float4(v[0], v[1], v[2], v[3]));
     }
 }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
+// The accumulator is promoted to fp32 registers chunk by chunk: the tensor core accumulates a
+// chunk of K (chunk_kb blocks of 32) into one of two TMEM buffers while the epilogue warps add
+// the other buffer's finished chunk into registers with round-to-nearest fp32 adds. Within a
+// buffer the dominant hi*hi products and the small correction terms (lo*hi + hi*lo) have
+// separate accumulators, so the small terms never round against the large running sum.
+// Together this keeps the rounding of long K sums at the level of an fp32 FMA chain, where one
+// TMEM accumulator over the whole K would drift (the tensor core's accumulation does not round
+// to nearest).
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_constant__ GemmKParams p) {
-    // An earlier kernel on this context already failed: do nothing rather than wait on it.
-    if (p.err && *reinterpret_cast<volatile int*>(p.err) != 0) return;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    const int bn = p.bn;
     const int stages = p.stages;
-    const int b_tile_bytes = bn * kBK * 4;
-    const int stage_bytes = 2 * kATileBytes + 2 * b_tile_bytes;
-    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(stages) * stage_bytes);
+    const int S = p.splits;
+    constexpr int b_tile_bytes = BN * kBK * 4;
+    constexpr int stage_bytes = 2 * kATileBytes + 2 * b_tile_bytes;
+    constexpr int bnp = BN + 4;  // padded row of the staging tile (floats): conflict-free float4 rows
+    const size_t pipe_bytes = static_cast<size_t>(stages) * stage_bytes;
+    constexpr size_t stage_tile_bytes = static_cast<size_t>(kBM) * bnp * 4;
+    const size_t bar_off = ((pipe_bytes > stage_tile_bytes ? pipe_bytes : stage_tile_bytes) + 7) & ~size_t(7);
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + bar_off);
     uint64_t* empty_bar = full_bar + stages;
-    uint64_t* accum_bar = empty_bar + stages;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
+    uint64_t* tfull_bar = empty_bar + stages;  // [2] chunk accumulated in TMEM buffer b
+    uint64_t* tempty_bar = tfull_bar + 2;      // [2] TMEM buffer b drained by the epilogue
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
     int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int nt = blockIdx.x, mt = blockIdx.y, split = blockIdx.z;
-    const int m0 = mt * kBM, n0 = nt * bn;
+    const int nt = blockIdx.x, mt = blockIdx.y;
+    const int split = (S > 1) ? static_cast<int>(cluster_ctarank()) : 0;
+    const int m0 = mt * kBM, n0 = nt * BN;
     const int kb0 = split * p.kb_per_split;
     const int kb1 = min(p.total_kb, kb0 + p.kb_per_split);
-    const int nkb = kb1 - kb0;
+    const int nkb = max(0, kb1 - kb0);
+    const int CK = p.chunk_kb;
+    const int nchunks = (nkb + CK - 1) / CK;
 
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&p.a_hi);
@@ -177,7 +212,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
-        mbar_init(accum_bar, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull_bar[b], 1);
+            mbar_init(&tempty_bar[b], 4);  // one arrival per epilogue warp
+        }
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -187,9 +225,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    const uint32_t tile_s = smem_u32(smem);  // staging tile (reuses the pipeline buffers)
 
     if (warp == 0) {
         if (lane == 0 && nkb > 0) {
+            int issued = 0;
             for (int i = 0; i < nkb; ++i) {
                 const int s = i % stages;
                 const uint32_t round = static_cast<uint32_t>(i / stages);
@@ -201,147 +241,180 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
                 tma_load_2d(st + kATileBytes, &p.a_lo, &full_bar[s], kx, m0);
                 tma_load_2d(st + 2 * kATileBytes, &p.b_hi, &full_bar[s], kx, n0);
                 tma_load_2d(st + 2 * kATileBytes + b_tile_bytes, &p.b_lo, &full_bar[s], kx, n0);
+                ++issued;
             }
+            // No copy may still be landing in shared memory when the CTA moves on: wait (bounded)
+            // for the last load of every stage. Immediate when the MMA warp consumed them all.
+            for (int i = max(0, issued - stages); i < issued; ++i)
+                mbar_wait(&full_bar[i % stages], static_cast<uint32_t>(i / stages) & 1u, p.err,
+                          kDevTimeoutTmaFull);
         }
     } else if (warp == 1) {
         if (lane == 0 && nkb > 0) {
             bool ok = true;
-            for (int i = 0; i < nkb && ok; ++i) {
-                const int s = i % stages;
-                const uint32_t round = static_cast<uint32_t>(i / stages);
-                if (!mbar_wait(&full_bar[s], round & 1u, p.err, kDevTimeoutTmaFull)) {
+            int i = 0;
+            for (int c = 0; c < nchunks && ok; ++c) {
+                const int b = c & 1;
+                const uint32_t use = static_cast<uint32_t>(c >> 1);
+                if (c >= 2 && !mbar_wait(&tempty_bar[b], (use - 1u) & 1u, p.err, kDevTimeoutAccum)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t st = smem_u32(smem + static_cast<size_t>(s) * stage_bytes);
-                const uint32_t a_hi = st, a_lo = st + kATileBytes;
-                const uint32_t b_hi = st + 2 * kATileBytes, b_lo = b_hi + b_tile_bytes;
+                const uint32_t t_big = tmem_base + static_cast<uint32_t>(b * 2 * BN);
+                const uint32_t t_small = t_big + BN;
+                const int kend = min(nkb, (c + 1) * CK);
+                for (; i < kend; ++i) {
+                    const int s = i % stages;
+                    const uint32_t round = static_cast<uint32_t>(i / stages);
+                    if (!mbar_wait(&full_bar[s], round & 1u, p.err, kDevTimeoutTmaFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t st = smem_u32(smem + static_cast<size_t>(s) * stage_bytes);
+                    const uint32_t a_hi = st, a_lo = st + kATileBytes;
+                    const uint32_t b_hi = st + 2 * kATileBytes, b_lo = b_hi + b_tile_bytes;
 #pragma unroll
-                for (int kk = 0; kk < kBK / 8; ++kk) {
-                    const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
-                    const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-                    // small terms first, then the dominant hi*hi product
-                    mma_tf32(tmem_base, smem_desc_k_sw128(a_lo + off), smem_desc_k_sw128(b_hi + off),
-                             p.idesc, acc);
-                    mma_tf32(tmem_base, smem_desc_k_sw128(a_hi + off), smem_desc_k_sw128(b_lo + off),
-                             p.idesc, 1u);
-                    mma_tf32(tmem_base, smem_desc_k_sw128(a_hi + off), smem_desc_k_sw128(b_hi + off),
-                             p.idesc, 1u);
+                    for (int kk = 0; kk < kBK / 8; ++kk) {
+                        const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
+                        const uint32_t acc = (i == c * CK && kk == 0) ? 0u : 1u;
+                        mma_tf32(t_small, smem_desc_k_sw128(a_lo + off), smem_desc_k_sw128(b_hi + off),
+                                 p.idesc, acc);
+                        mma_tf32(t_small, smem_desc_k_sw128(a_hi + off), smem_desc_k_sw128(b_lo + off),
+                                 p.idesc, 1u);
+                        mma_tf32(t_big, smem_desc_k_sw128(a_hi + off), smem_desc_k_sw128(b_hi + off),
+                                 p.idesc, acc);
+                    }
+                    mma_commit(&empty_bar[s]);
                 }
-                mma_commit(&empty_bar[s]);
+                if (ok) mma_commit(&tfull_bar[b]);
             }
-            if (ok) mma_commit(accum_bar);
         }
     } else {
-        // ---------------- epilogue warps 2..5 ----------------
+        // ---- warps 2..5: promote each finished chunk into fp32 registers ----
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int row_local = q * 32 + lane;
-        const int row = m0 + row_local;
-        const bool row_ok = row < p.M;
-        const bool have = nkb > 0 && mbar_wait(accum_bar, 0, p.err, kDevTimeoutAccum);
-        tc_fence_after();
-        ArgState as{-INFINITY, kArgNone, 0};
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-        if (p.splits == 1) {
-            for (int c0 = 0; c0 < bn; c0 += 16) {
-                float v[16];
-                if (have) {
-                    tmem_ld_16(taddr + c0, v);
-                } else {
+        float acc[BN];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = 0.f;
-                }
-                if (row_ok && n0 + c0 < p.N) epilogue16(p, row, n0 + c0, v, as);
+        for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+        for (int c = 0; c < nchunks; ++c) {
+            const int b = c & 1;
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(&tfull_bar[b], static_cast<uint32_t>(c >> 1) & 1u, p.err, kDevTimeoutAccum) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t t_big = taddr + static_cast<uint32_t>(b * 2 * BN);
+#pragma unroll
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                float vb[16], vs[16];
+                tmem_ld_16(t_big + c0, vb);
+                tmem_ld_16(t_big + BN + c0, vs);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) acc[c0 + j] += vb[j] + vs[j];
             }
-        } else {
-            const size_t tile_elems = static_cast<size_t>(kBM) * bn;
-            float* ws_mine = p.ws + (static_cast<size_t>(split * p.m_tiles + mt) * p.n_tiles + nt) * tile_elems +
-                             static_cast<size_t>(row_local) * bn;
-            for (int c0 = 0; c0 < bn; c0 += 16) {
-                float v[16];
-                if (have) {
-                    tmem_ld_16(taddr + c0, v);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = 0.f;
-                }
-#pragma unroll
-                for (int j = 0; j < 16; j += 4) st4(ws_mine + c0 + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
-            }
-            __threadfence();
-            epi_bar();
-            const int ticket_id = mt * p.n_tiles + nt;
-            if (threadIdx.x == 64) {
-                const int t = atomicAdd(p.tickets + ticket_id, 1);
-                *last_flag = (t == p.splits - 1) ? 1 : 0;
-            }
-            epi_bar();
-            if (*last_flag) {
-                __threadfence();
-                for (int c0 = 0; c0 < bn; c0 += 16) {
-                    float v[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = 0.f;
-                    for (int s = 0; s < p.splits; ++s) {
-                        const float* src = p.ws + (static_cast<size_t>(s * p.m_tiles + mt) * p.n_tiles + nt) * tile_elems +
-                                           static_cast<size_t>(row_local) * bn + c0;
-#pragma unroll
-                        for (int j = 0; j < 16; j += 4) {
-                            const float4 t4 = __ldcg(reinterpret_cast<const float4*>(src + j));
-                            v[j] += t4.x;
-                            v[j + 1] += t4.y;
-                            v[j + 2] += t4.z;
-                            v[j + 3] += t4.w;
-                        }
-                    }
-                    if (row_ok && n0 + c0 < p.N) epilogue16(p, row, n0 + c0, v, as);
-                }
-                if (threadIdx.x == 64) p.tickets[ticket_id] = 0;
-            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty_bar[b]);
         }
-        if (p.epi.flags & kEpiArgmax) {
-            // splits == 1 here (host-enforced). Partial of this N tile, then the last tile of the
-            // row block reduces the partials in tile order (first maximum wins).
-            if (row_ok) {
+        const uint32_t row_s = tile_s + static_cast<uint32_t>(row_local * bnp * 4);
+#pragma unroll
+        for (int j = 0; j < BN; j += 4)
+            st_shared_f4(row_s + j * 4, acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+    }
+    __syncwarp();
+    if (S > 1) cluster_sync_all(); else __syncthreads();
+    if (warp == 1) {  // accumulators drained: give the tensor memory back early
+        tc_fence_after();
+        tmem_dealloc(tmem_base, p.tmem_cols);
+    }
+
+    // ---- reduction over the cluster's K-slices + fused epilogue, one output row per warp ----
+    const int rows_per = (kBM + S - 1) / S;
+    const int r_lo = split * rows_per;
+    const int r_hi = min(kBM, r_lo + rows_per);
+    const bool argmax = (p.epi.flags & kEpiArgmax) != 0;
+    for (int rl = r_lo + warp; rl < r_hi; rl += kWarps) {
+        const int row = m0 + rl;
+        if (row >= p.M) break;
+        ArgState as{-INFINITY, kArgNone, 0};
+        for (int ch = lane; ch * 4 < BN; ch += 32) {
+            const int col = n0 + ch * 4;
+            if (col >= p.N) break;
+            const uint32_t off = tile_s + static_cast<uint32_t>((rl * bnp + ch * 4) * 4);
+            float4 a4;
+            if (S == 1) {
+                a4 = ld_shared_f4(off);
+            } else {
+                a4 = ld_dsmem_f4(dsmem_addr(off, 0));
+                for (int s = 1; s < S; ++s) {
+                    const float4 t = ld_dsmem_f4(dsmem_addr(off, s));
+                    a4.x += t.x;
+                    a4.y += t.y;
+                    a4.z += t.z;
+                    a4.w += t.w;
+                }
+            }
+            epilogue4(p, row, col, a4, as);
+        }
+        if (argmax) {
+            // first maximum of the row over this tile: larger value, or equal value at a lower index
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, as.best, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, as.idx, o);
+                const int onf = __shfl_xor_sync(0xffffffffu, as.nf, o);
+                if (ov > as.best || (ov == as.best && oi < as.idx)) {
+                    as.best = ov;
+                    as.idx = oi;
+                }
+                as.nf |= onf;
+            }
+            if (lane == 0) {
                 p.arg_val[static_cast<size_t>(row) * p.n_tiles + nt] = as.best;
                 p.arg_idx[static_cast<size_t>(row) * p.n_tiles + nt] =
                     (as.idx & 0x7FFFFFFF) | (as.nf ? static_cast<int>(0x80000000u) : 0);
             }
-            __threadfence();
-            epi_bar();
-            if (threadIdx.x == 64) {
-                const int t = atomicAdd(p.tickets + mt, 1);
-                *last_flag = (t == p.n_tiles - 1) ? 1 : 0;
-            }
-            epi_bar();
-            if (*last_flag) {
-                __threadfence();
-                if (row_ok) {
-                    float best = -INFINITY;
-                    int idx = kArgNone, nf = 0;
-                    for (int t = 0; t < p.n_tiles; ++t) {
-                        const float bv = __ldcg(p.arg_val + static_cast<size_t>(row) * p.n_tiles + t);
-                        const int bi = __ldcg(p.arg_idx + static_cast<size_t>(row) * p.n_tiles + t);
-                        nf |= (bi >> 31) & 1;
-                        const int ii = bi & 0x7FFFFFFF;
-                        if (ii != kArgNone && bv > best) {
-                            best = bv;
-                            idx = ii;
-                        }
-                    }
-                    p.epi.next_ids[row] = (idx == kArgNone) ? -1 : idx;
-                    if (p.epi.nonfinite) p.epi.nonfinite[row] = (nf || idx == kArgNone) ? 1 : 0;
-                }
-                if (threadIdx.x == 64) p.tickets[mt] = 0;
-            }
         }
-        tc_fence_before();
     }
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tmem_base, p.tmem_cols);
+    // No CTA may exit (freeing its shared memory) while a peer still reads its partial tile.
+    __syncwarp();
+    if (S > 1) cluster_sync_all(); else __syncthreads();
+
+    if (argmax) {
+        // splits == 1 (host-enforced). The last N tile of this row block to finish reduces the
+        // per-tile partials in tile order: the first maximum over the whole row.
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const int t = atomicAdd(p.tickets + mt, 1);
+            *last_flag = (t == p.n_tiles - 1) ? 1 : 0;
+        }
+        __syncthreads();
+        if (*last_flag) {
+            __threadfence();
+            for (int rl = threadIdx.x; rl < kBM; rl += kThreads) {
+                const int row = m0 + rl;
+                if (row >= p.M) break;
+                float best = -INFINITY;
+                int idx = kArgNone, nf = 0;
+                for (int t = 0; t < p.n_tiles; ++t) {
+                    const float bv = __ldcg(p.arg_val + static_cast<size_t>(row) * p.n_tiles + t);
+                    const int bi = __ldcg(p.arg_idx + static_cast<size_t>(row) * p.n_tiles + t);
+                    nf |= (bi >> 31) & 1;
+                    const int ii = bi & 0x7FFFFFFF;
+                    if (ii != kArgNone && bv > best) {
+                        best = bv;
+                        idx = ii;
+                    }
+                }
+                p.epi.next_ids[row] = (idx == kArgNone) ? -1 : idx;
+                if (p.epi.nonfinite) p.epi.nonfinite[row] = (nf || idx == kArgNone) ? 1 : 0;
+            }
+            if (threadIdx.x == 0) p.tickets[mt] = 0;
+        }
     }
 }
 
@@ -380,43 +453,74 @@ bool make_map(CUtensorMap* map, const float* base, int K, int rows, int box_rows
     return r == CUDA_SUCCESS;
 }
 
-size_t stage_bytes_for(int bn) { return 2 * static_cast<size_t>(kATileBytes) + 2 * static_cast<size_t>(bn) * kBK * 4; }
+size_t stage_bytes_for(int bn) {
+    return 2 * static_cast<size_t>(kATileBytes) + 2 * static_cast<size_t>(bn) * kBK * 4;
+}
+
+size_t staging_bytes_for(int bn) { return static_cast<size_t>(kBM) * (bn + 4) * 4; }
+
+// Two TMEM buffers, each with a hi*hi and a correction accumulator of BN columns.
+uint32_t tmem_cols_for(int bn) {
+    uint32_t cols = 32;
+    while (cols < static_cast<uint32_t>(4 * bn)) cols <<= 1;
+    return cols;
+}
+
+typedef void (*GemmKernelFn)(GemmKParams);
+
+GemmKernelFn kernel_for(int bn) {
+    switch (bn) {
+        case 16: return gemm_3xtf32_kernel<16>;
+        case 32: return gemm_3xtf32_kernel<32>;
+        case 48: return gemm_3xtf32_kernel<48>;
+        case 64: return gemm_3xtf32_kernel<64>;
+        case 96: return gemm_3xtf32_kernel<96>;
+        case 128: return gemm_3xtf32_kernel<128>;
+        default: return nullptr;
+    }
+}
 
 }  // namespace
 
 bool tensor_map_api_available() { return encode_fn() != nullptr; }
 
+// Picks the N tile and the cluster split of K from a simple time model (ns): per CTA a fixed
+// cost plus, per 32-wide K block, the slower of its HBM weight bytes (hi + lo planes), its
+// activation bytes (from L2) and its 12 tf32 MMAs; waves of CTAs over the SMs.
 GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms) {
     GemmPlan best;
     double best_t = 1e300;
     const int m_tiles = (M + kBM - 1) / kBM;
     const int total_kb = (K + kBK - 1) / kBK;
     const int n16 = (N + 15) / 16 * 16;
-    const int cands[] = {256, 224, 192, 160, 128, 96, 64, 48, 32, 16};
-    for (int bn : cands) {
+    for (int bn : {16, 32, 48, 64, 96, 128}) {
         if (bn > n16 && bn != 16) {
-            // a tile wider than the matrix only wastes work; keep the smallest that covers it
-            bool smaller_covers = false;
-            for (int b2 : cands)
-                if (b2 < bn && b2 >= n16) smaller_covers = true;
-            if (smaller_covers) continue;
+            // wider than the matrix: only waste, unless no narrower instance covers it
+            bool narrower_covers = false;
+            for (int b2 : {16, 32, 48, 64, 96})
+                if (b2 < bn && b2 >= n16) narrower_covers = true;
+            if (narrower_covers) continue;
         }
         const int n_tiles = (N + bn - 1) / bn;
         const int tiles = m_tiles * n_tiles;
-        const int max_split = (flags & (kEpiArgmax)) ? 1 : std::min(16, total_kb);
+        const int max_split = (flags & kEpiArgmax) ? 1 : std::min(kMaxCluster, total_kb);
         for (int s = 1; s <= max_split; ++s) {
             const int kbc = (total_kb + s - 1) / s;
-            const int s_eff = (total_kb + kbc - 1) / kbc;
-            if (s_eff != s) continue;
-            const long long ctas = static_cast<long long>(tiles) * s_eff;
+            if ((total_kb + kbc - 1) / kbc != s) continue;
+            const long long ctas = static_cast<long long>(tiles) * s;
+            const long long active = std::min<long long>(ctas, num_sms);
             const long long waves = (ctas + num_sms - 1) / num_sms;
-            // per-CTA time ~ fixed cost + per K-block cost (MMA ~ bn, A tile ~ constant)
-            double t = static_cast<double>(waves) * (40.0 + kbc * (bn + 96.0));
-            if (s_eff > 1) t += 3.0 * s_eff * bn / 16.0 + 30.0;
+            const double bw_sm = std::min(150.0, 6500.0 / static_cast<double>(active));  // B/ns
+            const double hbm_ns = 256.0 * bn / bw_sm;
+            const double l2_ns = 32768.0 / 120.0;
+            const double mma_ns = 24576.0 * bn / 7400.0;
+            const double per_kb = std::max(hbm_ns, std::max(l2_ns, mma_ns));
+            const double t = static_cast<double>(waves) *
+                             (1500.0 + kbc * per_kb + 2.0 * s * bn + 4.0 * bn);
             if (t < best_t - 1e-9) {
                 best_t = t;
                 best.bn = bn;
-                best.splits = s_eff;
+                best.splits = s;
                 best.kb_per_split = kbc;
                 best.m_tiles = m_tiles;
                 best.n_tiles = n_tiles;
@@ -424,15 +528,17 @@ GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms) {
         }
     }
     const size_t sb = stage_bytes_for(best.bn);
+    const size_t stb = staging_bytes_for(best.bn);
     int stages = static_cast<int>((kSmemLimit - kSmemReserve) / sb);
     stages = std::max(1, std::min(stages, 8));
     stages = std::min(stages, std::max(1, best.kb_per_split));
     best.stages = stages;
-    best.smem_bytes = stages * sb + kSmemReserve;
+    best.smem_bytes = std::max(stages * sb, stb) + kSmemReserve;
+    // promotion chunk: one 32-wide K block per chunk for short K-slices, two for long ones
+    best.chunk_kb = best.kb_per_split > 16 ? 2 : 1;
     // Keep (CTAs resident per SM) x (TMEM columns per CTA) <= 512: pad the shared-memory request
     // so that no more CTAs fit on an SM than its tensor memory can hold at once.
-    uint32_t cols = 32;
-    while (cols < static_cast<uint32_t>(best.bn)) cols <<= 1;
+    const uint32_t cols = tmem_cols_for(best.bn);
     const size_t max_ctas = 512 / cols;
     const size_t sm_bytes = 228 * 1024;
     const size_t min_smem = sm_bytes / (max_ctas + 1) + 1;  // max_ctas + 1 CTAs must not fit
@@ -440,9 +546,7 @@ GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms) {
     return best;
 }
 
-size_t gemm_ws_floats(const GemmPlan& p) {
-    return p.splits > 1 ? static_cast<size_t>(p.splits) * p.m_tiles * p.n_tiles * kBM * p.bn : 0;
-}
+size_t gemm_ws_floats(const GemmPlan&) { return 0; }
 
 size_t gemm_arg_entries(const GemmPlan& p) {
     return static_cast<size_t>(p.m_tiles) * kBM * p.n_tiles;
@@ -458,25 +562,28 @@ int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e
         cudaGetDevice(&dev);
         std::lock_guard<std::mutex> lock(mu);
         if (dev < 64 && !(done_mask & (1ull << dev))) {
-            const cudaError_t e = cudaFuncSetAttribute(
-                gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                static_cast<int>(kSmemLimit));
-            if (e != cudaSuccess) return static_cast<int>(e);
+            for (int bn : {16, 32, 48, 64, 96, 128}) {
+                const cudaError_t e = cudaFuncSetAttribute(
+                    kernel_for(bn), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                    static_cast<int>(kSmemLimit));
+                if (e != cudaSuccess) return static_cast<int>(e);
+            }
             done_mask |= (1ull << dev);
         }
     }
     if (M <= 0 || w.N <= 0 || w.K <= 0 || a.K != w.K) return cudaErrorInvalidValue;
     if (a.rows_alloc < plan.m_tiles * kBM) return cudaErrorInvalidValue;
-    if (plan.bn % 16 || plan.bn < 16 || plan.bn > 256) return cudaErrorInvalidValue;
+    GemmKernelFn kern = kernel_for(plan.bn);
+    if (kern == nullptr || plan.chunk_kb < 1) return cudaErrorInvalidValue;
+    if (plan.splits < 1 || plan.splits > kMaxCluster) return cudaErrorInvalidValue;
+    if (plan.smem_bytes > kSmemLimit) return cudaErrorInvalidValue;
     if ((epi.flags & kEpiArgmax) && plan.splits != 1) return cudaErrorInvalidValue;
-    if (plan.splits > 1 && (scratch.ws == nullptr || scratch.ws_floats < gemm_ws_floats(plan) ||
-                            scratch.n_tickets < plan.m_tiles * plan.n_tiles))
-        return cudaErrorInvalidValue;
     if ((epi.flags & kEpiArgmax) &&
         (scratch.arg_val == nullptr || scratch.arg_entries < gemm_arg_entries(plan) ||
          scratch.n_tickets < plan.m_tiles || epi.next_ids == nullptr))
         return cudaErrorInvalidValue;
-    if ((epi.flags & kEpiKvScatter) && (epi.d_model % 64 != 0 || w.N != 2 * epi.d_model))
+    if ((epi.flags & kEpiKvScatter) &&
+        (epi.head_dim % 4 != 0 || epi.d_model % epi.head_dim != 0 || w.N != 2 * epi.d_model))
         return cudaErrorInvalidValue;
     const int n_rows_alloc = (w.N + 255) / 256 * 256;
 
@@ -496,18 +603,31 @@ int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e
     p.n_tiles = plan.n_tiles;
     p.m_tiles = plan.m_tiles;
     p.total_kb = (w.K + kBK - 1) / kBK;
+    p.chunk_kb = plan.chunk_kb;
     p.idesc = idesc_tf32(kBM, plan.bn);
-    uint32_t cols = 32;
-    while (cols < static_cast<uint32_t>(plan.bn)) cols <<= 1;
-    p.tmem_cols = cols;
+    p.tmem_cols = tmem_cols_for(plan.bn);
     p.epi = epi;
-    p.ws = scratch.ws;
     p.tickets = scratch.tickets;
     p.arg_val = scratch.arg_val;
     p.arg_idx = scratch.arg_idx;
     p.err = err;
-    dim3 grid(plan.n_tiles, plan.m_tiles, plan.splits);
-    gemm_3xtf32_kernel<<<grid, kThreads, plan.smem_bytes, st>>>(p);
+
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(plan.n_tiles, plan.m_tiles, plan.splits);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = plan.smem_bytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (plan.splits > 1) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = plan.splits;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess) return static_cast<int>(e);
     return static_cast<int>(cudaGetLastError());
 }
 

@@ -154,17 +154,13 @@ __global__ void embed_ln_kernel(const float* __restrict__ table, const int* __re
 }
 
 // ---------------------------------------------------------------------------------------------
-// Decode attention. One CTA per (chunk of kAttnChunk cached rows, head, batch row); 4 warps; each
-// half-warp owns one cached row at a time (16 lanes x float4 = the 64-float head slice), so a
-// warp reads 512 contiguous bytes of K (and of V) per step and the CTA 2 KB. Online softmax per
-// half-warp, merged across halves, warps and (through scratch) chunks in a fixed order.
+// Decode attention, templated on the head width DH (32 or 64). One CTA per (chunk of kAttnChunk
+// cached rows, head, batch row), 4 warps. A row of one head is DH floats = LPR lanes x float4, so
+// a warp covers RPW = 32 / LPR rows per load and the CTA 4 * RPW consecutive rows (contiguous
+// bytes in the [slot][head][row][DH] cache). Online softmax per row group of lanes, merged across
+// row groups, warps and (through scratch) chunks in a fixed order.
 constexpr int kAttnWarps = 4;
 constexpr int kAttnUnroll = 4;
-
-struct Partial {
-    float m, l;
-    float4 acc;  // this lane's 4 of the 64 output dims
-};
 
 __device__ __forceinline__ void merge_into(float& m, float& l, float4& acc, float m2, float l2,
                                            float4 acc2) {
@@ -179,8 +175,9 @@ __device__ __forceinline__ void merge_into(float& m, float& l, float4& acc, floa
     m = mm;
 }
 
-__device__ __forceinline__ void write_out(const DecodeAttnArgs& a, int b, int h, int l16, float4 o) {
-    const size_t off = static_cast<size_t>(b) * a.ldo + h * 64 + l16 * 4;
+template <int DH>
+__device__ __forceinline__ void write_out(const DecodeAttnArgs& a, int b, int h, int l, float4 o) {
+    const size_t off = static_cast<size_t>(b) * a.ldo + h * DH + l * 4;
     if (a.out) *reinterpret_cast<float4*>(a.out + off) = o;
     if (a.out_hi) {
         float4 hi, lo;
@@ -193,54 +190,57 @@ __device__ __forceinline__ void write_out(const DecodeAttnArgs& a, int b, int h,
     }
 }
 
+template <int DH>
 __global__ void __launch_bounds__(kAttnWarps * 32) decode_attention_kernel(const __grid_constant__ DecodeAttnArgs a) {
+    constexpr int LPR = DH / 4;        // lanes per cached row
+    constexpr int RPW = 32 / LPR;      // rows per warp per load
+    constexpr int G = kAttnWarps * RPW;  // consecutive rows per CTA per load
+    constexpr unsigned kRowMask = (LPR == 32) ? 0xffffffffu : ((1u << LPR) - 1u);
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int slot = a.slots ? a.slots[b] : b;
     const int len = a.len_by_slot[slot] + a.len_add;
     const int nch = (len + kAttnChunk - 1) / kAttnChunk;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int half = lane >> 4, l16 = lane & 15;
+    const int rsub = lane / LPR, l = lane % LPR;
     if (len <= 0) {
         // No cached rows: the reference's softmax over an empty row leaves nothing; output 0.
-        if (c == 0 && warp == 0 && half == 0) write_out(a, b, h, l16, make_float4(0.f, 0.f, 0.f, 0.f));
+        if (c == 0 && warp == 0 && rsub == 0) write_out<DH>(a, b, h, l, make_float4(0.f, 0.f, 0.f, 0.f));
         return;
     }
     if (c >= nch) return;
-    float* Kh = a.kc + static_cast<long long>(slot) * a.slot_stride + static_cast<long long>(h) * a.cap * 64;
-    float* Vh = a.vc + static_cast<long long>(slot) * a.slot_stride + static_cast<long long>(h) * a.cap * 64;
+    float* Kh = a.kc + static_cast<long long>(slot) * a.slot_stride + static_cast<long long>(h) * a.cap * DH;
+    float* Vh = a.vc + static_cast<long long>(slot) * a.slot_stride + static_cast<long long>(h) * a.cap * DH;
 
     // Fused KV append: the CTA whose chunk holds the new row writes it (KVCache::append).
     if (a.k_new && (len - 1) / kAttnChunk == c) {
         const int t = len - 1;
-        if (threadIdx.x < 16) {
-            const float4 kv = *reinterpret_cast<const float4*>(a.k_new + static_cast<size_t>(b) * a.ldkv + h * 64 + threadIdx.x * 4);
-            *reinterpret_cast<float4*>(Kh + static_cast<size_t>(t) * 64 + threadIdx.x * 4) = kv;
-        } else if (threadIdx.x < 32) {
-            const int i = threadIdx.x - 16;
-            const float4 vv = *reinterpret_cast<const float4*>(a.v_new + static_cast<size_t>(b) * a.ldkv + h * 64 + i * 4);
-            *reinterpret_cast<float4*>(Vh + static_cast<size_t>(t) * 64 + i * 4) = vv;
+        if (threadIdx.x < LPR) {
+            const float4 kv = *reinterpret_cast<const float4*>(a.k_new + static_cast<size_t>(b) * a.ldkv + h * DH + threadIdx.x * 4);
+            *reinterpret_cast<float4*>(Kh + static_cast<size_t>(t) * DH + threadIdx.x * 4) = kv;
+        } else if (threadIdx.x < 2 * LPR) {
+            const int i = threadIdx.x - LPR;
+            const float4 vv = *reinterpret_cast<const float4*>(a.v_new + static_cast<size_t>(b) * a.ldkv + h * DH + i * 4);
+            *reinterpret_cast<float4*>(Vh + static_cast<size_t>(t) * DH + i * 4) = vv;
         }
         __syncthreads();
     }
 
-    const float4 q = *reinterpret_cast<const float4*>(a.q + static_cast<size_t>(b) * a.ldq + h * 64 + l16 * 4);
+    const float4 q = *reinterpret_cast<const float4*>(a.q + static_cast<size_t>(b) * a.ldq + h * DH + l * 4);
     const int r0 = c * kAttnChunk;
     const int r1 = min(len, r0 + kAttnChunk);
-    float m = -INFINITY, l = 0.f;
+    float m = -INFINITY, lsum = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 
-    // Row of (group g, unroll u) for this half-warp: r0 + 8*(g*U + u) + 2*warp + half. The loop
-    // bound is warp-uniform (gb), so both halves run the same iterations and every shuffle has
-    // all 32 lanes present.
-    for (int gb = r0 + 2 * warp; gb < r1; gb += 8 * kAttnUnroll) {
-        const int base = gb + half;
+    // The loop bound (gb) is warp-uniform, so every shuffle has all 32 lanes present.
+    for (int gb = r0 + warp * RPW; gb < r1; gb += G * kAttnUnroll) {
+        const int base = gb + rsub;
         float4 kk[kAttnUnroll], vv[kAttnUnroll];
 #pragma unroll
         for (int u = 0; u < kAttnUnroll; ++u) {
-            const int r = base + 8 * u;
+            const int r = base + G * u;
             if (r < r1) {
-                kk[u] = __ldcs(reinterpret_cast<const float4*>(Kh + static_cast<size_t>(r) * 64 + l16 * 4));
-                vv[u] = __ldcs(reinterpret_cast<const float4*>(Vh + static_cast<size_t>(r) * 64 + l16 * 4));
+                kk[u] = __ldcs(reinterpret_cast<const float4*>(Kh + static_cast<size_t>(r) * DH + l * 4));
+                vv[u] = __ldcs(reinterpret_cast<const float4*>(Vh + static_cast<size_t>(r) * DH + l * 4));
             } else {
                 kk[u] = make_float4(0.f, 0.f, 0.f, 0.f);
                 vv[u] = kk[u];
@@ -253,17 +253,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32) decode_attention_kernel(const
             d = fmaf(q.y, kk[u].y, d);
             d = fmaf(q.z, kk[u].z, d);
             d = fmaf(q.w, kk[u].w, d);
-            d += __shfl_xor_sync(0xffffffffu, d, 8);
-            d += __shfl_xor_sync(0xffffffffu, d, 4);
-            d += __shfl_xor_sync(0xffffffffu, d, 2);
-            d += __shfl_xor_sync(0xffffffffu, d, 1);
-            s[u] = (base + 8 * u < r1) ? d * a.scale : -INFINITY;
+#pragma unroll
+            for (int o = LPR / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+            s[u] = (base + G * u < r1) ? d * a.scale : -INFINITY;
         }
         float mu = m;
 #pragma unroll
         for (int u = 0; u < kAttnUnroll; ++u) mu = fmaxf(mu, s[u]);
         const float corr = (m == -INFINITY) ? 0.f : expf(m - mu);
-        l *= corr;
+        lsum *= corr;
         acc.x *= corr;
         acc.y *= corr;
         acc.z *= corr;
@@ -271,7 +269,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) decode_attention_kernel(const
 #pragma unroll
         for (int u = 0; u < kAttnUnroll; ++u) {
             const float pu = (s[u] == -INFINITY) ? 0.f : expf(s[u] - mu);
-            l += pu;
+            lsum += pu;
             acc.x = fmaf(pu, vv[u].x, acc.x);
             acc.y = fmaf(pu, vv[u].y, acc.y);
             acc.z = fmaf(pu, vv[u].z, acc.z);
@@ -279,66 +277,68 @@ __global__ void __launch_bounds__(kAttnWarps * 32) decode_attention_kernel(const
         }
         m = mu;
     }
-    // merge the two halves of the warp (lane i <-> lane i^16 hold the same output dims)
-    {
-        const float m2 = __shfl_xor_sync(0xffffffffu, m, 16);
-        const float l2 = __shfl_xor_sync(0xffffffffu, l, 16);
+    // merge the warp's row groups (lanes l, l+LPR, l+2LPR, ... hold the same output dims)
+#pragma unroll
+    for (int o = LPR; o < 32; o <<= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        const float l2 = __shfl_xor_sync(0xffffffffu, lsum, o);
         float4 a2;
-        a2.x = __shfl_xor_sync(0xffffffffu, acc.x, 16);
-        a2.y = __shfl_xor_sync(0xffffffffu, acc.y, 16);
-        a2.z = __shfl_xor_sync(0xffffffffu, acc.z, 16);
-        a2.w = __shfl_xor_sync(0xffffffffu, acc.w, 16);
-        merge_into(m, l, acc, m2, l2, a2);
+        a2.x = __shfl_xor_sync(0xffffffffu, acc.x, o);
+        a2.y = __shfl_xor_sync(0xffffffffu, acc.y, o);
+        a2.z = __shfl_xor_sync(0xffffffffu, acc.z, o);
+        a2.w = __shfl_xor_sync(0xffffffffu, acc.w, o);
+        merge_into(m, lsum, acc, m2, l2, a2);
     }
     __shared__ float sm_m[kAttnWarps], sm_l[kAttnWarps];
-    __shared__ float4 sm_acc[kAttnWarps][16];
-    if (half == 0) {
-        sm_acc[warp][l16] = acc;
-        if (l16 == 0) {
+    __shared__ float4 sm_acc[kAttnWarps][LPR];
+    if (rsub == 0) {
+        sm_acc[warp][l] = acc;
+        if (l == 0) {
             sm_m[warp] = m;
-            sm_l[warp] = l;
+            sm_l[warp] = lsum;
         }
     }
     __syncthreads();
-    if (warp != 0 || half != 0) return;
+    if (warp != 0 || rsub != 0) return;
     float M = sm_m[0], L = sm_l[0];
-    float4 A = sm_acc[0][l16];
+    float4 A = sm_acc[0][l];
 #pragma unroll
-    for (int w = 1; w < kAttnWarps; ++w) merge_into(M, L, A, sm_m[w], sm_l[w], sm_acc[w][l16]);
+    for (int w = 1; w < kAttnWarps; ++w) merge_into(M, L, A, sm_m[w], sm_l[w], sm_acc[w][l]);
 
     if (nch == 1) {
         const float inv = 1.0f / L;
-        write_out(a, b, h, l16, make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv));
+        write_out<DH>(a, b, h, l, make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv));
         return;
     }
     // Split-KV: publish this chunk's partial; the last chunk to finish merges them in order.
+    constexpr int kPart = DH + 4;  // m, l, 2 pad, DH accumulators
     const int pair = b * a.H + h;
     const int max_ch = (a.max_len + kAttnChunk - 1) / kAttnChunk;
-    float* part = a.ws + (static_cast<size_t>(pair) * max_ch + c) * kAttnPartial;
-    *reinterpret_cast<float4*>(part + 4 + l16 * 4) = A;
-    if (l16 == 0) {
+    float* part = a.ws + (static_cast<size_t>(pair) * max_ch + c) * kPart;
+    *reinterpret_cast<float4*>(part + 4 + l * 4) = A;
+    if (l == 0) {
         part[0] = M;
         part[1] = L;
     }
     __threadfence();
-    __syncwarp(0x0000ffffu);
+    __syncwarp(kRowMask);
     int last = 0;
-    if (l16 == 0) last = (atomicAdd(a.tickets + pair, 1) == nch - 1) ? 1 : 0;
-    last = __shfl_sync(0x0000ffffu, last, 0);
+    if (l == 0) last = (atomicAdd(a.tickets + pair, 1) == nch - 1) ? 1 : 0;
+    last = __shfl_sync(kRowMask, last, 0);
     if (!last) return;
     __threadfence();
-    const float* p0 = a.ws + static_cast<size_t>(pair) * max_ch * kAttnPartial;
+    const float* p0 = a.ws + static_cast<size_t>(pair) * max_ch * kPart;
     M = __ldcg(p0 + 0);
     L = __ldcg(p0 + 1);
-    A = __ldcg(reinterpret_cast<const float4*>(p0 + 4 + l16 * 4));
+    A = __ldcg(reinterpret_cast<const float4*>(p0 + 4 + l * 4));
     for (int j = 1; j < nch; ++j) {
-        const float* pj = p0 + static_cast<size_t>(j) * kAttnPartial;
+        const float* pj = p0 + static_cast<size_t>(j) * kPart;
         merge_into(M, L, A, __ldcg(pj + 0), __ldcg(pj + 1),
-                   __ldcg(reinterpret_cast<const float4*>(pj + 4 + l16 * 4)));
+                   __ldcg(reinterpret_cast<const float4*>(pj + 4 + l * 4)));
     }
     const float inv = 1.0f / L;
-    write_out(a, b, h, l16, make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv));
-    if (l16 == 0) a.tickets[pair] = 0;
+    write_out<DH>(a, b, h, l, make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv));
+    if (l == 0) a.tickets[pair] = 0;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -347,6 +347,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) decode_attention_kernel(const
 constexpr int kPreQ = 128;
 constexpr int kPreKT = 32;
 
+template <int DH>
 __global__ void __launch_bounds__(kPreQ) prefill_attention_kernel(
     const float* __restrict__ qkv, int D, const int* __restrict__ offsets,
     const int* __restrict__ lens, float* __restrict__ out_hi, float* __restrict__ out_lo,
@@ -359,13 +360,13 @@ __global__ void __launch_bounds__(kPreQ) prefill_attention_kernel(
     const int i = q0 + threadIdx.x;
     const bool active = i < S;
     const int ld = 3 * D;
-    __shared__ __align__(16) float Ks[kPreKT][64];
-    __shared__ __align__(16) float Vs[kPreKT][64];
-    float q[64], acc[64];
+    __shared__ __align__(16) float Ks[kPreKT][DH];
+    __shared__ __align__(16) float Vs[kPreKT][DH];
+    float q[DH], acc[DH];
     if (active) {
-        const float* qr = qkv + static_cast<size_t>(row0 + i) * ld + h * 64;
+        const float* qr = qkv + static_cast<size_t>(row0 + i) * ld + h * DH;
 #pragma unroll
-        for (int j = 0; j < 64; j += 4) {
+        for (int j = 0; j < DH; j += 4) {
             const float4 t = *reinterpret_cast<const float4*>(qr + j);
             q[j] = t.x;
             q[j + 1] = t.y;
@@ -374,16 +375,15 @@ __global__ void __launch_bounds__(kPreQ) prefill_attention_kernel(
         }
     }
 #pragma unroll
-    for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+    for (int j = 0; j < DH; ++j) acc[j] = 0.f;
     float m = -INFINITY, l = 0.f;
     for (int k0 = 0; k0 < S; k0 += kPreKT) {
         __syncthreads();
-        // 32 rows x 64 floats of K and of V = 512 float4 each; 128 threads x 4
-        for (int e = threadIdx.x; e < kPreKT * 16; e += kPreQ) {
-            const int r = e >> 4, c4 = (e & 15) * 4;
+        for (int e = threadIdx.x; e < kPreKT * (DH / 4); e += kPreQ) {
+            const int r = e / (DH / 4), c4 = (e % (DH / 4)) * 4;
             float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
             if (k0 + r < S) {
-                const float* base = qkv + static_cast<size_t>(row0 + k0 + r) * ld + h * 64 + c4;
+                const float* base = qkv + static_cast<size_t>(row0 + k0 + r) * ld + h * DH + c4;
                 kv = *reinterpret_cast<const float4*>(base + D);
                 vv = *reinterpret_cast<const float4*>(base + 2 * D);
             }
@@ -400,7 +400,7 @@ __global__ void __launch_bounds__(kPreQ) prefill_attention_kernel(
             for (int u = 0; u < 16; ++u) {
                 float d = 0.f;
 #pragma unroll
-                for (int j = 0; j < 64; j += 4) {
+                for (int j = 0; j < DH; j += 4) {
                     const float4 kk = *reinterpret_cast<const float4*>(&Ks[kb + u][j]);
                     d = fmaf(q[j], kk.x, d);
                     d = fmaf(q[j + 1], kk.y, d);
@@ -413,13 +413,13 @@ __global__ void __launch_bounds__(kPreQ) prefill_attention_kernel(
             const float corr = (m == -INFINITY) ? 0.f : expf(m - mu);
             l *= corr;
 #pragma unroll
-            for (int j = 0; j < 64; ++j) acc[j] *= corr;
+            for (int j = 0; j < DH; ++j) acc[j] *= corr;
 #pragma unroll
             for (int u = 0; u < 16; ++u) {
                 const float p = (sc[u] == -INFINITY) ? 0.f : expf(sc[u] - mu);
                 l += p;
 #pragma unroll
-                for (int j = 0; j < 64; j += 4) {
+                for (int j = 0; j < DH; j += 4) {
                     const float4 vv = *reinterpret_cast<const float4*>(&Vs[kb + u][j]);
                     acc[j] = fmaf(p, vv.x, acc[j]);
                     acc[j + 1] = fmaf(p, vv.y, acc[j + 1]);
@@ -432,9 +432,9 @@ __global__ void __launch_bounds__(kPreQ) prefill_attention_kernel(
     }
     if (!active) return;
     const float inv = 1.0f / l;
-    const size_t o = static_cast<size_t>(row0 + i) * D + h * 64;
+    const size_t o = static_cast<size_t>(row0 + i) * D + h * DH;
 #pragma unroll
-    for (int j = 0; j < 64; j += 4) {
+    for (int j = 0; j < DH; j += 4) {
         float4 hi, lo;
         split_tf32(acc[j] * inv, hi.x, lo.x);
         split_tf32(acc[j + 1] * inv, hi.y, lo.y);
@@ -506,9 +506,11 @@ void launch_embed_ln(const float* table, const int* ids, const float* pe, int pe
                      pos_direct, x, g, b, out_hi, out_lo, rows, D, vocab, err);
 }
 
-size_t decode_attn_ws_floats(int B, int H, int max_len) {
+bool attention_head_dim_supported(int dh) { return dh == 32 || dh == 64; }
+
+size_t decode_attn_ws_floats(int B, int H, int max_len, int head_dim) {
     const int max_ch = (std::max(max_len, 1) + kAttnChunk - 1) / kAttnChunk;
-    return static_cast<size_t>(B) * H * max_ch * kAttnPartial;
+    return static_cast<size_t>(B) * H * max_ch * (head_dim + 4);
 }
 
 void launch_decode_attention(const DecodeAttnArgs& a, int* err, cudaStream_t st) {
@@ -516,7 +518,10 @@ void launch_decode_attention(const DecodeAttnArgs& a, int* err, cudaStream_t st)
     if (a.B <= 0) return;
     const int max_ch = (std::max(a.max_len, 1) + kAttnChunk - 1) / kAttnChunk;
     dim3 grid(max_ch, a.H, a.B);
-    decode_attention_kernel<<<grid, kAttnWarps * 32, 0, st>>>(a);
+    if (a.head_dim == 32)
+        decode_attention_kernel<32><<<grid, kAttnWarps * 32, 0, st>>>(a);
+    else
+        decode_attention_kernel<64><<<grid, kAttnWarps * 32, 0, st>>>(a);
 }
 
 void launch_prefill_attention(const float* qkv, int D, int H, const int* offsets, const int* lens,
@@ -524,7 +529,10 @@ void launch_prefill_attention(const float* qkv, int D, int H, const int* offsets
                               cudaStream_t st) {
     if (nseq <= 0 || max_len <= 0) return;
     dim3 grid((max_len + kPreQ - 1) / kPreQ, H, nseq);
-    prefill_attention_kernel<<<grid, kPreQ, 0, st>>>(qkv, D, offsets, lens, out_hi, out_lo, scale);
+    if (D / H == 32)
+        prefill_attention_kernel<32><<<grid, kPreQ, 0, st>>>(qkv, D, offsets, lens, out_hi, out_lo, scale);
+    else
+        prefill_attention_kernel<64><<<grid, kPreQ, 0, st>>>(qkv, D, offsets, lens, out_hi, out_lo, scale);
 }
 
 void launch_advance(const int* next, int* ids, const int* slots, int* len_by_slot, int B,

@@ -40,7 +40,7 @@ struct GemmEpilogue {
     float* vc = nullptr;
     long long slot_stride = 0;  // floats between slots
     int cap = 0;                // rows per (slot, head)
-    int heads = 0;
+    int head_dim = 64;
     int d_model = 0;
     const int* row_slot = nullptr;
     const int* row_pos = nullptr;
@@ -65,6 +65,7 @@ struct GemmPlan {
     int splits = 1;
     int stages = 3;
     int kb_per_split = 0;
+    int chunk_kb = 1;  // K blocks accumulated in TMEM before promotion to fp32 registers
     int m_tiles = 1, n_tiles = 1;
     size_t smem_bytes = 0;
 };
@@ -111,12 +112,12 @@ void launch_embed_ln(const float* table, const int* ids, const float* pe, int pe
 // ------------------------------------------------------------------------------------------
 // Attention
 struct DecodeAttnArgs {
-    const float* q = nullptr;  // row b at q + b*ldq; head h at + h*64
+    const float* q = nullptr;  // row b at q + b*ldq; head h at + h*head_dim
     int ldq = 0;
     const float* k_new = nullptr;  // self-attention append source (null: no append)
     const float* v_new = nullptr;
     int ldkv = 0;
-    float* kc = nullptr;  // this layer's cache: [slot][H][cap][64]
+    float* kc = nullptr;  // this layer's cache: [slot][H][cap][head_dim]
     float* vc = nullptr;
     long long slot_stride = 0;
     int cap = 0;
@@ -128,14 +129,16 @@ struct DecodeAttnArgs {
     float* out_lo = nullptr;
     int ldo = 0;
     int B = 0, H = 0;
+    int head_dim = 64;  // 32 or 64
     int max_len = 0;  // upper bound of len over the batch (sizes the grid)
     float scale = 0.f;
     float* ws = nullptr;  // split-KV partials
     int* tickets = nullptr;
 };
 constexpr int kAttnChunk = 256;  // cached rows per CTA
-constexpr int kAttnPartial = 68; // floats per (b, h, chunk) partial: m, l, 64 acc, 2 pad
-size_t decode_attn_ws_floats(int B, int H, int max_len);
+bool attention_head_dim_supported(int head_dim);
+// split-KV partials: per (b, h, chunk) m, l, 2 pad, head_dim accumulators
+size_t decode_attn_ws_floats(int B, int H, int max_len, int head_dim);
 void launch_decode_attention(const DecodeAttnArgs& a, int* err, cudaStream_t st);
 
 // Encoder self-attention over ragged sequences: qkv [rows, 3D]; sequence s holds rows

@@ -154,13 +154,15 @@ ADAI_B200_API int adai_b200_sgemm_prepared(adai_b200_ctx* ctx, int m, const floa
 /* ---- op level: single-token attention over a KV cache with the append fused in
  * (MultiHeadAttention::forward_with_cache, src/MultiHeadAttention.cpp:278-395, per-head math
  * :336-367; KVCache::append, src/KVCache.hpp:99-128) ----
- * B sequences, H heads of width 64. Cache layout [B][H][capacity][64] (K and V), device
- * pointers. lens[b] rows are cached for sequence b; when k_new/v_new [B, H*64] are non-NULL they
- * are appended at row lens[b] first and attention runs over lens[b] + 1 rows (lens is not
- * updated). q [B, H*64]; out [B, H*64]. Asynchronous on the context's stream. */
-ADAI_B200_API int adai_b200_decode_attention(adai_b200_ctx* ctx, int B, int H, int capacity, const float* q,
-                               const float* k_new, const float* v_new, float* k_cache,
-                               float* v_cache, const int* lens, int max_len, float* out);
+ * B sequences, H heads of width head_dim (32 or 64), D = H * head_dim. Cache layout
+ * [B][H][capacity][head_dim] (K and V). All pointers are device pointers. lens[b] rows are cached
+ * for sequence b (max_len >= every lens[b]); when k_new/v_new [B, D] are non-NULL they are
+ * appended at row lens[b] first and attention runs over lens[b] + 1 rows (lens is not updated).
+ * q [B, D]; out [B, D]. Asynchronous on the context's stream. */
+ADAI_B200_API int adai_b200_decode_attention(adai_b200_ctx* ctx, int B, int H, int head_dim,
+                                             int capacity, const float* q, const float* k_new,
+                                             const float* v_new, float* k_cache, float* v_cache,
+                                             const int* lens, int max_len, float* out);
 
 /* ---- op level: LayerNorm (LayerNorm::forward, src/LayerNorm.cpp:56-109; the reference GPU
  * kernel matrix_layer_norm_fwd_gpu, src/gpu/MatrixGPU.hpp:140) ----
