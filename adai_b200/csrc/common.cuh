@@ -87,6 +87,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     }
 }
 
+// Bounded wait used to drain this CTA's own asynchronous work (copies landing in its shared
+// memory, MMAs still running on its tensor memory) before it frees those resources or exits. It
+// ignores the error word, so an aborted CTA still lets its in-flight operations finish; it gives
+// up (recording `code`) only after its own deadline.
+constexpr unsigned long long kDrainTimeoutNs = 1000000000ull;  // 1 s
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, int* err, int code) {
+    const uint32_t addr = smem_u32(bar);
+    if (mbar_try_wait(addr, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    while (true) {
+        for (int i = 0; i < 256; ++i)
+            if (mbar_try_wait(addr, parity)) return true;
+        if (globaltimer_ns() - t0 > kDrainTimeoutNs) {
+            record_error(err, code);
+            return false;
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------------------------
 // Thread-block clusters: rank, barrier, and loads from a peer CTA's shared memory (DSMEM).
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -99,6 +118,42 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
                  "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Split form of the cluster barrier: arrive early, wait later (both by every thread, in order).
+__device__ __forceinline__ void cluster_arrive_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_all() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Make this thread's generic-proxy shared-memory writes visible to the async proxy (bulk copies).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16) from this CTA's shared memory to another CTA's shared
+// memory in the cluster; completion is signalled as transaction bytes on the destination CTA's
+// mbarrier. dst and bar are shared::cluster addresses.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta,
+                                                  uint32_t bytes, uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(dst_cluster), "r"(src_cta), "r"(bytes), "r"(bar_cluster)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until the source reads of every committed bulk copy of this thread are done.
+__device__ __forceinline__ void bulk_wait_reads() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Programmatic dependent launch: wait for the preceding kernel's completion (and its memory) /
+// allow the next kernel in the stream to start launching. No-ops without the launch attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // shared::cluster address of the same shared-memory location in CTA `rank` of the cluster.
@@ -179,20 +234,50 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
         : "memory");
 }
 
+// tcgen05.ld writes its destination registers asynchronously: they hold the data only after
+// tcgen05.wait::ld. The load(s) and the wait are therefore one asm statement, so the compiler
+// never sees the outputs (nor reuses their registers) before the wait has completed.
+//
 // 32 lanes x 16 columns of 32-bit accumulator: thread i of the warp gets row (lane base + i),
 // columns [col, col+16).
 __device__ __forceinline__ void tmem_ld_16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-        "%14,%15}, [%16];"
+        "%14,%15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
           "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
           "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        : "r"(taddr)
+        : "memory");
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Two 32x32b.x16 loads (e.g. the hi*hi and the correction accumulators of the same columns) in
+// flight together, one wait.
+__device__ __forceinline__ void tmem_ld_16x2(uint32_t taddr_a, uint32_t taddr_b, float (&va)[16],
+                                             float (&vb)[16]) {
+    uint32_t a[16], b[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,"
+        "%28,%29,%30,%31}, [%33];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]),
+          "=r"(a[7]), "=r"(a[8]), "=r"(a[9]), "=r"(a[10]), "=r"(a[11]), "=r"(a[12]), "=r"(a[13]),
+          "=r"(a[14]), "=r"(a[15]), "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]),
+          "=r"(b[5]), "=r"(b[6]), "=r"(b[7]), "=r"(b[8]), "=r"(b[9]), "=r"(b[10]), "=r"(b[11]),
+          "=r"(b[12]), "=r"(b[13]), "=r"(b[14]), "=r"(b[15])
+        : "r"(taddr_a), "r"(taddr_b)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        va[i] = __uint_as_float(a[i]);
+        vb[i] = __uint_as_float(b[i]);
+    }
 }
 
 // Shared-memory matrix descriptor for a K-major operand stored in the canonical 128-byte

@@ -681,6 +681,8 @@ __global__ void record_and_advance_kernel(const int* __restrict__ next, int* __r
                                           int* __restrict__ hist, int hist_ld,
                                           const int* __restrict__ nonfinite, int* __restrict__ nf_any,
                                           int B, int feed_back) {
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     const int slot = slots[b];
@@ -711,10 +713,15 @@ cudaGraphExec_t get_graph(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) 
     cudaGraph_t g;
     cuda_ok(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
     try {
+        // The step's kernels overlap their prologues with the previous kernel's tail (PDL edges
+        // in the graph); each waits for its predecessor before touching data.
+        ScopedPdl pdl(true);
         record_step(c, kv, B, flags);
-        record_and_advance_kernel<<<(B + 127) / 128, 128, 0, c->stream>>>(
-            c->sb.next, c->sb.ids, c->sb.slots, kv->d_self_len, kv->d_hist, kv->self_cap,
-            c->sb.nonfinite, c->sb.nonfinite_any, B, (flags & kStepAdvanceIds) ? 1 : 0);
+        cuda_ok(launch_kernel(record_and_advance_kernel, dim3((B + 127) / 128), dim3(128), 0,
+                              c->stream, c->sb.next, c->sb.ids, c->sb.slots, kv->d_self_len,
+                              kv->d_hist, kv->self_cap, c->sb.nonfinite, c->sb.nonfinite_any, B,
+                              (flags & kStepAdvanceIds) ? 1 : 0),
+                "advance launch");
     } catch (...) {
         cudaGraph_t dummy;
         cudaStreamEndCapture(c->stream, &dummy);

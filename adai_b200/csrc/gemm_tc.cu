@@ -5,27 +5,33 @@
 // cross-attention, FFN, LM head) and the encoder prefill.
 //
 // Precision: 3xTF32. Each fp32 operand x is split into hi = tf32(x) and lo = tf32(x - hi)
-// (round to nearest); the product is accumulated in fp32 in TMEM as
-//     A*W ~= A_lo*W_hi + A_hi*W_lo + A_hi*W_hi,
-// the published error-corrected TF32 scheme (Ootomo & Yokota, 2022), which keeps the result
-// within a few fp32 ulps of an fp32 GEMM. The weights are split once at upload (stored W^T,
-// K-major, hi and lo planes); activations arrive already split by the kernel that produced them.
+// (round to nearest); the product is accumulated as
+//     A*W ~= A_hi*W_hi + (A_lo*W_hi + A_hi*W_lo),
+// the published error-corrected TF32 scheme (Ootomo & Yokota, 2022). The weights are split once
+// at upload (stored W^T, K-major, hi and lo planes); activations arrive already split by the
+// kernel that produced them. The tensor core's accumulation does not round to nearest, so a long
+// K sum kept in one TMEM accumulator drifts toward zero; here the accumulator is promoted to
+// fp32 registers chunk by chunk (double-buffered TMEM, hi*hi and correction terms in separate
+// accumulators), which keeps the error at or below an fp32 FMA chain.
 //
 // One CTA computes one 128 x BN output tile over one K-slice:
 //   warp 0    TMA producer: 4 boxes per stage (A_hi, A_lo 128x32; W_hi, W_lo BNx32), 128B swizzle
 //   warp 1    TMEM allocator + single-thread tcgen05.mma issuer (3 MMAs per K=8 step)
-//   warps 2-5 drain the TMEM accumulator (tcgen05.ld, 32 rows x 16 columns per warp) into a
-//             padded shared-memory tile.
-// Split-K: the S K-slices of a tile are the S CTAs of one thread-block cluster. After a cluster
-// barrier every CTA reduces its 128/S rows of the tile by reading the S partial tiles over
-// distributed shared memory in rank order 0..S-1 (deterministic, no global scratch), then all six
-// warps run the fused epilogue one row per warp, so every store is a coalesced float4 run:
+//   warps 2-5 promote finished TMEM chunks into fp32 registers (one output row per thread)
+// Split-K: the S K-slices of a tile are the S CTAs of one thread-block cluster. Each CTA stages
+// its partial tile in its own shared memory and ships the rows it does not own to their owners
+// with one bulk copy per owner (cp.async.bulk shared::cta -> shared::cluster, completing on the
+// owner's mbarrier); every CTA then sums its 128/S rows over the S slots in rank order 0..S-1
+// (deterministic) and runs the fused epilogue with coalesced float4 stores:
 // bias / GELU / residual / fp32 store / tf32 split of the output / KV-cache scatter /
-// first-maximum argmax partials (the LM head). No TMA multicast anywhere.
+// first-maximum argmax partials (the LM head). The epilogue is a template parameter so each
+// instantiation carries only its own code. No TMA multicast anywhere.
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -41,13 +47,21 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kATileBytes = kBM * kBK * 4;  // 16 KB
 constexpr size_t kSmemLimit = 227 * 1024;
 constexpr size_t kSmemReserve = 1024 /*alignment slack*/ + 256 /*barriers*/;
+constexpr int kMaxCluster = 16;  // 8 is portable; 16 is used only where the device can place it
 
-constexpr int kMaxCluster = 8;
+// The epilogue flag sets the decode step and the op-level entry points use.
+constexpr int kEpiSetStore = kEpiStore;
+constexpr int kEpiSetResid = kEpiStore | kEpiResid;
+constexpr int kEpiSetFfnUp = kEpiBias | kEpiGelu | kEpiSplit;
+constexpr int kEpiSetFfnDown = kEpiBias | kEpiResid | kEpiStore;
+constexpr int kEpiSetHead = kEpiBias | kEpiArgmax;
+constexpr int kEpiSetHeadLogits = kEpiBias | kEpiArgmax | kEpiStore;
+constexpr int kEpiSetScatter = kEpiKvScatter;
 
 struct __align__(64) GemmKParams {
     CUtensorMap a_hi, a_lo, b_hi, b_lo;
     int M, N, K;
-    int bn, stages, kb_per_split, splits, n_tiles, m_tiles, total_kb, chunk_kb;
+    int stages, kb_per_split, splits, n_tiles, m_tiles, total_kb, chunk_kb, rows_per;
     uint32_t idesc, tmem_cols;
     GemmEpilogue epi;
     int* tickets;
@@ -70,8 +84,7 @@ __device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
     float4 v;
     asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
                  : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(addr)
-                 : "memory");
+                 : "r"(addr));
     return v;
 }
 
@@ -82,22 +95,30 @@ __device__ __forceinline__ void st_shared_f4(uint32_t addr, float a, float b, fl
 }
 
 // Epilogue on 4 consecutive output columns [col, col+4) of one row (col % 4 == 0, col < N).
+template <int EPI>
 __device__ __forceinline__ void epilogue4(const GemmKParams& p, int row, int col, float4 acc,
                                           ArgState& as) {
     const GemmEpilogue& e = p.epi;
-    const int N = p.N;
-    const int nv = min(4, N - col);
+    const int nv = min(4, p.N - col);
     float v[4] = {acc.x, acc.y, acc.z, acc.w};
-    if (e.flags & kEpiBias) {
+    if constexpr ((EPI & kEpiBias) != 0) {
+        if (nv == 4) {
+            const float4 b4 = __ldg(reinterpret_cast<const float4*>(e.bias + col));
+            v[0] += b4.x;
+            v[1] += b4.y;
+            v[2] += b4.z;
+            v[3] += b4.w;
+        } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-            if (j < nv) v[j] += __ldg(e.bias + col + j);
+            for (int j = 0; j < 4; ++j)
+                if (j < nv) v[j] += __ldg(e.bias + col + j);
+        }
     }
-    if (e.flags & kEpiGelu) {
+    if constexpr ((EPI & kEpiGelu) != 0) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) v[j] = gelu_tanh(v[j]);
     }
-    if (e.flags & kEpiResid) {
+    if constexpr ((EPI & kEpiResid) != 0) {
         const float* r = e.resid + static_cast<size_t>(row) * e.ldr + col;
         if (nv == 4 && (e.ldr & 3) == 0) {
             const float4 rv = *reinterpret_cast<const float4*>(r);
@@ -111,7 +132,7 @@ __device__ __forceinline__ void epilogue4(const GemmKParams& p, int row, int col
                 if (j < nv) v[j] = r[j] + v[j];
         }
     }
-    if (e.flags & kEpiArgmax) {
+    if constexpr ((EPI & kEpiArgmax) != 0) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             if (j < nv) {
@@ -124,7 +145,7 @@ __device__ __forceinline__ void epilogue4(const GemmKParams& p, int row, int col
             }
         }
     }
-    if (e.flags & kEpiStore) {
+    if constexpr ((EPI & kEpiStore) != 0) {
         float* o = e.out + static_cast<size_t>(row) * e.ldo + col;
         if (nv == 4 && (e.ldo & 3) == 0) {
             st4(o, make_float4(v[0], v[1], v[2], v[3]));
@@ -134,7 +155,7 @@ __device__ __forceinline__ void epilogue4(const GemmKParams& p, int row, int col
                 if (j < nv) o[j] = v[j];
         }
     }
-    if (e.flags & kEpiSplit) {
+    if constexpr ((EPI & kEpiSplit) != 0) {
         float h[4], l[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) split_tf32(v[j], h[j], l[j]);
@@ -152,7 +173,7 @@ __device__ __forceinline__ void epilogue4(const GemmKParams& p, int row, int col
                 }
         }
     }
-    if (e.flags & kEpiKvScatter) {
+    if constexpr ((EPI & kEpiKvScatter) != 0) {
         // columns [0, D) are K, [D, 2D) are V; a 4-column group never straddles a head.
         const int kv = col / e.d_model;
         const int cc = col - kv * e.d_model;
@@ -164,40 +185,41 @@ __device__ __forceinline__ void epilogue4(const GemmKParams& p, int row, int col
     }
 }
 
-// The accumulator is promoted to fp32 registers chunk by chunk: the tensor core accumulates a
-// chunk of K (chunk_kb blocks of 32) into one of two TMEM buffers while the epilogue warps add
-// the other buffer's finished chunk into registers with round-to-nearest fp32 adds. Within a
-// buffer the dominant hi*hi products and the small correction terms (lo*hi + hi*lo) have
-// separate accumulators, so the small terms never round against the large running sum.
-// Together this keeps the rounding of long K sums at the level of an fp32 FMA chain, where one
-// TMEM accumulator over the whole K would drift (the tensor core's accumulation does not round
-// to nearest).
-template <int BN>
+template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_constant__ GemmKParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    const int stages = p.stages;
-    const int S = p.splits;
+    constexpr bool kArgmax = (EPI & kEpiArgmax) != 0;
     constexpr int b_tile_bytes = BN * kBK * 4;
     constexpr int stage_bytes = 2 * kATileBytes + 2 * b_tile_bytes;
-    constexpr int bnp = BN + 4;  // padded row of the staging tile (floats): conflict-free float4 rows
+    constexpr int kChunks = BN / 4;  // float4 columns per output row
+    const int stages = p.stages;
+    const int S = p.splits;
+    const int rows_per = p.rows_per;  // 128 / S: output rows each cluster rank finishes
     const size_t pipe_bytes = static_cast<size_t>(stages) * stage_bytes;
-    constexpr size_t stage_tile_bytes = static_cast<size_t>(kBM) * bnp * 4;
-    const size_t bar_off = ((pipe_bytes > stage_tile_bytes ? pipe_bytes : stage_tile_bytes) + 7) & ~size_t(7);
-    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + bar_off);
+    // Partial tile of this CTA, [128 rows][BN] fp32 with float4 columns XOR-swizzled by (row & 7)
+    // (conflict-free row writes and column reads); it reuses the pipeline buffers once the
+    // mainloop is over. With S > 1 a dedicated receive buffer holds the peers' partials of this
+    // rank's rows: [S slots][rows_per][BN], same swizzle (rows_per is a multiple of 8).
+    uint8_t* stage_out = smem;
+    uint8_t* recv = smem + pipe_bytes;
+    const size_t recv_bytes = (S > 1) ? static_cast<size_t>(S) * rows_per * BN * 4 : 0;
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(recv + recv_bytes);
     uint64_t* empty_bar = full_bar + stages;
     uint64_t* tfull_bar = empty_bar + stages;  // [2] chunk accumulated in TMEM buffer b
     uint64_t* tempty_bar = tfull_bar + 2;      // [2] TMEM buffer b drained by the epilogue
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+    uint64_t* recv_bar = tempty_bar + 2;       // peers' partials have landed in `recv`
+    uint64_t* done_bar = recv_bar + 1;         // every MMA this CTA issued has completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
     int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int nt = blockIdx.x, mt = blockIdx.y;
-    const int split = (S > 1) ? static_cast<int>(cluster_ctarank()) : 0;
+    const int rank = (S > 1) ? static_cast<int>(cluster_ctarank()) : 0;
     const int m0 = mt * kBM, n0 = nt * BN;
-    const int kb0 = split * p.kb_per_split;
+    const int kb0 = rank * p.kb_per_split;
     const int kb1 = min(p.total_kb, kb0 + p.kb_per_split);
     const int nkb = max(0, kb1 - kb0);
     const int CK = p.chunk_kb;
@@ -216,6 +238,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
             mbar_init(&tfull_bar[b], 1);
             mbar_init(&tempty_bar[b], 4);  // one arrival per epilogue warp
         }
+        mbar_init(recv_bar, 1);
+        mbar_init(done_bar, 1);
+        if (S > 1)  // the phase completes once every peer's rows have arrived
+            mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>((S - 1) * rows_per * BN * 4));
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -224,13 +250,35 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
     }
     __syncthreads();
     tc_fence_after();
+    // This CTA's barriers are initialised: peers may send to it once they pass the wait below.
+    if (S > 1) cluster_arrive_all();
+    // The next kernel in the stream may begin its own prologue (it waits before touching data).
+    pdl_trigger();
     const uint32_t tmem_base = *tmem_slot;
-    const uint32_t tile_s = smem_u32(smem);  // staging tile (reuses the pipeline buffers)
+    const uint32_t stage_s = smem_u32(stage_out);
+    const uint32_t recv_s = smem_u32(recv);
 
     if (warp == 0) {
         if (lane == 0 && nkb > 0) {
-            int issued = 0;
-            for (int i = 0; i < nkb; ++i) {
+            // Weights are constant: the first stages' weight boxes are requested before waiting
+            // for the preceding kernel; the activation boxes only after it.
+            const int first = min(stages, nkb);
+            for (int i = 0; i < first; ++i) {
+                uint8_t* st = smem + static_cast<size_t>(i) * stage_bytes;
+                mbar_arrive_expect_tx(&full_bar[i], static_cast<uint32_t>(stage_bytes));
+                const int kx = (kb0 + i) * kBK;
+                tma_load_2d(st + 2 * kATileBytes, &p.b_hi, &full_bar[i], kx, n0);
+                tma_load_2d(st + 2 * kATileBytes + b_tile_bytes, &p.b_lo, &full_bar[i], kx, n0);
+            }
+            pdl_wait();
+            for (int i = 0; i < first; ++i) {
+                uint8_t* st = smem + static_cast<size_t>(i) * stage_bytes;
+                const int kx = (kb0 + i) * kBK;
+                tma_load_2d(st, &p.a_hi, &full_bar[i], kx, m0);
+                tma_load_2d(st + kATileBytes, &p.a_lo, &full_bar[i], kx, m0);
+            }
+            int issued = first;
+            for (int i = first; i < nkb; ++i) {
                 const int s = i % stages;
                 const uint32_t round = static_cast<uint32_t>(i / stages);
                 if (!mbar_wait(&empty_bar[s], (round & 1u) ^ 1u, p.err, kDevTimeoutSmemEmpty)) break;
@@ -243,11 +291,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
                 tma_load_2d(st + 2 * kATileBytes + b_tile_bytes, &p.b_lo, &full_bar[s], kx, n0);
                 ++issued;
             }
-            // No copy may still be landing in shared memory when the CTA moves on: wait (bounded)
-            // for the last load of every stage. Immediate when the MMA warp consumed them all.
+            // No copy may still be landing in shared memory when the CTA moves on, also after an
+            // abort: drain the last load of every stage (immediate when the MMAs consumed them).
             for (int i = max(0, issued - stages); i < issued; ++i)
-                mbar_wait(&full_bar[i % stages], static_cast<uint32_t>(i / stages) & 1u, p.err,
-                          kDevTimeoutTmaFull);
+                mbar_wait_drain(&full_bar[i % stages], static_cast<uint32_t>(i / stages) & 1u,
+                                p.err, kDevTimeoutTmaFull);
         }
     } else if (warp == 1) {
         if (lane == 0 && nkb > 0) {
@@ -290,9 +338,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
                 }
                 if (ok) mma_commit(&tfull_bar[b]);
             }
+            // Tensor memory is released after the CTA barrier below: every MMA issued here must
+            // have completed by then, also when the loop was aborted.
+            mma_commit(done_bar);
+            mbar_wait_drain(done_bar, 0, p.err, kDevTimeoutAccum);
         }
     } else {
-        // ---- warps 2..5: promote each finished chunk into fp32 registers ----
+        // ---- warps 2..5: promote each finished chunk into fp32 registers, one row per thread ----
+        pdl_wait();  // the epilogue reads and writes data of earlier kernels
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int row_local = q * 32 + lane;
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
@@ -302,7 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
         for (int c = 0; c < nchunks; ++c) {
             const int b = c & 1;
             int ok = 1;
-            if (lane == 0) ok = mbar_wait(&tfull_bar[b], static_cast<uint32_t>(c >> 1) & 1u, p.err, kDevTimeoutAccum) ? 1 : 0;
+            if (lane == 0)
+                ok = mbar_wait(&tfull_bar[b], static_cast<uint32_t>(c >> 1) & 1u, p.err, kDevTimeoutAccum) ? 1 : 0;
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
@@ -310,8 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
 #pragma unroll
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 float vb[16], vs[16];
-                tmem_ld_16(t_big + c0, vb);
-                tmem_ld_16(t_big + BN + c0, vs);
+                tmem_ld_16x2(t_big + c0, t_big + BN + c0, vb, vs);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) acc[c0 + j] += vb[j] + vs[j];
             }
@@ -319,48 +372,87 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty_bar[b]);
         }
-        const uint32_t row_s = tile_s + static_cast<uint32_t>(row_local * bnp * 4);
+        // This row of the partial tile -> the staging tile (the pipeline buffers are free: every
+        // MMA that read them has completed).
+        const uint32_t row_s = stage_s + static_cast<uint32_t>(row_local * BN * 4);
+        const int sw = row_local & 7;
 #pragma unroll
-        for (int j = 0; j < BN; j += 4)
-            st_shared_f4(row_s + j * 4, acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        for (int ch = 0; ch < kChunks; ++ch)
+            st_shared_f4(row_s + static_cast<uint32_t>((ch ^ sw) * 16), acc[4 * ch], acc[4 * ch + 1],
+                         acc[4 * ch + 2], acc[4 * ch + 3]);
+        if (S > 1) fence_proxy_async_smem();  // the rows leave by bulk copy (async proxy)
     }
     __syncwarp();
-    if (S > 1) cluster_sync_all(); else __syncthreads();
+    __syncthreads();  // staging tile complete
     if (warp == 1) {  // accumulators drained: give the tensor memory back early
         tc_fence_after();
         tmem_dealloc(tmem_base, p.tmem_cols);
     }
+    if (S > 1) {
+        cluster_wait_all();  // every peer's receive barrier is initialised
+        if (threadIdx.x == 0) {
+            // rows [o*rows_per, (o+1)*rows_per) of this partial go to rank o, slot `rank`
+            const uint32_t bytes = static_cast<uint32_t>(rows_per * BN * 4);
+            for (int o = 0; o < S; ++o) {
+                if (o == rank) continue;
+                const uint32_t src = stage_s + static_cast<uint32_t>(o) * bytes;
+                const uint32_t dst = dsmem_addr(recv_s + static_cast<uint32_t>(rank) * bytes, o);
+                const uint32_t bar = dsmem_addr(smem_u32(recv_bar), o);
+                bulk_copy_to_peer(dst, src, bytes, bar);
+            }
+            bulk_commit();
+        }
+        // Peers' rows of this rank are here. After an abort elsewhere still drain: no copy may
+        // land in this CTA's memory after it exits.
+        if (!mbar_wait(recv_bar, 0, p.err, kDevTimeoutAccum))
+            mbar_wait_drain(recv_bar, 0, p.err, kDevTimeoutAccum);
+    }
 
-    // ---- reduction over the cluster's K-slices + fused epilogue, one output row per warp ----
-    const int rows_per = (kBM + S - 1) / S;
-    const int r_lo = split * rows_per;
-    const int r_hi = min(kBM, r_lo + rows_per);
-    const bool argmax = (p.epi.flags & kEpiArgmax) != 0;
-    for (int rl = r_lo + warp; rl < r_hi; rl += kWarps) {
-        const int row = m0 + rl;
-        if (row >= p.M) break;
-        ArgState as{-INFINITY, kArgNone, 0};
-        for (int ch = lane; ch * 4 < BN; ch += 32) {
+    // ---- sum the S slots in rank order and run the fused epilogue on this rank's rows ----
+    const int r_lo = rank * rows_per;
+    const int r_cnt = max(0, min(kBM, r_lo + rows_per) - r_lo);
+    auto slot_addr = [&](int s, int r, int ch) -> uint32_t {
+        const uint32_t phys = static_cast<uint32_t>((ch ^ (r & 7)) * 16);
+        return (s == rank) ? stage_s + static_cast<uint32_t>((r_lo + r) * BN * 4) + phys
+                           : recv_s + static_cast<uint32_t>((s * rows_per + r) * BN * 4) + phys;
+    };
+    if constexpr (!kArgmax) {
+        // flattened (row, float4 column) items; consecutive threads write consecutive columns
+        for (int it = threadIdx.x; it < r_cnt * kChunks; it += kThreads) {
+            const int r = it / kChunks, ch = it - r * kChunks;
+            const int row = m0 + r_lo + r;
             const int col = n0 + ch * 4;
-            if (col >= p.N) break;
-            const uint32_t off = tile_s + static_cast<uint32_t>((rl * bnp + ch * 4) * 4);
-            float4 a4;
-            if (S == 1) {
-                a4 = ld_shared_f4(off);
-            } else {
-                a4 = ld_dsmem_f4(dsmem_addr(off, 0));
+            if (row >= p.M || col >= p.N) continue;
+            float4 a4 = ld_shared_f4(slot_addr(0, r, ch));
+            for (int s = 1; s < S; ++s) {
+                const float4 t = ld_shared_f4(slot_addr(s, r, ch));
+                a4.x += t.x;
+                a4.y += t.y;
+                a4.z += t.z;
+                a4.w += t.w;
+            }
+            ArgState unused{0.f, 0, 0};
+            epilogue4<EPI>(p, row, col, a4, unused);
+        }
+    } else {
+        // one row per warp, so the row's first maximum over this tile is a warp reduction
+        for (int r = warp; r < r_cnt; r += kWarps) {
+            const int row = m0 + r_lo + r;
+            if (row >= p.M) break;
+            ArgState as{-INFINITY, kArgNone, 0};
+            for (int ch = lane; ch < kChunks; ch += 32) {
+                const int col = n0 + ch * 4;
+                if (col >= p.N) break;
+                float4 a4 = ld_shared_f4(slot_addr(0, r, ch));
                 for (int s = 1; s < S; ++s) {
-                    const float4 t = ld_dsmem_f4(dsmem_addr(off, s));
+                    const float4 t = ld_shared_f4(slot_addr(s, r, ch));
                     a4.x += t.x;
                     a4.y += t.y;
                     a4.z += t.z;
                     a4.w += t.w;
                 }
+                epilogue4<EPI>(p, row, col, a4, as);
             }
-            epilogue4(p, row, col, a4, as);
-        }
-        if (argmax) {
-            // first maximum of the row over this tile: larger value, or equal value at a lower index
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
                 const float ov = __shfl_xor_sync(0xffffffffu, as.best, o);
@@ -378,19 +470,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
                     (as.idx & 0x7FFFFFFF) | (as.nf ? static_cast<int>(0x80000000u) : 0);
             }
         }
-    }
-    // No CTA may exit (freeing its shared memory) while a peer still reads its partial tile.
-    __syncwarp();
-    if (S > 1) cluster_sync_all(); else __syncthreads();
-
-    if (argmax) {
-        // splits == 1 (host-enforced). The last N tile of this row block to finish reduces the
-        // per-tile partials in tile order: the first maximum over the whole row.
+        // The last CTA of this row block to finish reduces the per-tile partials in tile order:
+        // the first maximum over the whole row. (n_tiles x S CTAs arrive per row block.)
         __threadfence();
         __syncthreads();
         if (threadIdx.x == 0) {
             const int t = atomicAdd(p.tickets + mt, 1);
-            *last_flag = (t == p.n_tiles - 1) ? 1 : 0;
+            *last_flag = (t == p.n_tiles * S - 1) ? 1 : 0;
         }
         __syncthreads();
         if (*last_flag) {
@@ -416,6 +502,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
             if (threadIdx.x == 0) p.tickets[mt] = 0;
         }
     }
+    // Outgoing bulk copies must have read the staging tile before this CTA's memory is released.
+    if (S > 1 && threadIdx.x == 0) bulk_wait_reads();
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -457,7 +545,13 @@ size_t stage_bytes_for(int bn) {
     return 2 * static_cast<size_t>(kATileBytes) + 2 * static_cast<size_t>(bn) * kBK * 4;
 }
 
-size_t staging_bytes_for(int bn) { return static_cast<size_t>(kBM) * (bn + 4) * 4; }
+int rows_per_for(int s) { return (kBM + s - 1) / s; }
+
+// Receive buffer for the peers' partials (none without a cluster: the staging tile reuses the
+// pipeline buffers).
+size_t recv_bytes_for(int bn, int s) {
+    return s > 1 ? static_cast<size_t>(s) * rows_per_for(s) * bn * 4 : 0;
+}
 
 // Two TMEM buffers, each with a hi*hi and a correction accumulator of BN columns.
 uint32_t tmem_cols_for(int bn) {
@@ -468,55 +562,142 @@ uint32_t tmem_cols_for(int bn) {
 
 typedef void (*GemmKernelFn)(GemmKParams);
 
-GemmKernelFn kernel_for(int bn) {
-    switch (bn) {
-        case 16: return gemm_3xtf32_kernel<16>;
-        case 32: return gemm_3xtf32_kernel<32>;
-        case 48: return gemm_3xtf32_kernel<48>;
-        case 64: return gemm_3xtf32_kernel<64>;
-        case 96: return gemm_3xtf32_kernel<96>;
-        case 128: return gemm_3xtf32_kernel<128>;
+template <int BN>
+GemmKernelFn kernel_for_epi(int flags) {
+    switch (flags) {
+        case kEpiSetStore: return gemm_3xtf32_kernel<BN, kEpiSetStore>;
+        case kEpiSetResid: return gemm_3xtf32_kernel<BN, kEpiSetResid>;
+        case kEpiSetFfnUp: return gemm_3xtf32_kernel<BN, kEpiSetFfnUp>;
+        case kEpiSetFfnDown: return gemm_3xtf32_kernel<BN, kEpiSetFfnDown>;
+        case kEpiSetHead: return gemm_3xtf32_kernel<BN, kEpiSetHead>;
+        case kEpiSetHeadLogits: return gemm_3xtf32_kernel<BN, kEpiSetHeadLogits>;
+        case kEpiSetScatter: return gemm_3xtf32_kernel<BN, kEpiSetScatter>;
         default: return nullptr;
     }
+}
+
+constexpr int kTileWidths[] = {32, 64, 128};
+
+GemmKernelFn kernel_for(int bn, int flags) {
+    switch (bn) {
+        case 32: return kernel_for_epi<32>(flags);
+        case 64: return kernel_for_epi<64>(flags);
+        case 128: return kernel_for_epi<128>(flags);
+        default: return nullptr;
+    }
+}
+
+// Sets the shared-memory attribute of every instantiation once per device.
+cudaError_t prepare_device_attrs() {
+    static std::mutex mu;
+    static unsigned long long done_mask = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 64 || (done_mask & (1ull << dev))) return cudaSuccess;
+    const int sets[] = {kEpiSetStore, kEpiSetResid, kEpiSetFfnUp, kEpiSetFfnDown, kEpiSetHead,
+                        kEpiSetHeadLogits, kEpiSetScatter};
+    for (int bn : kTileWidths)
+        for (int f : sets) {
+            GemmKernelFn k = kernel_for(bn, f);
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(kSmemLimit));
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (e != cudaSuccess) return e;
+        }
+    done_mask |= (1ull << dev);
+    return cudaSuccess;
+}
+
+// How many clusters of `s` CTAs with `smem` bytes each the current device can hold at once.
+int max_active_clusters(int bn, int s, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, int, size_t>, int> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const auto key = std::make_tuple(dev, bn, s, smem);
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    int n = 0;
+    if (prepare_device_attrs() == cudaSuccess) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(1, 1, s);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = s;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, kernel_for(bn, kEpiSetStore), &cfg) != cudaSuccess) n = 0;
+        cudaGetLastError();
+    }
+    cache[key] = n;
+    return n;
+}
+
+size_t smem_for(int bn, int s, int stages) {
+    return stages * stage_bytes_for(bn) + recv_bytes_for(bn, s) + kSmemReserve;
 }
 
 }  // namespace
 
 bool tensor_map_api_available() { return encode_fn() != nullptr; }
 
-// Picks the N tile and the cluster split of K from a simple time model (ns): per CTA a fixed
-// cost plus, per 32-wide K block, the slower of its HBM weight bytes (hi + lo planes), its
-// activation bytes (from L2) and its 12 tf32 MMAs; waves of CTAs over the SMs.
+// Picks the N tile and the cluster split of K from a time model fitted to measurements on B200
+// (ns): each CTA pays a fixed ~2.5 us (launch, prologue, first load, epilogue) plus its bytes —
+// the weight tile (HBM) and the activation tile (L2, re-read once per N tile) — at the rate one
+// SM ingests (~70 GB/s when all SMs pull), or its MMAs if slower; clusters that do not fit on
+// the device at once run in waves.
 GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms) {
     GemmPlan best;
     double best_t = 1e300;
     const int m_tiles = (M + kBM - 1) / kBM;
     const int total_kb = (K + kBK - 1) / kBK;
     const int n16 = (N + 15) / 16 * 16;
-    for (int bn : {16, 32, 48, 64, 96, 128}) {
-        if (bn > n16 && bn != 16) {
-            // wider than the matrix: only waste, unless no narrower instance covers it
+    for (int bn : kTileWidths) {
+        if (bn > n16 && bn != kTileWidths[0]) {
             bool narrower_covers = false;
-            for (int b2 : {16, 32, 48, 64, 96})
+            for (int b2 : kTileWidths)
                 if (b2 < bn && b2 >= n16) narrower_covers = true;
             if (narrower_covers) continue;
         }
         const int n_tiles = (N + bn - 1) / bn;
         const int tiles = m_tiles * n_tiles;
-        const int max_split = (flags & kEpiArgmax) ? 1 : std::min(kMaxCluster, total_kb);
-        for (int s = 1; s <= max_split; ++s) {
+        for (int s = 1; s <= std::min(kMaxCluster, total_kb); ++s) {
             const int kbc = (total_kb + s - 1) / s;
             if ((total_kb + kbc - 1) / kbc != s) continue;
+            if (s > 1 && (kBM % s) != 0) continue;  // whole rows per rank
+            const size_t sb = stage_bytes_for(bn);
+            const size_t recv = recv_bytes_for(bn, s);
+            if (recv + sb + kSmemReserve > kSmemLimit) continue;
+            int stages = static_cast<int>((kSmemLimit - kSmemReserve - recv) / sb);
+            stages = std::max(1, std::min({stages, 8, kbc}));
+            const size_t smem = smem_for(bn, s, stages);
             const long long ctas = static_cast<long long>(tiles) * s;
+            long long waves;
+            if (s > 1) {
+                const int cap = max_active_clusters(bn, s, smem);
+                if (cap <= 0) continue;
+                waves = (static_cast<long long>(tiles) + cap - 1) / cap;
+            } else {
+                waves = (ctas + num_sms - 1) / num_sms;
+            }
             const long long active = std::min<long long>(ctas, num_sms);
-            const long long waves = (ctas + num_sms - 1) / num_sms;
-            const double bw_sm = std::min(150.0, 6500.0 / static_cast<double>(active));  // B/ns
-            const double hbm_ns = 256.0 * bn / bw_sm;
-            const double l2_ns = 32768.0 / 120.0;
+            // One SM keeps ~`stages` boxes in flight against ~1.7 us of load latency; all SMs
+            // together are capped near 9.5 TB/s (L2 + HBM) and the weights alone by HBM.
+            const double ingest = std::min({static_cast<double>(stages) * sb / 1700.0, 150.0,
+                                            9500.0 / static_cast<double>(active)});  // B/ns
+            const double bytes_kb = static_cast<double>(sb);                       // A + W tiles
             const double mma_ns = 24576.0 * bn / 7400.0;
-            const double per_kb = std::max(hbm_ns, std::max(l2_ns, mma_ns));
-            const double t = static_cast<double>(waves) *
-                             (1500.0 + kbc * per_kb + 2.0 * s * bn + 4.0 * bn);
+            const double per_kb = std::max(bytes_kb / ingest, mma_ns);
+            const double hbm_floor = static_cast<double>(N) * K * 8.0 / 6500.0;    // W hi + lo
+            const double t = std::max(static_cast<double>(waves) * (2500.0 + kbc * per_kb + 60.0 * s),
+                                      hbm_floor + 2500.0);
             if (t < best_t - 1e-9) {
                 best_t = t;
                 best.bn = bn;
@@ -524,16 +705,11 @@ GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms) {
                 best.kb_per_split = kbc;
                 best.m_tiles = m_tiles;
                 best.n_tiles = n_tiles;
+                best.stages = stages;
+                best.smem_bytes = smem;
             }
         }
     }
-    const size_t sb = stage_bytes_for(best.bn);
-    const size_t stb = staging_bytes_for(best.bn);
-    int stages = static_cast<int>((kSmemLimit - kSmemReserve) / sb);
-    stages = std::max(1, std::min(stages, 8));
-    stages = std::min(stages, std::max(1, best.kb_per_split));
-    best.stages = stages;
-    best.smem_bytes = std::max(stages * sb, stb) + kSmemReserve;
     // promotion chunk: one 32-wide K block per chunk for short K-slices, two for long ones
     best.chunk_kb = best.kb_per_split > 16 ? 2 : 1;
     // Keep (CTAs resident per SM) x (TMEM columns per CTA) <= 512: pad the shared-memory request
@@ -543,6 +719,7 @@ GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms) {
     const size_t sm_bytes = 228 * 1024;
     const size_t min_smem = sm_bytes / (max_ctas + 1) + 1;  // max_ctas + 1 CTAs must not fit
     if (best.smem_bytes < min_smem) best.smem_bytes = min_smem;
+    (void)flags;
     return best;
 }
 
@@ -554,30 +731,17 @@ size_t gemm_arg_entries(const GemmPlan& p) {
 
 int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& epi,
                 const GemmPlan& plan, const GemmScratch& scratch, int* err, cudaStream_t st) {
-    {
-        // The attribute is per device; set it once for each device this process launches on.
-        static std::mutex mu;
-        static unsigned long long done_mask = 0;
-        int dev = 0;
-        cudaGetDevice(&dev);
-        std::lock_guard<std::mutex> lock(mu);
-        if (dev < 64 && !(done_mask & (1ull << dev))) {
-            for (int bn : {16, 32, 48, 64, 96, 128}) {
-                const cudaError_t e = cudaFuncSetAttribute(
-                    kernel_for(bn), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                    static_cast<int>(kSmemLimit));
-                if (e != cudaSuccess) return static_cast<int>(e);
-            }
-            done_mask |= (1ull << dev);
-        }
-    }
+    const cudaError_t ae = prepare_device_attrs();
+    if (ae != cudaSuccess) return static_cast<int>(ae);
     if (M <= 0 || w.N <= 0 || w.K <= 0 || a.K != w.K) return cudaErrorInvalidValue;
     if (a.rows_alloc < plan.m_tiles * kBM) return cudaErrorInvalidValue;
-    GemmKernelFn kern = kernel_for(plan.bn);
-    if (kern == nullptr || plan.chunk_kb < 1) return cudaErrorInvalidValue;
-    if (plan.splits < 1 || plan.splits > kMaxCluster) return cudaErrorInvalidValue;
-    if (plan.smem_bytes > kSmemLimit) return cudaErrorInvalidValue;
-    if ((epi.flags & kEpiArgmax) && plan.splits != 1) return cudaErrorInvalidValue;
+    GemmKernelFn kern = kernel_for(plan.bn, epi.flags);
+    if (kern == nullptr || plan.chunk_kb < 1 || plan.stages < 1) return cudaErrorInvalidValue;
+    if (plan.splits < 1 || plan.splits > kMaxCluster || (plan.splits > 1 && kBM % plan.splits))
+        return cudaErrorInvalidValue;
+    if (plan.smem_bytes > kSmemLimit ||
+        plan.smem_bytes < smem_for(plan.bn, plan.splits, plan.stages))
+        return cudaErrorInvalidValue;
     if ((epi.flags & kEpiArgmax) &&
         (scratch.arg_val == nullptr || scratch.arg_entries < gemm_arg_entries(plan) ||
          scratch.n_tickets < plan.m_tiles || epi.next_ids == nullptr))
@@ -596,10 +760,10 @@ int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e
     p.M = M;
     p.N = w.N;
     p.K = w.K;
-    p.bn = plan.bn;
     p.stages = plan.stages;
     p.kb_per_split = plan.kb_per_split;
     p.splits = plan.splits;
+    p.rows_per = rows_per_for(plan.splits);
     p.n_tiles = plan.n_tiles;
     p.m_tiles = plan.m_tiles;
     p.total_kb = (w.K + kBK - 1) / kBK;
@@ -617,15 +781,22 @@ int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = plan.smem_bytes;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
+    int na = 0;
     if (plan.splits > 1) {
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 1;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = plan.splits;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = plan.splits;
+        ++na;
     }
+    if (launch_pdl_enabled()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
     if (e != cudaSuccess) return static_cast<int>(e);
     return static_cast<int>(cudaGetLastError());

@@ -102,6 +102,8 @@ template <int NV>
 __global__ void layernorm_kernel(const float* __restrict__ x, int ldx,
                                  const float* __restrict__ g, const float* __restrict__ b,
                                  float* out, float* out_hi, float* out_lo, int rows, int D) {
+    pdl_trigger();
+    pdl_wait();
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -122,6 +124,8 @@ __global__ void embed_ln_kernel(const float* __restrict__ table, const int* __re
                                 const float* __restrict__ g, const float* __restrict__ b,
                                 float* out_hi, float* out_lo, int rows, int D, int vocab,
                                 int* err) {
+    pdl_trigger();
+    pdl_wait();
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -196,6 +200,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) decode_attention_kernel(const
     constexpr int RPW = 32 / LPR;      // rows per warp per load
     constexpr int G = kAttnWarps * RPW;  // consecutive rows per CTA per load
     constexpr unsigned kRowMask = (LPR == 32) ? 0xffffffffu : ((1u << LPR) - 1u);
+    pdl_trigger();
+    pdl_wait();
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int slot = a.slots ? a.slots[b] : b;
     const int len = a.len_by_slot[slot] + a.len_add;
@@ -448,6 +454,8 @@ __global__ void __launch_bounds__(kPreQ) prefill_attention_kernel(
 __global__ void advance_kernel(const int* __restrict__ next, int* __restrict__ ids,
                                const int* __restrict__ slots, int* __restrict__ len_by_slot,
                                int B) {
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     ids[b] = next[b];
@@ -470,18 +478,24 @@ void launch_transpose_split(const float* w, int K, int N, float* hi_t, float* lo
     transpose_split_kernel<<<grid, dim3(32, 8), 0, st>>>(w, K, N, hi_t, lo_t);
 }
 
-#define ADAI_LN_DISPATCH(NV_, KERNEL, ...)                 \
-    switch (NV_) {                                         \
-        case 1: KERNEL<1><<<grid, block, 0, st>>>(__VA_ARGS__); break; \
-        case 2: KERNEL<2><<<grid, block, 0, st>>>(__VA_ARGS__); break; \
-        case 3: KERNEL<3><<<grid, block, 0, st>>>(__VA_ARGS__); break; \
-        case 4: KERNEL<4><<<grid, block, 0, st>>>(__VA_ARGS__); break; \
-        case 6: KERNEL<6><<<grid, block, 0, st>>>(__VA_ARGS__); break; \
-        case 8: KERNEL<8><<<grid, block, 0, st>>>(__VA_ARGS__); break; \
-        case 12: KERNEL<12><<<grid, block, 0, st>>>(__VA_ARGS__); break; \
-        case 16: KERNEL<16><<<grid, block, 0, st>>>(__VA_ARGS__); break; \
-        default: break;                                    \
+#define ADAI_LN_DISPATCH(NV_, KERNEL, ...)                                          \
+    switch (NV_) {                                                                  \
+        case 1: launch_kernel(KERNEL<1>, grid, block, 0, st, __VA_ARGS__); break;   \
+        case 2: launch_kernel(KERNEL<2>, grid, block, 0, st, __VA_ARGS__); break;   \
+        case 3: launch_kernel(KERNEL<3>, grid, block, 0, st, __VA_ARGS__); break;   \
+        case 4: launch_kernel(KERNEL<4>, grid, block, 0, st, __VA_ARGS__); break;   \
+        case 6: launch_kernel(KERNEL<6>, grid, block, 0, st, __VA_ARGS__); break;   \
+        case 8: launch_kernel(KERNEL<8>, grid, block, 0, st, __VA_ARGS__); break;   \
+        case 12: launch_kernel(KERNEL<12>, grid, block, 0, st, __VA_ARGS__); break; \
+        case 16: launch_kernel(KERNEL<16>, grid, block, 0, st, __VA_ARGS__); break; \
+        default: break;                                                             \
     }
+
+namespace {
+thread_local bool t_launch_pdl = false;
+}
+bool launch_pdl_enabled() { return t_launch_pdl; }
+void set_launch_pdl(bool on) { t_launch_pdl = on; }
 
 bool layernorm_width_supported(int D) {
     if (D % 128) return false;
@@ -519,9 +533,9 @@ void launch_decode_attention(const DecodeAttnArgs& a, int* err, cudaStream_t st)
     const int max_ch = (std::max(a.max_len, 1) + kAttnChunk - 1) / kAttnChunk;
     dim3 grid(max_ch, a.H, a.B);
     if (a.head_dim == 32)
-        decode_attention_kernel<32><<<grid, kAttnWarps * 32, 0, st>>>(a);
+        launch_kernel(decode_attention_kernel<32>, grid, dim3(kAttnWarps * 32), 0, st, a);
     else
-        decode_attention_kernel<64><<<grid, kAttnWarps * 32, 0, st>>>(a);
+        launch_kernel(decode_attention_kernel<64>, grid, dim3(kAttnWarps * 32), 0, st, a);
 }
 
 void launch_prefill_attention(const float* qkv, int D, int H, const int* offsets, const int* lens,
@@ -538,7 +552,8 @@ void launch_prefill_attention(const float* qkv, int D, int H, const int* offsets
 void launch_advance(const int* next, int* ids, const int* slots, int* len_by_slot, int B,
                     cudaStream_t st) {
     if (B <= 0) return;
-    advance_kernel<<<(B + 127) / 128, 128, 0, st>>>(next, ids, slots, len_by_slot, B);
+    launch_kernel(advance_kernel, dim3((B + 127) / 128), dim3(128), 0, st, next, ids, slots,
+                  len_by_slot, B);
 }
 
 }  // namespace adai_b200

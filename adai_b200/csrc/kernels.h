@@ -6,8 +6,41 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <utility>
 
 namespace adai_b200 {
+
+// ------------------------------------------------------------------------------------------
+// Programmatic dependent launch. While enabled on the calling thread, every launch below asks
+// for programmatic stream serialization: the kernel may start its prologue while the preceding
+// kernel finishes; each kernel waits (griddepcontrol.wait) before touching data of earlier
+// kernels. The decode step enables it around the launches it captures into its CUDA graph.
+bool launch_pdl_enabled();
+void set_launch_pdl(bool on);
+
+struct ScopedPdl {
+    bool prev;
+    explicit ScopedPdl(bool on) : prev(launch_pdl_enabled()) { set_launch_pdl(on); }
+    ~ScopedPdl() { set_launch_pdl(prev); }
+};
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t st, Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (launch_pdl_enabled()) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ------------------------------------------------------------------------------------------
 // 3xTF32 tcgen05 GEMM: out[M,N] = epilogue(A[M,K] * W[K,N]) with A given as its tf32 split
