@@ -648,6 +648,10 @@ size_t smem_for(int bn, int s, int stages) {
 
 bool tensor_map_api_available() { return encode_fn() != nullptr; }
 
+int gemm_cluster_capacity(int bn, int splits, int stages) {
+    return max_active_clusters(bn, splits, smem_for(bn, splits, stages));
+}
+
 // Picks the N tile and the cluster split of K from a time model fitted to measurements on B200
 // (ns): each CTA pays a fixed ~2.5 us (launch, prologue, first load, epilogue) plus its bytes —
 // the weight tile (HBM) and the activation tile (L2, re-read once per N tile) — at the rate one

@@ -125,6 +125,8 @@ int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e
                 const GemmPlan& plan, const GemmScratch& scratch, int* err, cudaStream_t st);
 
 bool tensor_map_api_available();
+// Clusters of `splits` GEMM CTAs (tile width bn, `stages` pipeline stages) the device holds at once.
+int gemm_cluster_capacity(int bn, int splits, int stages);
 
 // ------------------------------------------------------------------------------------------
 // Row kernels

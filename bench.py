@@ -156,6 +156,78 @@ def run_reference_arm(args, wl, rank):
     print(json.dumps(line), flush=True)
 
 
+DECODE_GEMMS = [(128, 3072, 1024), (128, 1024, 1024), (128, 4096, 1024), (128, 1024, 4096),
+                (128, 32000, 1024)]
+
+
+def run_op(args):
+    """Op-level cases, one JSON line each (not the headline metric): `--op gemm` times the
+    prepared-weight product C = A B for each M,N,K of --shapes (default: the large model's
+    decode projections at 128 rows); `--op attention` times single-token attention over a KV
+    cache of --attn-batch sequences x 16 heads x 64 with lengths uniform in --attn-lens and one
+    appended row per step (--attn-append 1) or none (the cross-attention form)."""
+    import torch
+
+    from adai_b200 import Context
+    ctx = Context(0)
+    st = torch.cuda.ExternalStream(ctx.stream)
+    g = torch.Generator(device="cuda").manual_seed(0)
+
+    def timed(fn, iters):
+        for _ in range(args.warmup):
+            fn()
+        ctx.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(iters):
+            fn()
+        e1.record(st)
+        ctx.synchronize()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters
+
+    if args.op == "gemm":
+        shapes = ([tuple(int(x) for x in s.split(",")) for s in args.shapes.split(";")]
+                  if args.shapes else DECODE_GEMMS)
+        for M, N, K in shapes:
+            A = torch.randn(M, K, device="cuda", generator=g)
+            B = torch.randn(K, N, device="cuda", generator=g)
+            C = torch.empty(M, N, device="cuda")
+            torch.cuda.synchronize()
+            w = ctx.weight(B.data_ptr(), K, N)
+            ms = timed(lambda: w.matmul(M, A.data_ptr(), C.data_ptr()), args.steps)
+            w.close()
+            flops = 2.0 * M * N * K
+            print(json.dumps({"op": "gemm", "M": M, "N": N, "K": K, "us": ms * 1e3,
+                              "TFLOP/s": flops / ms / 1e9,
+                              "algorithmic_GB/s": 4.0 * (M * K + K * N + M * N) / ms / 1e6,
+                              "note": "per call: A split into tf32 hi/lo + the GEMM"}), flush=True)
+    else:
+        B, H, dh = args.attn_batch, 16, 64
+        lo, hi = (int(x) for x in args.attn_lens.split(","))
+        cap = hi + (1 if args.attn_append else 0)   # the append lands at row lens[b] every call
+        lens = np.random.default_rng(0).integers(lo, hi + 1, size=B).astype(np.int32)
+        kc = torch.randn((B, H, cap, dh), generator=g, device="cuda")
+        vc = torch.randn((B, H, cap, dh), generator=g, device="cuda")
+        q = torch.randn((B, H * dh), generator=g, device="cuda")
+        kn = torch.randn((B, H * dh), generator=g, device="cuda") if args.attn_append else None
+        vn = torch.randn((B, H * dh), generator=g, device="cuda") if args.attn_append else None
+        out = torch.empty_like(q)
+        dl = torch.from_numpy(lens).cuda()
+        torch.cuda.synchronize()
+        ptr = (lambda t: None if t is None else t.data_ptr())
+        ms = timed(lambda: ctx.decode_attention(B, H, cap, q.data_ptr(), ptr(kn), ptr(vn),
+                                                kc.data_ptr(), vc.data_ptr(), dl.data_ptr(),
+                                                int(lens.max()), out.data_ptr()), args.steps)
+        rows = float(lens.sum() + (B if args.attn_append else 0))
+        nbytes = rows * 2 * H * dh * 4 + B * H * dh * 4 * (4 if args.attn_append else 2)
+        print(json.dumps({"op": "attention", "batch": B, "heads": H, "head_dim": dh,
+                          "capacity": cap, "lens": [lo, hi], "append": bool(args.attn_append),
+                          "us": ms * 1e3, "GB/s": nbytes / ms / 1e6,
+                          "algorithmic_bytes": nbytes}), flush=True)
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -167,9 +239,17 @@ def main():
     ap.add_argument("--cpu-baseline-steps", type=int, default=12)
     ap.add_argument("--reference-max-steps", type=int, default=48)
     ap.add_argument("--profile-steps", type=int, default=3)
+    ap.add_argument("--op", choices=["gemm", "attention"], default=None)
+    ap.add_argument("--shapes", default="", help="--op gemm: 'M,N,K;M,N,K;...'")
+    ap.add_argument("--attn-batch", type=int, default=256)
+    ap.add_argument("--attn-lens", default="256,2047")
+    ap.add_argument("--attn-append", type=int, default=1)
     args = ap.parse_args()
     if args.warmup < 1 or args.steps < 1:
         ap.error("--steps and --warmup must be positive")
+    if args.op:
+        run_op(args)
+        return
     wl = WORKLOADS[args.workload]
     rank, world, local = dist_env()
 
