@@ -50,7 +50,7 @@ EXPORTS = [
     "adai_b200_decode_step", "adai_b200_generate", "adai_b200_sgemm", "adai_b200_weight_create",
     "adai_b200_weight_destroy", "adai_b200_sgemm_prepared", "adai_b200_decode_attention",
     "adai_b200_layernorm", "adai_b200_ctx_last_timing", "adai_b200_profile_step",
-    "adai_b200_kv_clear_self",
+    "adai_b200_kv_clear_self", "adai_b200_decode_attention_static",
 ]
 
 # Kernel classes of adai_b200_profile_step (adai_b200_kernel_class).
@@ -103,6 +103,7 @@ def load() -> C.CDLL:
     lib.adai_b200_sgemm_prepared.argtypes = [_vp, C.c_int, _vp, _vp, _vp]
     lib.adai_b200_decode_attention.argtypes = [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp,
                                                _vp, _vp, _vp, C.c_int, _vp]
+    lib.adai_b200_decode_attention_static.argtypes = lib.adai_b200_decode_attention.argtypes
     lib.adai_b200_layernorm.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int]
     lib.adai_b200_ctx_last_timing.argtypes = [_vp, C.POINTER(C.c_double), _ip]
     lib.adai_b200_profile_step.argtypes = [_vp, _vp, C.c_int, _vp, _vp, C.c_int, _vp, _vp, _vp,
@@ -204,6 +205,15 @@ class Context:
                          out, head_dim=64) -> None:
         check(self.lib.adai_b200_decode_attention(self.h, B, H, head_dim, capacity, q, k_new,
                                                   v_new, k_cache, v_cache, lens, max_len, out))
+
+    def decode_attention_static(self, B, H, capacity, q, k_new, v_new, k_cache, v_cache, lens,
+                                max_len, out, head_dim=64) -> None:
+        """decode_attention without any device allocation: the split-KV scratch is a fixed
+        16 MiB array per device, shared by every caller on that device (calls that overlap in
+        time race). Too-large calls raise IndexError."""
+        check(self.lib.adai_b200_decode_attention_static(self.h, B, H, head_dim, capacity, q,
+                                                         k_new, v_new, k_cache, v_cache, lens,
+                                                         max_len, out))
 
     def layernorm(self, x, gamma, beta, out, rows, D) -> None:
         check(self.lib.adai_b200_layernorm(self.h, x, gamma, beta, out, rows, D))

@@ -15,6 +15,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <set>
 #include <stdexcept>
 #include <string>
@@ -1488,6 +1489,105 @@ int adai_b200_layernorm(adai_b200_ctx* c, const float* x, const float* gamma, co
         if (!layernorm_width_supported(D)) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "D must be 128 * {1,2,3,4,6,8,12,16}");
         launch_layernorm(x, D, gamma, beta, out, nullptr, nullptr, rows, D, c->stream);
         cuda_ok(cudaGetLastError(), "layernorm launch");
+    });
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Decode attention with static scratch: adai_b200_decode_attention for callers that must not
+// allocate device memory at call time. The split-KV partials and the per-(sequence, head) merge
+// tickets live in one fixed array that is part of this library's device image, so the call
+// itself neither allocates nor frees: it suits a host that has handed all free device memory to
+// its own pool up front (nothing is left for a late cudaMalloc, and a cudaMalloc would also
+// stall the device while its streams are busy), or that forbids allocation on its serving path.
+// The price is a hard size limit and one shared buffer per device: calls that overlap in time
+// on the same device (two streams, two contexts, two threads) race on it and corrupt each
+// other's results. Serialize them.
+static constexpr size_t kStaticAttnScratchBytes = size_t(16) << 20;  // per device
+static constexpr size_t kStaticAttnTicketBytes = size_t(64) << 10;   // first part: tickets
+static constexpr int kStaticAttnMaxPairs = static_cast<int>(kStaticAttnTicketBytes / sizeof(int));
+
+static __device__ __align__(256) unsigned char g_static_attn_scratch[kStaticAttnScratchBytes];
+
+namespace {
+
+constexpr int kStaticMaxDevices = 64;
+std::mutex g_static_attn_mu;
+unsigned char* g_static_attn_base[kStaticMaxDevices] = {};
+
+// The scratch array's address on the current device. The first call on a device looks the
+// address up and zeroes the tickets (the merge counts on them starting at zero; every launch
+// hands them back at zero). `device` must be the current device.
+unsigned char* static_attn_scratch(int device, cudaStream_t st) {
+    if (device < 0 || device >= kStaticMaxDevices)
+        fail(ADAI_B200_ERR_INVALID_ARGUMENT, "device index out of range for the static scratch table");
+    std::lock_guard<std::mutex> lock(g_static_attn_mu);
+    if (g_static_attn_base[device] == nullptr) {
+        void* p = nullptr;
+        cuda_ok(cudaGetSymbolAddress(&p, g_static_attn_scratch), "cudaGetSymbolAddress(static attention scratch)");
+        cuda_ok(cudaMemsetAsync(p, 0, kStaticAttnTicketBytes, st), "zero static attention tickets");
+        g_static_attn_base[device] = static_cast<unsigned char*>(p);
+    }
+    return g_static_attn_base[device];
+}
+
+}  // namespace
+
+extern "C" {
+
+int adai_b200_decode_attention_static(adai_b200_ctx* c, int B, int H, int head_dim, int capacity,
+                                      const float* q, const float* k_new, const float* v_new,
+                                      float* k_cache, float* v_cache, const int* lens, int max_len,
+                                      float* out) {
+    return guarded([&] {
+        check_ctx(c);
+        if (B <= 0 || H <= 0 || capacity <= 0 || !q || !k_cache || !v_cache || !lens || !out)
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad attention arguments");
+        if (!attention_head_dim_supported(head_dim))
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "head_dim must be 32 or 64");
+        if ((k_new == nullptr) != (v_new == nullptr))
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "k_new and v_new must both be given or both be null");
+        const int add = k_new ? 1 : 0;
+        if (max_len < 0 || max_len + add > capacity)
+            fail(ADAI_B200_ERR_OUT_OF_RANGE, "max_len exceeds the cache capacity");
+        const long long pairs = static_cast<long long>(B) * H;
+        const size_t part_bytes = decode_attn_ws_floats(B, H, max_len + add, head_dim) * sizeof(float);
+        const size_t part_max = kStaticAttnScratchBytes - kStaticAttnTicketBytes;
+        if (pairs > kStaticAttnMaxPairs || part_bytes > part_max) {
+            char msg[256];
+            std::snprintf(msg, sizeof msg,
+                          "static attention scratch too small: B*H = %lld (max %d) and %zu bytes of "
+                          "split partials (max %zu); use adai_b200_decode_attention",
+                          pairs, kStaticAttnMaxPairs, part_bytes, part_max);
+            fail(ADAI_B200_ERR_OUT_OF_RANGE, msg);
+        }
+        unsigned char* base = static_attn_scratch(c->device, c->stream);
+        const int D = H * head_dim;
+        DecodeAttnArgs a;
+        a.q = q;
+        a.ldq = D;
+        a.k_new = k_new;
+        a.v_new = v_new;
+        a.ldkv = D;
+        a.kc = k_cache;
+        a.vc = v_cache;
+        a.slot_stride = static_cast<long long>(H) * capacity * head_dim;
+        a.cap = capacity;
+        a.slots = nullptr;
+        a.len_by_slot = lens;
+        a.len_add = add;
+        a.out = out;
+        a.ldo = D;
+        a.B = B;
+        a.H = H;
+        a.head_dim = head_dim;
+        a.max_len = max_len + add;
+        a.scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
+        a.tickets = reinterpret_cast<int*>(base);
+        a.ws = reinterpret_cast<float*>(base + kStaticAttnTicketBytes);
+        launch_decode_attention(a, c->d_err, c->stream);
+        cuda_ok(cudaGetLastError(), "attention launch");
     });
 }
 

@@ -9,7 +9,8 @@
  * Threading: one context per GPU, used by one host thread at a time (the reference serialises its
  * GPU path the same way: EncoderDecoderModel::model_mutex_, src/EncoderDecoderModel.cpp:366 and
  * :1476, and the cuBLAS mutex, src/gpu/MatrixGPU.cu:356). Several contexts on several GPUs may be
- * driven from several threads at once; nothing is shared between contexts.
+ * driven from several threads at once; nothing is shared between contexts except the scratch
+ * array of adai_b200_decode_attention_static (one per device).
  *
  * Layouts: host tensors are row-major fp32 exactly as the reference Matrix holds them
  * (src/Matrix.hpp:32); weights are W[in, out] as the reference setters take them.
@@ -163,6 +164,25 @@ ADAI_B200_API int adai_b200_decode_attention(adai_b200_ctx* ctx, int B, int H, i
                                              int capacity, const float* q, const float* k_new,
                                              const float* v_new, float* k_cache, float* v_cache,
                                              const int* lens, int max_len, float* out);
+
+/* No counterpart in the reference. adai_b200_decode_attention for callers that must not allocate
+ * device memory at call time: a host that has reserved all free device memory for its own pool,
+ * or a serving loop that forbids allocation (a device allocation can stall every stream of the
+ * device). Same arguments, same arithmetic and same results as adai_b200_decode_attention, but
+ * the split-KV scratch is a fixed 16 MiB array inside this library's device image (per device),
+ * so the call allocates and frees nothing.
+ * Limits: B * H <= 16384, and the split partials, B * H * ceil((max_len + appended) / 256) *
+ * (head_dim + 4) floats, must fit in 16 MiB - 64 KiB (B = 256, H = 16, head_dim = 64 fits while
+ * max_len + appended <= 3840); larger calls return ADAI_B200_ERR_OUT_OF_RANGE and launch nothing.
+ * The first call on each device does a one-time setup (looks up the array's address and zeroes
+ * its merge counters on ctx's stream); make that first call before any stream capture.
+ * The array is shared by every caller on a device: calls that overlap in time on one device race
+ * and corrupt each other's results, so serialize them. */
+ADAI_B200_API int adai_b200_decode_attention_static(adai_b200_ctx* ctx, int B, int H, int head_dim,
+                                                    int capacity, const float* q,
+                                                    const float* k_new, const float* v_new,
+                                                    float* k_cache, float* v_cache,
+                                                    const int* lens, int max_len, float* out);
 
 /* ---- op level: LayerNorm (LayerNorm::forward, src/LayerNorm.cpp:56-109; the reference GPU
  * kernel matrix_layer_norm_fwd_gpu, src/gpu/MatrixGPU.hpp:140) ----
