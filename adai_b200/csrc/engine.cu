@@ -292,8 +292,8 @@ struct adai_b200_ctx {
     void ensure_gemm_scratch(const GemmPlan& p) {
         const size_t ws = gemm_ws_floats(p);
         const int tk = p.m_tiles * p.n_tiles;
-        const size_t ae = gemm_arg_entries(p);
-        if (ws > gs.ws_floats || tk > gs.n_tickets || ae > gs.arg_entries) {
+        const size_t ar = gemm_arg_rows(p);
+        if (ws > gs.ws_floats || tk > gs.n_tickets || ar > gs.arg_rows) {
             cuda_ok(cudaStreamSynchronize(stream), "sync before scratch growth");
             clear_graphs();
             if (ws > gs.ws_floats) {
@@ -306,12 +306,12 @@ struct adai_b200_ctx {
                 gs.n_tickets = std::max(tk, 1024);
                 gs.tickets = dzalloc_t<int>(gs.n_tickets);
             }
-            if (ae > gs.arg_entries) {
-                dfree(gs.arg_val);
-                dfree(gs.arg_idx);
-                gs.arg_entries = std::max(ae, gs.arg_entries * 2);
-                gs.arg_val = dalloc_t<float>(gs.arg_entries);
-                gs.arg_idx = dalloc_t<int>(gs.arg_entries);
+            if (ar > gs.arg_rows) {
+                dfree(gs.arg_key);
+                dfree(gs.arg_nf);
+                gs.arg_rows = std::max(ar, gs.arg_rows * 2);
+                gs.arg_key = dzalloc_t<unsigned long long>(gs.arg_rows);
+                gs.arg_nf = dzalloc_t<int>(gs.arg_rows);
             }
         }
     }

@@ -29,6 +29,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -65,12 +66,26 @@ struct __align__(64) GemmKParams {
     uint32_t idesc, tmem_cols;
     GemmEpilogue epi;
     int* tickets;
-    float* arg_val;
-    int* arg_idx;
+    unsigned long long* arg_key;
+    int* arg_nf;
     int* err;
 };
 
 constexpr int kArgNone = 0x7FFFFFFF;
+
+// First-maximum argmax across CTAs as one 64-bit atomicMax per row: the high word orders like
+// the float (sign-magnitude bits mapped to an unsigned order; -0 folded into +0 so the two
+// compare equal, as they do in the reference's `>`), the low word is the complemented column,
+// so equal values resolve to the lowest column. Zero means "no candidate": every finite value
+// and +inf map to a non-zero high word.
+__device__ __forceinline__ unsigned long long arg_key_of(float v, int col) {
+    const uint32_t u = __float_as_uint(v == 0.f ? 0.f : v);
+    const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return (static_cast<unsigned long long>(ord) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(col));
+}
+__device__ __forceinline__ int arg_col_of(unsigned long long key) {
+    return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
+}
 
 struct ArgState {
     float best;
@@ -465,13 +480,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
                 as.nf |= onf;
             }
             if (lane == 0) {
-                p.arg_val[static_cast<size_t>(row) * p.n_tiles + nt] = as.best;
-                p.arg_idx[static_cast<size_t>(row) * p.n_tiles + nt] =
-                    (as.idx & 0x7FFFFFFF) | (as.nf ? static_cast<int>(0x80000000u) : 0);
+                if (as.idx != kArgNone) atomicMax(p.arg_key + row, arg_key_of(as.best, as.idx));
+                if (as.nf) atomicOr(p.arg_nf + row, 1);
             }
         }
-        // The last CTA of this row block to finish reduces the per-tile partials in tile order:
-        // the first maximum over the whole row. (n_tiles x S CTAs arrive per row block.)
+        // The last CTA of this row block to finish (n_tiles x S arrive) reads every row's key,
+        // which by then holds the first maximum over the whole row, and hands the keys and
+        // flags back at zero for the next launch.
         __threadfence();
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -484,20 +499,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
             for (int rl = threadIdx.x; rl < kBM; rl += kThreads) {
                 const int row = m0 + rl;
                 if (row >= p.M) break;
-                float best = -INFINITY;
-                int idx = kArgNone, nf = 0;
-                for (int t = 0; t < p.n_tiles; ++t) {
-                    const float bv = __ldcg(p.arg_val + static_cast<size_t>(row) * p.n_tiles + t);
-                    const int bi = __ldcg(p.arg_idx + static_cast<size_t>(row) * p.n_tiles + t);
-                    nf |= (bi >> 31) & 1;
-                    const int ii = bi & 0x7FFFFFFF;
-                    if (ii != kArgNone && bv > best) {
-                        best = bv;
-                        idx = ii;
-                    }
-                }
-                p.epi.next_ids[row] = (idx == kArgNone) ? -1 : idx;
-                if (p.epi.nonfinite) p.epi.nonfinite[row] = (nf || idx == kArgNone) ? 1 : 0;
+                const unsigned long long key = atomicExch(p.arg_key + row, 0ull);
+                const int nf = atomicExch(p.arg_nf + row, 0);
+                p.epi.next_ids[row] = key ? arg_col_of(key) : -1;
+                if (p.epi.nonfinite) p.epi.nonfinite[row] = (nf || key == 0ull) ? 1 : 0;
             }
             if (threadIdx.x == 0) p.tickets[mt] = 0;
         }
@@ -657,13 +662,106 @@ int gemm_cluster_capacity(int bn, int splits, int stages) {
 // the weight tile (HBM) and the activation tile (L2, re-read once per N tile) — at the rate one
 // SM ingests (~70 GB/s when all SMs pull), or its MMAs if slower; clusters that do not fit on
 // the device at once run in waves.
+//
+// Decode projections (one 128-row tile) of the supported model widths use plans measured on B200
+// instead: candidate (N tile, cluster split, stages, promotion chunk) sets were timed for each
+// shape, alone and inside the captured decode step (where the overlap of consecutive launches
+// decides: plans that fill every SM leave the next launch no room to start early), and the
+// fastest kept. The model mispredicts these latency-bound launches by up to 1.5x (K = 4096:
+// split 8 with 128-wide tiles runs in 18.9 us against 28.7 us for its pick).
+struct MeasuredPlan {
+    int n, k, bn, splits, stages, chunk_kb;
+};
+constexpr MeasuredPlan kMeasuredPlans[] = {
+    // d_model 1024, d_ff 4096, vocab 32000
+    {3072, 1024, 128, 4, 2, 8},
+    {1024, 1024, 32, 4, 4, 8},
+    {4096, 1024, 128, 4, 2, 8},
+    {1024, 4096, 128, 8, 2, 8},
+    {32000, 1024, 128, 1, 3, 8},
+    // d_model 512, d_ff 2048, vocab 16000
+    {1536, 512, 64, 4, 2, 4},
+    {16000, 512, 128, 1, 3, 8},
+    // d_model 128, d_ff 512
+    {384, 128, 32, 2, 2, 2},
+    {128, 128, 32, 2, 2, 2},
+    {512, 128, 32, 2, 2, 2},
+    {128, 512, 32, 8, 2, 2},
+};
+
+// Keep (CTAs resident per SM) x (TMEM columns per CTA) <= 512: the smallest shared-memory request
+// that lets no more CTAs fit on an SM than its tensor memory can hold at once.
+size_t tmem_bound_smem(int bn) {
+    const size_t max_ctas = 512 / tmem_cols_for(bn);
+    return 228 * 1024 / (max_ctas + 1) + 1;  // max_ctas + 1 CTAs must not fit
+}
+
+// Fills kb_per_split, tile counts and the shared-memory request of a plan whose bn, splits and
+// stages are set; false if it does not fit or its clusters cannot be placed.
+bool complete_plan(GemmPlan& p, int M, int N, int K) {
+    const int total_kb = (K + kBK - 1) / kBK;
+    if (p.splits < 1 || p.splits > std::min(kMaxCluster, total_kb) || kBM % p.splits) return false;
+    p.kb_per_split = (total_kb + p.splits - 1) / p.splits;
+    if ((total_kb + p.kb_per_split - 1) / p.kb_per_split != p.splits) return false;
+    p.m_tiles = (M + kBM - 1) / kBM;
+    p.n_tiles = (N + p.bn - 1) / p.bn;
+    p.stages = std::max(1, std::min(p.stages, p.kb_per_split));
+    p.chunk_kb = std::max(1, std::min(p.chunk_kb, p.kb_per_split));
+    p.smem_bytes = std::max(smem_for(p.bn, p.splits, p.stages), tmem_bound_smem(p.bn));
+    if (p.smem_bytes > kSmemLimit) return false;
+    if (p.splits > 1 && max_active_clusters(p.bn, p.splits, p.smem_bytes) <= 0) return false;
+    return true;
+}
+
 GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms) {
     GemmPlan best;
     double best_t = 1e300;
     const int m_tiles = (M + kBM - 1) / kBM;
     const int total_kb = (K + kBK - 1) / kBK;
+    bool measured = false;
+    // ADAI_B200_GEMM_PLANS="N:K:bn:splits:stages:chunk,..." replaces table entries (plan tuning).
+    if (m_tiles == 1) {
+        if (const char* env = std::getenv("ADAI_B200_GEMM_PLANS")) {
+            const char* q = env;
+            while (*q && !measured) {
+                MeasuredPlan mp{};
+                int used = 0;
+                if (std::sscanf(q, "%d:%d:%d:%d:%d:%d%n", &mp.n, &mp.k, &mp.bn, &mp.splits,
+                                &mp.stages, &mp.chunk_kb, &used) != 6)
+                    break;
+                q += used;
+                if (*q == ',') ++q;
+                if (mp.n != N || mp.k != K || kernel_for(mp.bn, kEpiSetStore) == nullptr) continue;
+                GemmPlan p;
+                p.bn = mp.bn;
+                p.splits = mp.splits;
+                p.stages = mp.stages;
+                p.chunk_kb = mp.chunk_kb;
+                if (complete_plan(p, M, N, K)) {
+                    best = p;
+                    measured = true;
+                }
+            }
+        }
+    }
+    if (m_tiles == 1 && !measured) {
+        for (const MeasuredPlan& mp : kMeasuredPlans) {
+            if (mp.n != N || mp.k != K) continue;
+            GemmPlan p;
+            p.bn = mp.bn;
+            p.splits = mp.splits;
+            p.stages = mp.stages;
+            p.chunk_kb = mp.chunk_kb;
+            if (complete_plan(p, M, N, K)) {
+                best = p;
+                measured = true;
+            }
+            break;
+        }
+    }
     const int n16 = (N + 15) / 16 * 16;
     for (int bn : kTileWidths) {
+        if (measured) break;
         if (bn > n16 && bn != kTileWidths[0]) {
             bool narrower_covers = false;
             for (int b2 : kTileWidths)
@@ -714,24 +812,21 @@ GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms) {
             }
         }
     }
-    // promotion chunk: one 32-wide K block per chunk for short K-slices, two for long ones
-    best.chunk_kb = best.kb_per_split > 16 ? 2 : 1;
-    // Keep (CTAs resident per SM) x (TMEM columns per CTA) <= 512: pad the shared-memory request
-    // so that no more CTAs fit on an SM than its tensor memory can hold at once.
-    const uint32_t cols = tmem_cols_for(best.bn);
-    const size_t max_ctas = 512 / cols;
-    const size_t sm_bytes = 228 * 1024;
-    const size_t min_smem = sm_bytes / (max_ctas + 1) + 1;  // max_ctas + 1 CTAs must not fit
-    if (best.smem_bytes < min_smem) best.smem_bytes = min_smem;
+    // Promotion chunk: the accumulators move to fp32 registers after every 4 K blocks (128 k, 16
+    // MMA steps; 8 blocks in some measured plans). The tensor core's accumulation into TMEM does
+    // not round to nearest, so its error grows with the steps between promotions; 16-32 steps
+    // keep it at the size of the fp32 in-order CPU product's own rounding, while each promotion
+    // costs a TMEM round trip that stalls the MMA issue (one-block chunks measured up to ~25%
+    // slower per K block).
+    if (!measured) best.chunk_kb = std::min(best.kb_per_split, 4);
+    best.smem_bytes = std::max(best.smem_bytes, tmem_bound_smem(best.bn));
     (void)flags;
     return best;
 }
 
 size_t gemm_ws_floats(const GemmPlan&) { return 0; }
 
-size_t gemm_arg_entries(const GemmPlan& p) {
-    return static_cast<size_t>(p.m_tiles) * kBM * p.n_tiles;
-}
+size_t gemm_arg_rows(const GemmPlan& p) { return static_cast<size_t>(p.m_tiles) * kBM; }
 
 int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& epi,
                 const GemmPlan& plan, const GemmScratch& scratch, int* err, cudaStream_t st) {
@@ -747,7 +842,8 @@ int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e
         plan.smem_bytes < smem_for(plan.bn, plan.splits, plan.stages))
         return cudaErrorInvalidValue;
     if ((epi.flags & kEpiArgmax) &&
-        (scratch.arg_val == nullptr || scratch.arg_entries < gemm_arg_entries(plan) ||
+        (scratch.arg_key == nullptr || scratch.arg_nf == nullptr ||
+         scratch.arg_rows < gemm_arg_rows(plan) ||
          scratch.n_tickets < plan.m_tiles || epi.next_ids == nullptr))
         return cudaErrorInvalidValue;
     if ((epi.flags & kEpiKvScatter) &&
@@ -776,8 +872,8 @@ int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e
     p.tmem_cols = tmem_cols_for(plan.bn);
     p.epi = epi;
     p.tickets = scratch.tickets;
-    p.arg_val = scratch.arg_val;
-    p.arg_idx = scratch.arg_idx;
+    p.arg_key = scratch.arg_key;
+    p.arg_nf = scratch.arg_nf;
     p.err = err;
 
     cudaLaunchConfig_t cfg{};

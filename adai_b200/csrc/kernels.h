@@ -110,14 +110,17 @@ struct GemmScratch {
     size_t ws_floats = 0;
     int* tickets = nullptr;
     int n_tickets = 0;
-    float* arg_val = nullptr;
-    int* arg_idx = nullptr;
-    size_t arg_entries = 0;
+    // LM-head argmax: per output row the running first maximum as one 64-bit key (the value's
+    // order-preserving bits above the complemented column) and a non-finite flag. Both start at
+    // zero; the last CTA of each row block reads them back and leaves them at zero.
+    unsigned long long* arg_key = nullptr;
+    int* arg_nf = nullptr;
+    size_t arg_rows = 0;
 };
 
 GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms);
 size_t gemm_ws_floats(const GemmPlan& p);
-size_t gemm_arg_entries(const GemmPlan& p);
+size_t gemm_arg_rows(const GemmPlan& p);
 
 // Encodes (or reuses) the tensor maps and launches. Returns a cudaError_t-style code: 0 ok,
 // cudaErrorInvalidValue for shapes the kernel cannot take.

@@ -122,6 +122,7 @@ def test_mid_model_lockstep(port):
         srcs = make_sources(MID, 4, (256, 256), 1)
         kv = c.kv_arena(4, 16, 256)
         worst, mism = lockstep(kv, MID, port.model(MID, w), [0, 1, 2, 3], srcs, 12)
+        print(f"mid lockstep: worst tolerance ratio {worst:.4f}")
         assert worst <= 1.0, worst
         assert all(tie for _, _, tie in mism), mism
         kv.close()
@@ -136,6 +137,7 @@ def test_large_model_lockstep(port):
         srcs = make_sources(LARGE, 2, (128, 300), 2)
         kv = c.kv_arena(2, 8, 1024)
         worst, mism = lockstep(kv, LARGE, port.model(LARGE, w), [0, 1], srcs, 4)
+        print(f"large lockstep: worst tolerance ratio {worst:.4f}")
         assert worst <= 1.0, worst
         assert all(tie for _, _, tie in mism), mism
         kv.close()
@@ -162,3 +164,41 @@ def test_errors_follow_reference_exceptions(ctx, tiny):
     kv.reset(0)
     assert kv.length(0) == (0, 0)
     kv.close()
+
+
+def test_lm_head_argmax_first_maximum_and_nonfinite():
+    """The fused LM-head argmax returns the first maximum (TextGenerator::argmax's strict `>`,
+    src/TextGenerator.cpp:151-153) when equal maxima sit in the same N tile and in other tiles,
+    and a NaN or +inf logit, or a row of -inf, fails the step as next_logits throws
+    (src/TextGenerator.cpp:177-206)."""
+    from adai_b200.api import NonFiniteLogits
+    srcs = make_sources(TINY, 3, (5, 20), 9)
+    base = make_weights(TINY, 5, affine=True)
+    with Context(0) as c:
+        def run(weights):
+            c.upload(TINY, weights)
+            kv = c.kv_arena(3, 4, 32)
+            kv.encode([0, 1, 2], srcs)
+            return kv
+        w = [a.copy() for a in base]
+        hw, hb = w[-2], w[-1]                  # head.w [D, V], head.b [V]
+        for col in (9, 4000, 4095):            # same tile as 5, later tiles, the last column
+            hw[:, col] = hw[:, 5]
+        hb[[5, 9, 4000, 4095]] = 60.0
+        kv = run(w)
+        nxt, lg = kv.decode_step([0, 1, 2], [BOS] * 3, want_logits=True)
+        assert (lg[:, 5] == lg[:, 9]).all() and (lg[:, 5] == lg[:, 4000]).all()
+        assert (lg[:, 5] == lg[:, 4095]).all()
+        assert nxt.tolist() == [5, 5, 5]
+        assert (kv.generate([0, 1, 2], [5] * 3, 3) == 5).all()
+        kv.close()
+        for bad in ("nan", "inf", "all-neg-inf"):
+            w = [a.copy() for a in base]
+            if bad == "all-neg-inf":
+                w[-1][:] = -np.inf
+            else:
+                w[-1][7] = float(bad)
+            kv = run(w)
+            with pytest.raises(NonFiniteLogits):
+                kv.decode_step([0, 1, 2], [BOS] * 3)
+            kv.close()
