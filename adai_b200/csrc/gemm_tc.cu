@@ -213,14 +213,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
     const int S = p.splits;
     const int rows_per = p.rows_per;  // 128 / S: output rows each cluster rank finishes
     const size_t pipe_bytes = static_cast<size_t>(stages) * stage_bytes;
-    // Partial tile of this CTA, [128 rows][BN] fp32 with float4 columns XOR-swizzled by (row & 7)
-    // (conflict-free row writes and column reads); it reuses the pipeline buffers once the
-    // mainloop is over. With S > 1 a dedicated receive buffer holds the peers' partials of this
-    // rank's rows: [S slots][rows_per][BN], same swizzle (rows_per is a multiple of 8).
+    // Once the mainloop is over the pipeline buffers hold, from their start: this CTA's partial
+    // tile, [128 rows][BN] fp32 with float4 columns XOR-swizzled by (row & 7) (conflict-free row
+    // writes and column reads), then with S > 1 the peers' partials of this rank's rows,
+    // [S slots][rows_per][BN], same swizzle (rows_per is a multiple of 8). Peers write there
+    // only after the cluster barrier that follows this CTA's last pipeline use.
+    constexpr size_t stage_tile_bytes = static_cast<size_t>(kBM) * BN * 4;
     uint8_t* stage_out = smem;
-    uint8_t* recv = smem + pipe_bytes;
+    uint8_t* recv = smem + stage_tile_bytes;
     const size_t recv_bytes = (S > 1) ? static_cast<size_t>(S) * rows_per * BN * 4 : 0;
-    uint64_t* full_bar = reinterpret_cast<uint64_t*>(recv + recv_bytes);
+    const size_t region_bytes = max(pipe_bytes, stage_tile_bytes + recv_bytes);
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + region_bytes);
     uint64_t* empty_bar = full_bar + stages;
     uint64_t* tfull_bar = empty_bar + stages;  // [2] chunk accumulated in TMEM buffer b
     uint64_t* tempty_bar = tfull_bar + 2;      // [2] TMEM buffer b drained by the epilogue
@@ -265,8 +268,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
     }
     __syncthreads();
     tc_fence_after();
-    // This CTA's barriers are initialised: peers may send to it once they pass the wait below.
-    if (S > 1) cluster_arrive_all();
     // The next kernel in the stream may begin its own prologue (it waits before touching data).
     pdl_trigger();
     const uint32_t tmem_base = *tmem_slot;
@@ -404,7 +405,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
         tmem_dealloc(tmem_base, p.tmem_cols);
     }
     if (S > 1) {
-        cluster_wait_all();  // every peer's receive barrier is initialised
+        // This CTA's pipeline is drained and its receive barrier initialised: peers may write
+        // into its buffers once every CTA of the cluster has passed this point.
+        cluster_arrive_all();
+        cluster_wait_all();
         if (threadIdx.x == 0) {
             // rows [o*rows_per, (o+1)*rows_per) of this partial go to rank o, slot `rank`
             const uint32_t bytes = static_cast<uint32_t>(rows_per * BN * 4);
@@ -645,8 +649,10 @@ int max_active_clusters(int bn, int s, size_t smem) {
     return n;
 }
 
+// The pipeline buffers, reused after the mainloop for the partial tile and the peers' partials.
 size_t smem_for(int bn, int s, int stages) {
-    return stages * stage_bytes_for(bn) + recv_bytes_for(bn, s) + kSmemReserve;
+    const size_t after = static_cast<size_t>(kBM) * bn * 4 + recv_bytes_for(bn, s);
+    return std::max(stages * stage_bytes_for(bn), after) + kSmemReserve;
 }
 
 }  // namespace
@@ -674,10 +680,10 @@ struct MeasuredPlan {
 };
 constexpr MeasuredPlan kMeasuredPlans[] = {
     // d_model 1024, d_ff 4096, vocab 32000
-    {3072, 1024, 128, 4, 2, 8},
+    {3072, 1024, 128, 4, 3, 8},
     {1024, 1024, 32, 4, 4, 8},
-    {4096, 1024, 128, 4, 2, 8},
-    {1024, 4096, 128, 8, 2, 8},
+    {4096, 1024, 128, 4, 3, 8},
+    {1024, 4096, 128, 8, 3, 8},
     {32000, 1024, 128, 1, 3, 8},
     // d_model 512, d_ff 2048, vocab 16000
     {1536, 512, 64, 4, 2, 4},
@@ -775,9 +781,8 @@ GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms) {
             if ((total_kb + kbc - 1) / kbc != s) continue;
             if (s > 1 && (kBM % s) != 0) continue;  // whole rows per rank
             const size_t sb = stage_bytes_for(bn);
-            const size_t recv = recv_bytes_for(bn, s);
-            if (recv + sb + kSmemReserve > kSmemLimit) continue;
-            int stages = static_cast<int>((kSmemLimit - kSmemReserve - recv) / sb);
+            if (smem_for(bn, s, 1) > kSmemLimit) continue;
+            int stages = static_cast<int>((kSmemLimit - kSmemReserve) / sb);
             stages = std::max(1, std::min({stages, 8, kbc}));
             const size_t smem = smem_for(bn, s, stages);
             const long long ctas = static_cast<long long>(tiles) * s;

@@ -271,19 +271,16 @@ def main():
         if dist is not None:
             dist.barrier()
 
-    def reduce_max(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     from adai_b200 import Context
+    from adai_b200.parallel import max_over_ranks, shard_ranges
+    reduce_max = max_over_ranks
 
     cfg = wl.model
     B, K, W = wl.batch, args.steps, args.warmup
     weights = make_weights(cfg, seed=0)
-    srcs = make_sources(cfg, B, wl.src_len, seed=rank)   # this rank's shard of the batch
+    # the global batch (B sequences per GPU) and this rank's contiguous shard of it
+    lo, hi = shard_ranges(B * world, world)[rank]
+    srcs = make_sources(cfg, B * world, wl.src_len, seed=0)[lo:hi]
     ctx = Context(local)
     ctx.upload(cfg, weights)
     self_cap = max(W, K) + args.profile_steps + 8
