@@ -55,6 +55,17 @@ def peaks():
                 source="fallback")
 
 
+def dram_traffic(workload: str, kernel_class: str):
+    """DRAM bytes per launch of a kernel class, from the ncu capture summarised under profiles/
+    (a benchmark run cannot read hardware counters itself); (None, None) if not captured."""
+    p = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    try:
+        d = json.load(open(p))[workload]
+        return float(d[kernel_class]), d.get("source")
+    except (OSError, KeyError, ValueError):
+        return None, None
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -349,9 +360,12 @@ def main():
             peak = pk["hbm_gbs"]
             achieved = d["bytes"] / d["launches"] / (launch_ms / 1000.0) / 1e9
             roof = {"bound": "hbm", "unit": "GB/s", "peak_note": f"{pk['source']} hbm_gbs"}
+        traffic, tsrc = dram_traffic(wl.name, dom)
         roof.update({"kernel": dom, "achieved": achieved, "peak": peak,
-                     "frac": achieved / peak, "traffic": None,
+                     "frac": achieved / peak, "traffic": traffic,
                      "launch_ms": launch_ms})
+        if tsrc:
+            roof["traffic_source"] = tsrc
         breakdown = {k: {"share": v["ms"] / total_ms,
                          "ms_per_step": v["ms"] / args.profile_steps,
                          "launches_per_step": v["launches"] // args.profile_steps,

@@ -48,7 +48,7 @@ typedef struct adai_b200_weight adai_b200_weight;
 typedef struct {
     int vocab;
     int d_model;
-    int n_heads;    /* d_model / n_heads must be 64 */
+    int n_heads;    /* d_model / n_heads must be 32 or 64 */
     int d_ff;
     int enc_layers;
     int dec_layers;
