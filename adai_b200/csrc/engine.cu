@@ -1388,6 +1388,10 @@ int adai_b200_decode_attention(adai_b200_ctx* c, int B, int H, int head_dim, int
             fail(ADAI_B200_ERR_INVALID_ARGUMENT, "head_dim must be 32 or 64");
         if ((k_new == nullptr) != (v_new == nullptr))
             fail(ADAI_B200_ERR_INVALID_ARGUMENT, "k_new and v_new must both be given or both be null");
+        for (const void* p : {(const void*)q, (const void*)k_new, (const void*)v_new,
+                              (const void*)k_cache, (const void*)v_cache, (const void*)out})
+            if (reinterpret_cast<uintptr_t>(p) % 16)
+                fail(ADAI_B200_ERR_INVALID_ARGUMENT, "attention buffers must be 16-byte aligned");
         const int add = k_new ? 1 : 0;
         if (max_len < 0 || max_len + add > capacity)
             fail(ADAI_B200_ERR_OUT_OF_RANGE, "max_len exceeds the cache capacity");
@@ -1548,6 +1552,10 @@ int adai_b200_decode_attention_static(adai_b200_ctx* c, int B, int H, int head_d
             fail(ADAI_B200_ERR_INVALID_ARGUMENT, "head_dim must be 32 or 64");
         if ((k_new == nullptr) != (v_new == nullptr))
             fail(ADAI_B200_ERR_INVALID_ARGUMENT, "k_new and v_new must both be given or both be null");
+        for (const void* p : {(const void*)q, (const void*)k_new, (const void*)v_new,
+                              (const void*)k_cache, (const void*)v_cache, (const void*)out})
+            if (reinterpret_cast<uintptr_t>(p) % 16)
+                fail(ADAI_B200_ERR_INVALID_ARGUMENT, "attention buffers must be 16-byte aligned");
         const int add = k_new ? 1 : 0;
         if (max_len < 0 || max_len + add > capacity)
             fail(ADAI_B200_ERR_OUT_OF_RANGE, "max_len exceeds the cache capacity");

@@ -95,20 +95,6 @@ struct ArgState {
 
 __device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
 
-__device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
-    float4 v;
-    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(addr));
-    return v;
-}
-
-__device__ __forceinline__ void st_shared_f4(uint32_t addr, float a, float b, float c, float d) {
-    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c),
-                 "f"(d)
-                 : "memory");
-}
-
 // Epilogue on 4 consecutive output columns [col, col+4) of one row (col % 4 == 0, col < N).
 template <int EPI>
 __device__ __forceinline__ void epilogue4(const GemmKParams& p, int row, int col, float4 acc,

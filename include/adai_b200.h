@@ -156,7 +156,8 @@ ADAI_B200_API int adai_b200_sgemm_prepared(adai_b200_ctx* ctx, int m, const floa
  * (MultiHeadAttention::forward_with_cache, src/MultiHeadAttention.cpp:278-395, per-head math
  * :336-367; KVCache::append, src/KVCache.hpp:99-128) ----
  * B sequences, H heads of width head_dim (32 or 64), D = H * head_dim. Cache layout
- * [B][H][capacity][head_dim] (K and V). All pointers are device pointers. lens[b] rows are cached
+ * [B][H][capacity][head_dim] (K and V). All pointers are 16-byte aligned device pointers (rows
+ * are read and written as float4). lens[b] rows are cached
  * for sequence b (max_len >= every lens[b]); when k_new/v_new [B, D] are non-NULL they are
  * appended at row lens[b] first and attention runs over lens[b] + 1 rows (lens is not updated).
  * q [B, D]; out [B, D]. Asynchronous on the context's stream. */
