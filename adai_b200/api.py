@@ -2,8 +2,9 @@
 
 Error mapping follows the reference's exceptions on the same conditions:
 ADAI_B200_ERR_INVALID_ARGUMENT -> ValueError (std::invalid_argument),
-ADAI_B200_ERR_OUT_OF_RANGE -> IndexError (std::out_of_range), everything else -> RuntimeError
-(std::runtime_error), with DeviceTimeout / NonFiniteLogits / NoDevice as subclasses.
+ADAI_B200_ERR_OUT_OF_RANGE -> IndexError (std::out_of_range), ADAI_B200_ERR_IO -> OSError,
+everything else -> RuntimeError (std::runtime_error), with DeviceTimeout / NonFiniteLogits /
+NoDevice as subclasses.
 
 There is no CPU fallback: if the library is missing, `load()` raises.
 """
@@ -19,7 +20,7 @@ from .config import ModelConfig
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libadai_b200.so")
 
-OK, INVALID, OUT_OF_RANGE, CUDA, TIMEOUT, NONFINITE, STATE, NO_DEVICE = range(8)
+OK, INVALID, OUT_OF_RANGE, CUDA, TIMEOUT, NONFINITE, STATE, NO_DEVICE, IO = range(9)
 
 
 class AdaiError(RuntimeError):
@@ -50,7 +51,8 @@ EXPORTS = [
     "adai_b200_decode_step", "adai_b200_generate", "adai_b200_sgemm", "adai_b200_weight_create",
     "adai_b200_weight_destroy", "adai_b200_sgemm_prepared", "adai_b200_decode_attention",
     "adai_b200_layernorm", "adai_b200_ctx_last_timing", "adai_b200_profile_step",
-    "adai_b200_kv_clear_self", "adai_b200_decode_attention_static",
+    "adai_b200_kv_clear_self", "adai_b200_decode_attention_static", "adai_b200_checkpoint_config",
+    "adai_b200_checkpoint_read", "adai_b200_model_load",
 ]
 
 # Kernel classes of adai_b200_profile_step (adai_b200_kernel_class).
@@ -89,6 +91,9 @@ def load() -> C.CDLL:
     lib.adai_b200_ctx_stream.restype = _vp
     lib.adai_b200_model_tensor_count.argtypes = [C.POINTER(ModelDesc)]
     lib.adai_b200_model_upload.argtypes = [_vp, C.POINTER(ModelDesc), C.POINTER(_vp), _vp]
+    lib.adai_b200_checkpoint_config.argtypes = [C.c_char_p, C.POINTER(ModelDesc)]
+    lib.adai_b200_checkpoint_read.argtypes = [C.c_char_p, C.POINTER(ModelDesc), C.POINTER(_vp)]
+    lib.adai_b200_model_load.argtypes = [_vp, C.c_char_p, C.POINTER(ModelDesc)]
     lib.adai_b200_kv_create.argtypes = [_vp, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]
     lib.adai_b200_kv_destroy.argtypes = [_vp, _vp]
     lib.adai_b200_kv_reset.argtypes = [_vp, _vp, C.c_int]
@@ -128,7 +133,28 @@ def check(rc: int) -> None:
         raise NoDevice(msg)
     if rc == STATE:
         raise StateError(msg)
+    if rc == IO:
+        raise OSError(msg)
     raise AdaiError(msg)
+
+
+def checkpoint_config(directory: str) -> ModelConfig:
+    """The model shape of a SafeTensors checkpoint directory (host only)."""
+    d = ModelDesc()
+    check(load().adai_b200_checkpoint_config(os.fsencode(directory), C.byref(d)))
+    return ModelConfig(d.vocab, d.d_model, d.n_heads, d.d_ff, d.enc_layers, d.dec_layers,
+                       d.max_seq)
+
+
+def read_checkpoint(directory: str, cfg: ModelConfig | None = None) -> list[np.ndarray]:
+    """The tensors of a SafeTensors checkpoint in the model-upload order and layouts, read by
+    the library's own reader (host only)."""
+    from .synth import tensor_specs
+    cfg = cfg or checkpoint_config(directory)
+    out = [np.empty(shape, np.float32) for _, shape in tensor_specs(cfg)]
+    arr = (_vp * len(out))(*[o.ctypes.data for o in out])
+    check(load().adai_b200_checkpoint_read(os.fsencode(directory), C.byref(ModelDesc.of(cfg)), arr))
+    return out
 
 
 def _i32(a) -> np.ndarray:
@@ -190,6 +216,14 @@ class Context:
         pe = None if pe_table is None else np.ascontiguousarray(pe_table, np.float32)
         check(self.lib.adai_b200_model_upload(self.h, C.byref(desc), arr, _ptr(pe)))
         self.cfg = cfg
+
+    def load(self, directory: str, expect: ModelConfig | None = None) -> ModelConfig:
+        """Loads a SafeTensors checkpoint directory (config.json + model.safetensors, the
+        reference's ModelSerializer layout); with `expect`, its shape must match."""
+        exp = C.byref(ModelDesc.of(expect)) if expect is not None else None
+        check(self.lib.adai_b200_model_load(self.h, os.fsencode(directory), exp))
+        self.cfg = checkpoint_config(directory)
+        return self.cfg
 
     def kv_arena(self, max_slots: int, self_capacity: int, cross_capacity: int) -> "KVArena":
         return KVArena(self, max_slots, self_capacity, cross_capacity)

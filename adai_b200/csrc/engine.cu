@@ -25,6 +25,7 @@
 
 #include "../../include/adai_b200.h"
 #include "common.cuh"
+#include "checkpoint.h"
 #include "kernels.h"
 
 using namespace adai_b200;
@@ -65,6 +66,12 @@ int guarded(Fn&& fn) {
     } catch (const std::bad_alloc&) {
         g_last_error = "host allocation failed";
         return ADAI_B200_ERR_CUDA;
+    } catch (const CheckpointIoError& e) {
+        g_last_error = e.what();
+        return ADAI_B200_ERR_IO;
+    } catch (const std::invalid_argument& e) {
+        g_last_error = e.what();
+        return ADAI_B200_ERR_INVALID_ARGUMENT;
     } catch (const std::exception& e) {
         g_last_error = e.what();
         return ADAI_B200_ERR_CUDA;
@@ -949,6 +956,52 @@ int adai_b200_model_upload(adai_b200_ctx* c, const adai_b200_model_desc* d,
         }
         c->dfree(staging);
         c->model = std::move(m);
+    });
+}
+
+int adai_b200_checkpoint_config(const char* dir, adai_b200_model_desc* out) {
+    return guarded([&] {
+        if (!dir || !out) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null argument");
+        *out = read_checkpoint_config(dir);
+    });
+}
+
+int adai_b200_checkpoint_read(const char* dir, const adai_b200_model_desc* d, float* const* t) {
+    return guarded([&] {
+        if (!dir || !t) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null argument");
+        validate_desc(d);
+        const int n = tensor_count(d);
+        std::vector<float*> out(t, t + n);
+        for (int i = 0; i < n; ++i)
+            if (!out[i]) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "tensor " + std::to_string(i) + " is null");
+        read_checkpoint_tensors(dir, *d, out);
+    });
+}
+
+int adai_b200_model_load(adai_b200_ctx* c, const char* dir, const adai_b200_model_desc* expect) {
+    return guarded([&] {
+        check_ctx(c);
+        if (!dir) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null checkpoint directory");
+        const adai_b200_model_desc d = read_checkpoint_config(dir);
+        if (expect && std::memcmp(expect, &d, sizeof d) != 0)
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT,
+                 "architecture mismatch between " + std::string(dir) + "/config.json (vocab " +
+                     std::to_string(d.vocab) + ", d_model " + std::to_string(d.d_model) + ", heads " +
+                     std::to_string(d.n_heads) + ", d_ff " + std::to_string(d.d_ff) + ", layers " +
+                     std::to_string(d.enc_layers) + "+" + std::to_string(d.dec_layers) +
+                     ", max_length " + std::to_string(d.max_seq) + ") and the expected model");
+        validate_desc(&d);
+        const std::vector<size_t> sizes = upload_tensor_sizes(d);
+        std::vector<std::vector<float>> host(sizes.size());
+        std::vector<float*> ptr(sizes.size());
+        for (size_t i = 0; i < sizes.size(); ++i) {
+            host[i].resize(sizes[i]);
+            ptr[i] = host[i].data();
+        }
+        read_checkpoint_tensors(dir, d, ptr);
+        std::vector<const float*> cptr(ptr.begin(), ptr.end());
+        const int rc = adai_b200_model_upload(c, &d, cptr.data(), nullptr);
+        if (rc != ADAI_B200_OK) fail(rc, g_last_error);
     });
 }
 

@@ -36,7 +36,8 @@ typedef enum {
     ADAI_B200_ERR_TIMEOUT = 4,          /* a bounded wait expired; the context is marked unusable */
     ADAI_B200_ERR_NONFINITE = 5,        /* NaN/+inf logits (TextGenerator::next_logits throws) */
     ADAI_B200_ERR_STATE = 6,            /* call order (no model, context unusable, ...) */
-    ADAI_B200_ERR_NO_DEVICE = 7         /* no sm_100 device / the tensor-map API is missing */
+    ADAI_B200_ERR_NO_DEVICE = 7,        /* no sm_100 device / the tensor-map API is missing */
+    ADAI_B200_ERR_IO = 8                /* a checkpoint file cannot be opened or read */
 } adai_b200_status;
 
 typedef struct adai_b200_ctx adai_b200_ctx;
@@ -96,6 +97,25 @@ ADAI_B200_API int adai_b200_model_tensor_count(const adai_b200_model_desc* desc)
  * computed on the host. Replaces the previous model, if any. */
 ADAI_B200_API int adai_b200_model_upload(adai_b200_ctx* ctx, const adai_b200_model_desc* desc,
                            const float* const* tensors, const float* pe_table);
+
+/* ---- checkpoints: the reference's SafeTensors directories (ModelSerializer::export_safetensors /
+ * import_safetensors, src/ModelSerializer.cpp:243-391 and :395-579): <dir>/config.json and
+ * <dir>/model.safetensors, T5-style tensor names, projections stored [out, in], F32 ----
+ * Reads the model shape from <dir>/config.json. Host only (no device needed). */
+ADAI_B200_API int adai_b200_checkpoint_config(const char* dir, adai_b200_model_desc* out);
+/* Reads <dir>/model.safetensors into caller buffers, in the order and layouts of
+ * adai_b200_model_upload (projections back to W[in, out]). A file with no
+ * model.decoder.embed_tokens.weight gives the decoder model.shared.weight, and one with no final
+ * LayerNorm gives gamma 1 / beta 0, as the reference's import does. Tensors not used here are
+ * ignored. Host only. Errors: ADAI_B200_ERR_INVALID_ARGUMENT naming the tensor (missing, wrong
+ * shape, dtype other than F32, malformed header), ADAI_B200_ERR_IO (unreadable file). */
+ADAI_B200_API int adai_b200_checkpoint_read(const char* dir, const adai_b200_model_desc* desc,
+                                            float* const* tensors);
+/* adai_b200_checkpoint_config + adai_b200_checkpoint_read + adai_b200_model_upload. When expect
+ * is non-NULL the checkpoint's shape must equal it (the reference's architecture check,
+ * src/ModelSerializer.cpp:410-432), else ADAI_B200_ERR_INVALID_ARGUMENT. */
+ADAI_B200_API int adai_b200_model_load(adai_b200_ctx* ctx, const char* dir,
+                                       const adai_b200_model_desc* expect);
 
 /* ---- KV cache arena (replaces GPUDecoderKVCache, src/gpu/MatrixGPU.hpp:563-623, and the CPU
  * DecoderKVCache, src/KVCache.hpp:155-245) ----

@@ -62,6 +62,12 @@ class Context {
         check(adai_b200_model_upload(ctx_, &d, tensors.data(), pe_table));
         desc_ = d;
     }
+    // A checkpoint directory in the reference's SafeTensors layout (ModelSerializer,
+    // src/ModelSerializer.cpp:243-579); with `expect`, its shape must match.
+    void load(const std::string& dir, const adai_b200_model_desc* expect = nullptr) {
+        check(adai_b200_model_load(ctx_, dir.c_str(), expect));
+        check(adai_b200_checkpoint_config(dir.c_str(), &desc_));
+    }
     void synchronize(double timeout_s = 0.0) { check(adai_b200_ctx_synchronize(ctx_, timeout_s)); }
     const adai_b200_model_desc& desc() const { return desc_; }
     adai_b200_ctx* get() const { return ctx_; }
