@@ -334,7 +334,8 @@ def main():
     # ---- per-kernel device times of a profiled step at mid-generation (roofline) ----
     for s in slots:
         kv.clear_self(int(s))
-    kv.generate(slots, bos, K // 2)
+    if K >= 2:
+        kv.generate(slots, bos, K // 2)
     prof = None
     feed = ids_dev[:, K // 2 - 1] if K >= 2 else bos
     for _ in range(args.profile_steps):

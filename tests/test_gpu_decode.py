@@ -202,3 +202,20 @@ def test_lm_head_argmax_first_maximum_and_nonfinite():
             with pytest.raises(NonFiniteLogits):
                 kv.decode_step([0, 1, 2], [BOS] * 3)
             kv.close()
+
+
+def test_decoding_past_the_positional_table(port):
+    # Past max_seq_length no positional row is added (src/Decoder.cpp:230-242); 20 steps with a
+    # 12-row table, lockstep against the oracle.
+    from adai_b200.config import ModelConfig
+    cfg = ModelConfig(vocab=512, d_model=128, n_heads=2, d_ff=256, enc_layers=1, dec_layers=2,
+                      max_seq=12)
+    with Context(0) as c:
+        w = make_weights(cfg, 8, affine=True)
+        c.upload(cfg, w)
+        srcs = make_sources(cfg, 3, (4, 12), 8)
+        kv = c.kv_arena(3, 24, 12)
+        worst, mism = lockstep(kv, cfg, port.model(cfg, w), [0, 1, 2], srcs, 20)
+        assert worst <= 1.0, worst
+        assert all(tie for _, _, tie in mism), mism
+        kv.close()
