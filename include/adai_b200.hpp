@@ -15,6 +15,7 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "adai_b200.h"
@@ -144,67 +145,87 @@ struct Result {
 };
 
 // BatchedInferenceEngine::process_batch (src/BatchedInferenceEngine.hpp:465-537) with a real
-// batch: every request is encoded, then all of them advance together one stacked decode step at a
-// time; a request leaves the batch at a stop id or at its max_length. A request that cannot be
-// admitted (bad ids, too long) gets its error and the others proceed.
+// batch and continuous admission (the engine's v2 plan: admit and retire sequences between decode
+// steps). Up to max_slots requests decode together, one stacked step at a time. A request leaves
+// at a stop id or at its max_length, and its slot goes to the next waiting request before the next
+// step. A request that cannot be admitted (bad ids, source too long) gets its error, and the
+// others proceed. The tokens of a request do not depend on which requests share its steps.
 class BatchGenerator {
    public:
     explicit BatchGenerator(KVArena& kv) : kv_(kv) {}
 
     std::vector<Result> generate(const std::vector<Request>& reqs) {
         std::vector<Result> out(reqs.size());
-        for (size_t base = 0; base < reqs.size(); base += static_cast<size_t>(kv_.max_slots())) {
-            const size_t end = std::min(reqs.size(), base + static_cast<size_t>(kv_.max_slots()));
-            run_wave(reqs, base, end, out);
+        std::vector<int> free_slots;
+        for (int s = kv_.max_slots() - 1; s >= 0; --s) free_slots.push_back(s);
+        Active act;
+        size_t next = 0;
+        admit(reqs, out, next, free_slots, act);
+        while (!act.slots.empty()) {
+            const std::vector<int> ids = kv_.decode_step(act.slots, act.feed);
+            Active keep;
+            for (size_t j = 0; j < act.slots.size(); ++j) {
+                const Request& rq = reqs[act.owner[j]];
+                const bool stop = std::find(rq.stop_ids.begin(), rq.stop_ids.end(), ids[j]) !=
+                                  rq.stop_ids.end();
+                out[act.owner[j]].tokens.push_back(ids[j]);
+                if (!stop && act.remaining[j] > 1)
+                    keep.add(act.slots[j], ids[j], act.remaining[j] - 1, act.owner[j]);
+                else
+                    free_slots.push_back(act.slots[j]);
+            }
+            act = std::move(keep);
+            admit(reqs, out, next, free_slots, act);
         }
         return out;
     }
 
    private:
-    void run_wave(const std::vector<Request>& reqs, size_t base, size_t end, std::vector<Result>& out) {
-        std::vector<int> slots, feed;
+    struct Active {
+        std::vector<int> slots, feed, remaining;
         std::vector<size_t> owner;
-        for (size_t i = base; i < end; ++i) {
-            const int slot = static_cast<int>(i - base);
-            try {
-                kv_.encode({slot}, {reqs[i].source});
-                out[i].tokens.push_back(reqs[i].bos);
-                slots.push_back(slot);
-                feed.push_back(reqs[i].bos);
-                owner.push_back(i);
-            } catch (const std::exception& e) {
-                out[i].error = e.what();
-            }
+        void add(int slot, int id, int left, size_t who) {
+            slots.push_back(slot);
+            feed.push_back(id);
+            remaining.push_back(left);
+            owner.push_back(who);
         }
-        std::vector<int> remaining;
-        for (size_t j = 0; j < owner.size(); ++j) remaining.push_back(reqs[owner[j]].max_length);
-        for (size_t j = slots.size(); j-- > 0;) {
-            if (remaining[j] > 0) continue;
-            slots.erase(slots.begin() + static_cast<long>(j));
-            feed.erase(feed.begin() + static_cast<long>(j));
-            owner.erase(owner.begin() + static_cast<long>(j));
-            remaining.erase(remaining.begin() + static_cast<long>(j));
+    };
+
+    // Encodes waiting requests into free slots: all of them in one call, or one by one when the
+    // joint call fails, so that a bad request does not hold up the others.
+    void admit(const std::vector<Request>& reqs, std::vector<Result>& out, size_t& next,
+               std::vector<int>& free_slots, Active& act) {
+        std::vector<int> slots;
+        std::vector<size_t> who;
+        while (!free_slots.empty() && next < reqs.size()) {
+            slots.push_back(free_slots.back());
+            free_slots.pop_back();
+            who.push_back(next++);
         }
-        while (!slots.empty()) {
-            const std::vector<int> next = kv_.decode_step(slots, feed);
-            std::vector<int> s2, f2, r2;
-            std::vector<size_t> o2;
+        if (slots.empty()) return;
+        std::vector<std::vector<int>> sources;
+        for (size_t i : who) sources.push_back(reqs[i].source);
+        std::vector<bool> ok(slots.size(), true);
+        try {
+            kv_.encode(slots, sources);
+        } catch (const std::exception&) {
             for (size_t j = 0; j < slots.size(); ++j) {
-                const Request& rq = reqs[owner[j]];
-                const bool stop = std::find(rq.stop_ids.begin(), rq.stop_ids.end(), next[j]) !=
-                                  rq.stop_ids.end();
-                out[owner[j]].tokens.push_back(next[j]);
-                if (!stop && remaining[j] > 1) {
-                    s2.push_back(slots[j]);
-                    f2.push_back(next[j]);
-                    r2.push_back(remaining[j] - 1);
-                    o2.push_back(owner[j]);
+                try {
+                    kv_.encode({slots[j]}, {sources[j]});
+                } catch (const std::exception& e) {
+                    out[who[j]].error = e.what();
+                    ok[j] = false;
                 }
             }
-            slots.swap(s2);
-            feed.swap(f2);
-            remaining.swap(r2);
-            owner.swap(o2);
+        }
+        for (size_t j = 0; j < slots.size(); ++j) {
+            const Request& rq = reqs[who[j]];
+            if (ok[j]) out[who[j]].tokens.push_back(rq.bos);
+            if (ok[j] && rq.max_length > 0)
+                act.add(slots[j], rq.bos, rq.max_length, who[j]);
+            else
+                free_slots.push_back(slots[j]);
         }
     }
 
