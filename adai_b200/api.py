@@ -52,7 +52,9 @@ EXPORTS = [
     "adai_b200_weight_destroy", "adai_b200_sgemm_prepared", "adai_b200_decode_attention",
     "adai_b200_layernorm", "adai_b200_ctx_last_timing", "adai_b200_profile_step",
     "adai_b200_kv_clear_self", "adai_b200_decode_attention_static", "adai_b200_checkpoint_config",
-    "adai_b200_checkpoint_read", "adai_b200_model_load",
+    "adai_b200_checkpoint_read", "adai_b200_model_load", "adai_b200_gemm_strided",
+    "adai_b200_softmax_rows", "adai_b200_layernorm_fwd", "adai_b200_add_row_bias",
+    "adai_b200_activation", "adai_b200_embedding_gather_add_pe", "adai_b200_backend_bind",
 ]
 
 # Kernel classes of adai_b200_profile_step (adai_b200_kernel_class).
@@ -110,6 +112,16 @@ def load() -> C.CDLL:
                                                _vp, _vp, _vp, C.c_int, _vp]
     lib.adai_b200_decode_attention_static.argtypes = lib.adai_b200_decode_attention.argtypes
     lib.adai_b200_layernorm.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int]
+    lib.adai_b200_gemm_strided.argtypes = [_vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
+                                           _vp, C.c_int, _vp, C.c_int, _vp, C.c_int]
+    lib.adai_b200_softmax_rows.argtypes = [_vp, _vp, C.c_int, C.c_int]
+    lib.adai_b200_layernorm_fwd.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int,
+                                            C.c_float]
+    lib.adai_b200_add_row_bias.argtypes = [_vp, _vp, _vp, _vp, C.c_int, C.c_int]
+    lib.adai_b200_activation.argtypes = [_vp, _vp, C.c_int, C.c_int]
+    lib.adai_b200_embedding_gather_add_pe.argtypes = [_vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp,
+                                                      C.c_int, C.c_int, C.c_int]
+    lib.adai_b200_backend_bind.argtypes = [_vp]
     lib.adai_b200_ctx_last_timing.argtypes = [_vp, C.POINTER(C.c_double), _ip]
     lib.adai_b200_profile_step.argtypes = [_vp, _vp, C.c_int, _vp, _vp, C.c_int, _vp, _vp, _vp,
                                            _vp]
@@ -251,6 +263,33 @@ class Context:
 
     def layernorm(self, x, gamma, beta, out, rows, D) -> None:
         check(self.lib.adai_b200_layernorm(self.h, x, gamma, beta, out, rows, D))
+
+    # ---- the reference backend table's decode-path entries (device pointers) ----
+    def gemm_strided(self, trans_a, trans_b, m, n, k, alpha, a, lda, b, ldb, c, ldc) -> None:
+        check(self.lib.adai_b200_gemm_strided(self.h, int(trans_a), int(trans_b), m, n, k, alpha,
+                                              a, lda, b, ldb, c, ldc))
+
+    def softmax_rows(self, data, rows, cols) -> None:
+        check(self.lib.adai_b200_softmax_rows(self.h, data, rows, cols))
+
+    def layernorm_fwd(self, x, y, x_normed, gamma, beta, mean, rstd, rows, cols, eps=1e-5) -> None:
+        check(self.lib.adai_b200_layernorm_fwd(self.h, x, y, x_normed, gamma, beta, mean, rstd,
+                                               rows, cols, eps))
+
+    def add_row_bias(self, m, bias, out, rows, cols) -> None:
+        check(self.lib.adai_b200_add_row_bias(self.h, m, bias, out, rows, cols))
+
+    def activation(self, data, size, kind) -> None:
+        """kind: 0 ReLU, 1 sigmoid, 2 tanh, 3 GELU (tanh form)."""
+        check(self.lib.adai_b200_activation(self.h, data, size, kind))
+
+    def embedding_gather_add_pe(self, table, ids, pe, pe_rows, pos_offset, out, n, d, vocab=0):
+        check(self.lib.adai_b200_embedding_gather_add_pe(self.h, table, ids, pe, pe_rows,
+                                                         pos_offset, out, n, d, vocab))
+
+    def bind_backend(self) -> None:
+        """Makes this context the one the adai::gpu::matrix_*_gpu C++ functions run on."""
+        check(self.lib.adai_b200_backend_bind(self.h))
 
     def last_timing(self) -> tuple[float, int]:
         """(device ms of the last generate() decode loop, kernels launched per step)."""

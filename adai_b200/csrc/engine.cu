@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <limits>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -196,6 +197,8 @@ struct adai_b200_ctx {
     int attn_n_tickets = 0;
     float *op_a_hi = nullptr, *op_a_lo = nullptr;
     size_t op_a_floats = 0;
+    float* op_c = nullptr;  // packed output of op-level GEMMs whose C is not float4-aligned
+    size_t op_c_floats = 0;
     int* h_pin = nullptr;  // pinned staging for ids / slots / lengths
     size_t h_pin_ints = 0;
     std::map<GraphKey, cudaGraphExec_t> graphs;
@@ -1304,26 +1307,33 @@ int adai_b200_generate(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slo
 
 // ---- op level ----------------------------------------------------------------------------------
 namespace {
-__global__ void split_pad_kernel(const float* __restrict__ x, int rows, int k, float* __restrict__ hi,
-                                 float* __restrict__ lo, int kpad, int rows_alloc) {
+// A [m, k] operand of the op-level GEMMs, times alpha, as its tf32 pair in the layout the GEMM
+// streams: [rows_alloc, kpad] row-major, zero padded. op(A)[r][c] is a[r * lda + c], or
+// a[c * lda + r] when trans.
+__global__ void pack_split_a_kernel(const float* __restrict__ a, int lda, int trans, int m, int k,
+                                    float alpha, float* __restrict__ hi, float* __restrict__ lo,
+                                    int kpad, int rows_alloc) {
     const size_t n = static_cast<size_t>(rows_alloc) * kpad;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
         const int r = static_cast<int>(i / kpad), cc = static_cast<int>(i % kpad);
-        const float v = (r < rows && cc < k) ? x[static_cast<size_t>(r) * k + cc] : 0.f;
+        float v = 0.f;
+        if (r < m && cc < k)
+            v = alpha * (trans ? a[static_cast<size_t>(cc) * lda + r] : a[static_cast<size_t>(r) * lda + cc]);
         float h, l;
         split_tf32(v, h, l);
         hi[i] = h;
         lo[i] = l;
     }
 }
-__global__ void transpose_split_pad_kernel(const float* __restrict__ w, int K, int N, int Kpad,
+// B [k, n] row-major (row stride ldb) -> B^T hi/lo [n, kpad], through a shared-memory tile.
+__global__ void transpose_split_pad_kernel(const float* __restrict__ w, int ldb, int K, int N, int Kpad,
                                            float* __restrict__ hi_t, float* __restrict__ lo_t) {
     __shared__ float tile[32][33];
     const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
         const int k = k0 + i, nn = n0 + threadIdx.x;
-        tile[i][threadIdx.x] = (k < K && nn < N) ? w[static_cast<size_t>(k) * N + nn] : 0.f;
+        tile[i][threadIdx.x] = (k < K && nn < N) ? w[static_cast<size_t>(k) * ldb + nn] : 0.f;
     }
     __syncthreads();
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -1336,9 +1346,28 @@ __global__ void transpose_split_pad_kernel(const float* __restrict__ w, int K, i
         }
     }
 }
+// B stored transposed ([n, k], row stride ldb): already the B^T layout, split and padded.
+__global__ void copy_split_pad_kernel(const float* __restrict__ w, int ldb, int K, int N, int Kpad,
+                                      float* __restrict__ hi_t, float* __restrict__ lo_t) {
+    const size_t total = static_cast<size_t>(N) * Kpad;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int nn = static_cast<int>(i / Kpad), k = static_cast<int>(i % Kpad);
+        const float v = (k < K) ? w[static_cast<size_t>(nn) * ldb + k] : 0.f;
+        float h, l;
+        split_tf32(v, h, l);
+        hi_t[i] = h;
+        lo_t[i] = l;
+    }
+}
 
-adai_b200_weight* prepare_weight(adai_b200_ctx* c, const float* B, int k, int n) {
+int blocks_for(size_t n) { return static_cast<int>(std::min<size_t>((n + 255) / 256, 148 * 16)); }
+
+adai_b200_weight* prepare_weight(adai_b200_ctx* c, const float* B, int k, int n, int ldb = -1,
+                                 bool trans_b = false) {
     if (!B || k <= 0 || n <= 0) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad weight shape");
+    if (ldb < 0) ldb = trans_b ? k : n;
+    if (ldb < (trans_b ? k : n)) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "ldb is smaller than a row of B");
     auto w = std::make_unique<adai_b200_weight>();
     const int kpad = round_up(k, 4);
     const size_t rows = static_cast<size_t>(round_up(n, 256));
@@ -1348,9 +1377,14 @@ adai_b200_weight* prepare_weight(adai_b200_ctx* c, const float* B, int k, int n)
     w->w.N = n;
     w->w.hi = c->dzalloc_t<float>(rows * kpad);
     w->w.lo = c->dzalloc_t<float>(rows * kpad);
-    dim3 grid((n + 31) / 32, (kpad + 31) / 32);
-    transpose_split_pad_kernel<<<grid, dim3(32, 8), 0, c->stream>>>(B, k, n, kpad, w->w.hi, w->w.lo);
-    cuda_ok(cudaGetLastError(), "transpose-split");
+    if (trans_b) {
+        copy_split_pad_kernel<<<blocks_for(static_cast<size_t>(n) * kpad), 256, 0, c->stream>>>(
+            B, ldb, k, n, kpad, w->w.hi, w->w.lo);
+    } else {
+        dim3 grid((n + 31) / 32, (kpad + 31) / 32);
+        transpose_split_pad_kernel<<<grid, dim3(32, 8), 0, c->stream>>>(B, ldb, k, n, kpad, w->w.hi, w->w.lo);
+    }
+    cuda_ok(cudaGetLastError(), "weight split");
     return w.release();
 }
 
@@ -1360,31 +1394,51 @@ void free_weight(adai_b200_ctx* c, adai_b200_weight* w) {
     delete w;
 }
 
-void sgemm_prepared(adai_b200_ctx* c, int m, const float* A, const adai_b200_weight* w, float* C, int k) {
+// C[m, n] (row stride ldc) = alpha op(A) W. The fused epilogue stores float4 rows, so an output
+// that is not 16-byte aligned with ldc % 4 == 0 goes through a packed buffer and a 2-D copy.
+void gemm_run(adai_b200_ctx* c, int m, const float* A, int lda, bool trans_a, float alpha,
+              const adai_b200_weight* w, float* C, int ldc) {
     if (m <= 0 || !A || !C) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad GEMM arguments");
-    const int kpad = w->Kpad;
+    const int k = w->K, n = w->w.N, kpad = w->Kpad;
+    if (lda < (trans_a ? m : k)) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "lda is smaller than a row of A");
+    if (ldc < n) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "ldc is smaller than a row of C");
     const int rows_alloc = round_up(m, 128);
     const size_t need = static_cast<size_t>(rows_alloc) * kpad;
-    if (need > c->op_a_floats) {
+    const bool direct = reinterpret_cast<uintptr_t>(C) % 16 == 0 && ldc % 4 == 0;
+    const int ldp = round_up(n, 4);
+    const size_t need_c = direct ? 0 : static_cast<size_t>(m) * ldp;
+    if (need > c->op_a_floats || need_c > c->op_c_floats) {
         cuda_ok(cudaStreamSynchronize(c->stream), "sync");
-        c->dfree(c->op_a_hi);
-        c->dfree(c->op_a_lo);
-        c->op_a_hi = nullptr;
-        c->op_a_lo = nullptr;
-        c->op_a_floats = 0;
-        c->op_a_hi = c->dalloc_t<float>(need);
-        c->op_a_lo = c->dalloc_t<float>(need);
-        c->op_a_floats = need;
+        if (need > c->op_a_floats) {
+            c->dfree(c->op_a_hi);
+            c->dfree(c->op_a_lo);
+            c->op_a_hi = c->op_a_lo = nullptr;
+            c->op_a_floats = 0;
+            c->op_a_hi = c->dalloc_t<float>(need);
+            c->op_a_lo = c->dalloc_t<float>(need);
+            c->op_a_floats = need;
+        }
+        if (need_c > c->op_c_floats) {
+            c->dfree(c->op_c);
+            c->op_c = nullptr;
+            c->op_c_floats = 0;
+            c->op_c = c->dalloc_t<float>(need_c);
+            c->op_c_floats = need_c;
+        }
     }
-    const size_t n = need;
-    const int blocks = static_cast<int>(std::min<size_t>((n + 255) / 256, 148 * 16));
-    split_pad_kernel<<<blocks, 256, 0, c->stream>>>(A, m, k, c->op_a_hi, c->op_a_lo, kpad, rows_alloc);
+    pack_split_a_kernel<<<blocks_for(need), 256, 0, c->stream>>>(A, lda, trans_a ? 1 : 0, m, k, alpha,
+                                                                 c->op_a_hi, c->op_a_lo, kpad, rows_alloc);
     cuda_ok(cudaGetLastError(), "split");
     GemmEpilogue e;
     e.flags = kEpiStore;
-    e.out = C;
-    e.ldo = w->w.N;
+    e.out = direct ? C : c->op_c;
+    e.ldo = direct ? ldc : ldp;
     c->gemm(acts(c->op_a_hi, c->op_a_lo, kpad, rows_alloc), m, w->w, e);
+    if (!direct)
+        cuda_ok(cudaMemcpy2DAsync(C, static_cast<size_t>(ldc) * sizeof(float), c->op_c,
+                                  static_cast<size_t>(ldp) * sizeof(float), static_cast<size_t>(n) * sizeof(float),
+                                  static_cast<size_t>(m), cudaMemcpyDeviceToDevice, c->stream),
+                "copy out");
 }
 }  // namespace
 
@@ -1409,7 +1463,7 @@ int adai_b200_sgemm_prepared(adai_b200_ctx* c, int m, const float* A, const adai
     return guarded([&] {
         check_ctx(c);
         if (!w) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null weight");
-        sgemm_prepared(c, m, A, w, C, w->K);
+        gemm_run(c, m, A, w->K, false, 1.0f, w, C, w->w.N);
     });
 }
 
@@ -1418,7 +1472,7 @@ int adai_b200_sgemm(adai_b200_ctx* c, int m, int n, int k, const float* A, const
         check_ctx(c);
         adai_b200_weight* w = prepare_weight(c, B, k, n);
         try {
-            sgemm_prepared(c, m, A, w, C, k);
+            gemm_run(c, m, A, k, false, 1.0f, w, C, n);
         } catch (...) {
             cudaStreamSynchronize(c->stream);
             free_weight(c, w);
@@ -1546,6 +1600,90 @@ int adai_b200_layernorm(adai_b200_ctx* c, const float* x, const float* gamma, co
         if (!layernorm_width_supported(D)) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "D must be 128 * {1,2,3,4,6,8,12,16}");
         launch_layernorm(x, D, gamma, beta, out, nullptr, nullptr, rows, D, c->stream);
         cuda_ok(cudaGetLastError(), "layernorm launch");
+    });
+}
+
+// ---- the decode-path entries of the reference backend table (adai::gpu::matrix_*_gpu) ----------
+int adai_b200_gemm_strided(adai_b200_ctx* c, int trans_a, int trans_b, int m, int n, int k,
+                           float alpha, const float* a, int lda, const float* b, int ldb, float* out,
+                           int ldc) {
+    return guarded([&] {
+        check_ctx(c);
+        if (m <= 0 || n <= 0) return;  // nothing to write, as the reference returns early
+        if (!out || ldc < n) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad output of the strided GEMM");
+        if (k <= 0) {  // an empty inner dimension: C = 0
+            cuda_ok(cudaMemset2DAsync(out, static_cast<size_t>(ldc) * sizeof(float), 0,
+                                      static_cast<size_t>(n) * sizeof(float), static_cast<size_t>(m),
+                                      c->stream),
+                    "zero C");
+            return;
+        }
+        if (!a || !b) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null operand");
+        adai_b200_weight* w = prepare_weight(c, b, k, n, ldb, trans_b != 0);
+        try {
+            gemm_run(c, m, a, lda, trans_a != 0, alpha, w, out, ldc);
+        } catch (...) {
+            cudaStreamSynchronize(c->stream);
+            free_weight(c, w);
+            throw;
+        }
+        cuda_ok(cudaStreamSynchronize(c->stream), "sync");
+        free_weight(c, w);
+    });
+}
+
+int adai_b200_softmax_rows(adai_b200_ctx* c, float* data, int rows, int cols) {
+    return guarded([&] {
+        check_ctx(c);
+        if (rows < 0 || cols < 0 || (rows && cols && !data)) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad softmax arguments");
+        launch_softmax_rows(data, rows, cols, c->stream);
+        cuda_ok(cudaGetLastError(), "softmax launch");
+    });
+}
+
+int adai_b200_layernorm_fwd(adai_b200_ctx* c, const float* x, float* y, float* x_normed,
+                            const float* gamma, const float* beta, float* mean, float* rstd,
+                            int rows, int cols, float eps) {
+    return guarded([&] {
+        check_ctx(c);
+        if (rows < 0 || cols <= 0 || (rows && (!x || !y || !gamma || !beta)))
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad LayerNorm arguments");
+        launch_layernorm_rows(x, y, x_normed, gamma, beta, mean, rstd, rows, cols, eps, c->stream);
+        cuda_ok(cudaGetLastError(), "layernorm launch");
+    });
+}
+
+int adai_b200_add_row_bias(adai_b200_ctx* c, const float* m, const float* bias, float* out, int rows,
+                           int cols) {
+    return guarded([&] {
+        check_ctx(c);
+        if (rows < 0 || cols <= 0 || (rows && (!m || !bias || !out)))
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad bias arguments");
+        launch_add_row_bias(m, bias, out, rows, cols, c->stream);
+        cuda_ok(cudaGetLastError(), "bias launch");
+    });
+}
+
+int adai_b200_activation(adai_b200_ctx* c, float* data, int size, int type) {
+    return guarded([&] {
+        check_ctx(c);
+        if (size < 0 || (size && !data)) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad activation arguments");
+        if (type < 0 || type > 3) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "activation type must be 0..3");
+        launch_activation(data, static_cast<size_t>(size), type, c->stream);
+        cuda_ok(cudaGetLastError(), "activation launch");
+    });
+}
+
+int adai_b200_embedding_gather_add_pe(adai_b200_ctx* c, const float* table, const int* ids,
+                                      const float* pe, int pe_rows, int pos_offset, float* out, int n,
+                                      int d, int vocab) {
+    return guarded([&] {
+        check_ctx(c);
+        if (n < 0 || d <= 0 || (n && (!table || !ids || !out)))
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad embedding arguments");
+        launch_embed_pe(table, ids, pe, pe_rows, pos_offset, out, n, d,
+                        vocab > 0 ? vocab : std::numeric_limits<int>::max(), c->d_err, c->stream);
+        cuda_ok(cudaGetLastError(), "embedding launch");
     });
 }
 

@@ -179,6 +179,16 @@ bool attention_head_dim_supported(int head_dim);
 size_t decode_attn_ws_floats(int B, int H, int max_len, int head_dim);
 void launch_decode_attention(const DecodeAttnArgs& a, int* err, cudaStream_t st);
 
+// Row and elementwise operations of the reference backend table (backend_ops.cu).
+void launch_softmax_rows(float* data, int rows, int cols, cudaStream_t st);
+void launch_layernorm_rows(const float* x, float* y, float* xn, const float* g, const float* b,
+                           float* mean, float* rstd, int rows, int cols, float eps, cudaStream_t st);
+void launch_add_row_bias(const float* m, const float* bias, float* out, int rows, int cols,
+                         cudaStream_t st);
+void launch_activation(float* data, size_t n, int type, cudaStream_t st);  // 0 ReLU 1 sigmoid 2 tanh 3 GELU
+void launch_embed_pe(const float* table, const int* ids, const float* pe, int pe_rows, int pos_offset,
+                     float* out, int n, int d, int vocab, int* err, cudaStream_t st);
+
 // Encoder self-attention over ragged sequences: qkv [rows, 3D]; sequence s holds rows
 // [offsets[s], offsets[s] + lens[s]); out split [rows, D].
 void launch_prefill_attention(const float* qkv, int D, int H, const int* offsets, const int* lens,

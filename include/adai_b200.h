@@ -212,6 +212,41 @@ ADAI_B200_API int adai_b200_decode_attention_static(adai_b200_ctx* ctx, int B, i
 ADAI_B200_API int adai_b200_layernorm(adai_b200_ctx* ctx, const float* x, const float* gamma, const float* beta,
                         float* out, int rows, int D);
 
+/* ---- the decode-path entries of the reference GPU backend table (adai::gpu::matrix_*_gpu,
+ * src/gpu/MatrixGPU.hpp:43-201), for callers of that table outside the fused decode step. Device
+ * pointers, row-major, on the context's stream. include/adai_b200_backend.hpp gives them the
+ * reference's own C++ signatures. ---- */
+/* C[m, n] (row stride ldc) = alpha * op(A) * op(B); op(A) is m x k (A stored k x m when trans_a),
+ * op(B) is k x n (B stored n x k when trans_b); beta = 0 (matrix_gemm_strided_gpu,
+ * src/gpu/MatrixGPU.hpp:92-100). 3xTF32 on the tensor cores; waits for completion. */
+ADAI_B200_API int adai_b200_gemm_strided(adai_b200_ctx* ctx, int trans_a, int trans_b, int m, int n,
+                                         int k, float alpha, const float* a, int lda,
+                                         const float* b, int ldb, float* c, int ldc);
+/* In-place row softmax, Activation::softmax_row semantics (src/Activation.cpp:12-31): a row whose
+ * exponentials sum to 0 is left unnormalised (matrix_softmax_rows_gpu). */
+ADAI_B200_API int adai_b200_softmax_rows(adai_b200_ctx* ctx, float* data, int rows, int cols);
+/* y = gamma * (x - mean) * rstd + beta per row, any width; x_normed, mean, rstd may be NULL
+ * (matrix_layer_norm_fwd_gpu, src/gpu/MatrixGPU.hpp:147-149). */
+ADAI_B200_API int adai_b200_layernorm_fwd(adai_b200_ctx* ctx, const float* x, float* y,
+                                          float* x_normed, const float* gamma, const float* beta,
+                                          float* mean, float* rstd, int rows, int cols, float eps);
+/* out[r, c] = m[r, c] + bias[c] (matrix_add_row_bias_gpu). */
+ADAI_B200_API int adai_b200_add_row_bias(adai_b200_ctx* ctx, const float* m, const float* bias,
+                                         float* out, int rows, int cols);
+/* In place: type 0 ReLU, 1 sigmoid, 2 tanh, 3 GELU (tanh form), the ActivationType values of
+ * src/gpu/MatrixGPU.hpp:27 (matrix_apply_activation_gpu). */
+ADAI_B200_API int adai_b200_activation(adai_b200_ctx* ctx, float* data, int size, int type);
+/* out[i, :] = table[ids[i], :] + pe[pos_offset + i, :], no positional row past pe_rows or when pe
+ * is NULL (embedding_gather_add_pe_gpu, src/gpu/MatrixGPU.hpp:182-185). With vocab > 0 an id
+ * outside [0, vocab) is reported by the next synchronisation as ADAI_B200_ERR_OUT_OF_RANGE. */
+ADAI_B200_API int adai_b200_embedding_gather_add_pe(adai_b200_ctx* ctx, const float* table,
+                                                    const int* ids, const float* pe, int pe_rows,
+                                                    int pos_offset, float* out, int n, int d,
+                                                    int vocab);
+/* The context the adai::gpu::matrix_*_gpu functions of include/adai_b200_backend.hpp run on (one
+ * per process, as the reference's GPUManager singleton; NULL unbinds). */
+ADAI_B200_API int adai_b200_backend_bind(adai_b200_ctx* ctx);
+
 /* ---- measurement ----
  * Device time (CUDA events on the context stream, around the graph replays) of the decode loop
  * of the last adai_b200_generate call, and the kernels one replayed step launches. The reference
