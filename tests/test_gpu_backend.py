@@ -166,3 +166,42 @@ def test_reference_signatures_link_and_run(tmp_path):
     r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "all ok" in r.stdout, r.stdout
+
+
+def test_softmax_known_answers(ctx, torch_cuda):
+    # tests/matrixgpu_td003_test.cpp:234-249: [0, 0] -> [0.5, 0.5]; [0, ln 3] -> [0.25, 0.75]
+    torch = torch_cuda
+    d = dev(torch, np.array([[0.0, 0.0], [0.0, np.log(3.0)]], np.float32))
+    torch.cuda.synchronize()
+    ctx.softmax_rows(d.data_ptr(), 2, 2)
+    ctx.synchronize()
+    got = d.cpu().numpy()
+    assert abs(got[0, 0] - 0.5) <= 1e-4 and abs(got[0, 1] - 0.5) <= 1e-4
+    assert abs(got[1, 0] - 0.25) <= 1e-3 and abs(got[1, 1] - 0.75) <= 1e-3
+
+
+def test_strided_gemm_known_answers(ctx, torch_cuda):
+    # tests/matrixgpu_td003_test.cpp:396-446: sin / cos operands viewed inside wider rows, every
+    # transpose combination, against a float64 host product within 1e-4; columns outside the
+    # output view keep their value.
+    torch = torch_cuda
+    m, n, k, a_off, b_off, c_off, alpha = 3, 5, 4, 2, 1, 3, 0.75
+    for trans_a in (False, True):
+        for trans_b in (False, True):
+            a_rows, a_cols = (k, m) if trans_a else (m, k)
+            b_rows, b_cols = (n, k) if trans_b else (k, n)
+            lda, ldb, ldc = a_cols + 4, b_cols + 3, n + 6
+            a = np.sin(0.37 * np.arange(a_rows * lda, dtype=np.float32)).astype(np.float32)
+            b = np.cos(0.23 * np.arange(b_rows * ldb, dtype=np.float32)).astype(np.float32)
+            da, db = dev(torch, a), dev(torch, b)
+            dc = torch.full((m * ldc,), 99.0, device="cuda")
+            torch.cuda.synchronize()
+            ctx.gemm_strided(trans_a, trans_b, m, n, k, alpha, da.data_ptr() + 4 * a_off, lda,
+                             db.data_ptr() + 4 * b_off, ldb, dc.data_ptr() + 4 * c_off, ldc)
+            ctx.synchronize()
+            out = dc.cpu().numpy().reshape(m, ldc)
+            A = a.reshape(a_rows, lda)[:, a_off:a_off + a_cols].astype(np.float64)
+            B = b.reshape(b_rows, ldb)[:, b_off:b_off + b_cols].astype(np.float64)
+            ref = alpha * ((A.T if trans_a else A) @ (B.T if trans_b else B))
+            assert np.all(np.abs(out[:, c_off:c_off + n] - ref) <= 1e-4), (trans_a, trans_b)
+            assert np.all(out[:, :c_off] == 99.0)
