@@ -132,6 +132,10 @@ struct EncBufs {
           *attn_lo = nullptr, *h_hi = nullptr, *h_lo = nullptr, *out = nullptr;
     int *ids = nullptr, *row_slot = nullptr, *row_pos = nullptr, *offsets = nullptr,
         *lens = nullptr;
+    // tensor-core prefill attention: split Q|K|V rows and the transposed V columns
+    float *qkv_hi = nullptr, *qkv_lo = nullptr, *vt_hi = nullptr, *vt_lo = nullptr;
+    int ldv = 0;
+    int *row_vcol = nullptr, *seq_vcol = nullptr;
 };
 
 struct adai_b200_kv {
@@ -499,13 +503,24 @@ void ensure_enc_bufs(adai_b200_ctx* c) {
     e.row_pos = c->dzalloc_t<int>(R);
     e.offsets = c->dzalloc_t<int>(R);
     e.lens = c->dzalloc_t<int>(R);
+    if (prefill_tc_supported(D / m.d.n_heads)) {
+        e.ldv = 2 * R + 32;  // sequences start on 32-column boundaries: at most 31 padding each
+        e.qkv_hi = c->dzalloc_t<float>(R * 3 * D);
+        e.qkv_lo = c->dzalloc_t<float>(R * 3 * D);
+        e.vt_hi = c->dzalloc_t<float>(D * static_cast<size_t>(e.ldv));
+        e.vt_lo = c->dzalloc_t<float>(D * static_cast<size_t>(e.ldv));
+        e.row_vcol = c->dzalloc_t<int>(R);
+        e.seq_vcol = c->dzalloc_t<int>(R);
+    }
 }
 
 void free_enc_bufs(adai_b200_ctx* c) {
     EncBufs& e = c->eb;
     for (void* p : {(void*)e.x, (void*)e.nrm_hi, (void*)e.nrm_lo, (void*)e.qkv, (void*)e.attn_hi,
                     (void*)e.attn_lo, (void*)e.h_hi, (void*)e.h_lo, (void*)e.out, (void*)e.ids,
-                    (void*)e.row_slot, (void*)e.row_pos, (void*)e.offsets, (void*)e.lens})
+                    (void*)e.row_slot, (void*)e.row_pos, (void*)e.offsets, (void*)e.lens,
+                    (void*)e.qkv_hi, (void*)e.qkv_lo, (void*)e.vt_hi, (void*)e.vt_lo,
+                    (void*)e.row_vcol, (void*)e.seq_vcol})
         c->dfree(p);
     e = EncBufs{};
 }
@@ -1141,22 +1156,34 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
             while (i1 < n && rows + src_lens[i1] <= e.rows) rows += src_lens[i1++];
             const int nseq = i1 - i0;
             int max_len = 0;
-            int* pin = c->pinned(static_cast<size_t>(rows) * 3 + 2 * static_cast<size_t>(nseq));
+            int* pin = c->pinned(static_cast<size_t>(rows) * 4 + 3 * static_cast<size_t>(nseq));
             int* p_ids = pin;
             int* p_slot = pin + rows;
             int* p_pos = pin + 2 * rows;
-            int* p_off = pin + 3 * rows;
+            int* p_vcol = pin + 3 * rows;
+            int* p_off = pin + 4 * rows;
             int* p_len = p_off + nseq;
-            int r = 0;
+            int* p_svcol = p_len + nseq;
+            int r = 0, vcol = 0;
             for (int i = i0; i < i1; ++i) {
                 p_off[i - i0] = r;
                 p_len[i - i0] = src_lens[i];
+                p_svcol[i - i0] = vcol;
                 max_len = std::max(max_len, src_lens[i]);
                 for (int t = 0; t < src_lens[i]; ++t, ++r) {
                     p_ids[r] = ids[row_base + r];
                     p_slot[r] = slots[i];
                     p_pos[r] = t;
+                    p_vcol[r] = vcol + t;
                 }
+                vcol = round_up(vcol + src_lens[i], 32);
+            }
+            // The tensor-core attention needs every sequence's transposed V to start on a
+            // 32-column boundary; a chunk of very many short sources may not fit its buffer.
+            const bool tc_attn = e.vt_hi != nullptr && vcol <= e.ldv;
+            if (tc_attn) {
+                cuda_ok(cudaMemcpyAsync(e.row_vcol, p_vcol, rows * sizeof(int), cudaMemcpyHostToDevice, st), "H2D");
+                cuda_ok(cudaMemcpyAsync(e.seq_vcol, p_svcol, nseq * sizeof(int), cudaMemcpyHostToDevice, st), "H2D");
             }
             cuda_ok(cudaMemcpyAsync(e.ids, p_ids, rows * sizeof(int), cudaMemcpyHostToDevice, st), "H2D");
             cuda_ok(cudaMemcpyAsync(e.row_slot, p_slot, rows * sizeof(int), cudaMemcpyHostToDevice, st), "H2D");
@@ -1179,8 +1206,32 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
                 q.out = e.qkv;
                 q.ldo = 3 * D;
                 c->gemm(a_nrm, rows, w.qkv, q);
-                launch_prefill_attention(e.qkv, D, H, e.offsets, e.lens, nseq, max_len, e.attn_hi,
-                                         e.attn_lo, scale, st);
+                if (tc_attn) {
+                    PrefillTcArgs pa;
+                    pa.qkv = e.qkv;
+                    pa.qkv_hi = e.qkv_hi;
+                    pa.qkv_lo = e.qkv_lo;
+                    pa.vt_hi = e.vt_hi;
+                    pa.vt_lo = e.vt_lo;
+                    pa.ldv = e.ldv;
+                    pa.row_vcol = e.row_vcol;
+                    pa.seq_vcol = e.seq_vcol;
+                    pa.offsets = e.offsets;
+                    pa.lens = e.lens;
+                    pa.nseq = nseq;
+                    pa.max_len = max_len;
+                    pa.rows = rows;
+                    pa.D = D;
+                    pa.head_dim = D / H;
+                    pa.out_hi = e.attn_hi;
+                    pa.out_lo = e.attn_lo;
+                    pa.scale = scale;
+                    pa.err = c->d_err;
+                    launch_ok(launch_prefill_attention_tc(pa, st), "prefill attention launch");
+                } else {
+                    launch_prefill_attention(e.qkv, D, H, e.offsets, e.lens, nseq, max_len, e.attn_hi,
+                                             e.attn_lo, scale, st);
+                }
                 GemmEpilogue o;
                 o.flags = kEpiStore | kEpiResid;
                 o.resid = e.x;

@@ -179,6 +179,29 @@ bool attention_head_dim_supported(int head_dim);
 size_t decode_attn_ws_floats(int B, int H, int max_len, int head_dim);
 void launch_decode_attention(const DecodeAttnArgs& a, int* err, cudaStream_t st);
 
+// Encoder self-attention on the tensor cores (prefill_tc.cu). qkv [rows, 3D] fp32 is split into
+// qkv_hi/lo and its V columns transposed into vt_hi/lo [D, ldv]: row r of sequence s lands in
+// column row_vcol[r] = seq_vcol[s] + position, seq_vcol multiples of 32.
+struct PrefillTcArgs {
+    const float* qkv = nullptr;
+    float* qkv_hi = nullptr;
+    float* qkv_lo = nullptr;
+    float* vt_hi = nullptr;
+    float* vt_lo = nullptr;
+    int ldv = 0;
+    const int* row_vcol = nullptr;
+    const int* seq_vcol = nullptr;
+    const int* offsets = nullptr;
+    const int* lens = nullptr;
+    int nseq = 0, max_len = 0, rows = 0, D = 0, head_dim = 64;
+    float* out_hi = nullptr;
+    float* out_lo = nullptr;
+    float scale = 0.f;
+    int* err = nullptr;
+};
+bool prefill_tc_supported(int head_dim);
+int launch_prefill_attention_tc(const PrefillTcArgs& a, cudaStream_t st);
+
 // Row and elementwise operations of the reference backend table (backend_ops.cu).
 void launch_softmax_rows(float* data, int rows, int cols, cudaStream_t st);
 void launch_layernorm_rows(const float* x, float* y, float* xn, const float* g, const float* b,
