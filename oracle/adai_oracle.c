@@ -318,3 +318,217 @@ int orc_generate(orc_model* m, const int* src, int S, int bos, int steps, const 
     free(x); free(nrm); free(q); free(a); free(o); free(h); free(lg);
     return tok < 0 ? -1 : 0;
 }
+
+/* ------------------------------------------------------------------------------------------ */
+/* Sampling: TextGenerator::generate (src/TextGenerator.cpp:519-565) and the filters it applies
+ * (:26-137), with the generator's std::mt19937 and std::discrete_distribution as GCC's libstdc++
+ * implements them (the reference is built with g++; TextGenerator.hpp:95).                      */
+
+/* MT19937 (Matsumoto and Nishimura, 1998): the published initialisation and recurrence with the
+ * std::mt19937 parameters. st[0..623] is the state, st[624] the read position. */
+void orc_mt_seed(unsigned int* st, unsigned int seed) {
+    st[0] = seed;
+    for (unsigned int i = 1; i < 624; ++i) st[i] = 1812433253u * (st[i - 1] ^ (st[i - 1] >> 30)) + i;
+    st[624] = 624;
+}
+
+static void mt_twist(unsigned int* mt) {
+    for (int i = 0; i < 624; ++i) {
+        const unsigned int y = (mt[i] & 0x80000000u) | (mt[(i + 1) % 624] & 0x7fffffffu);
+        mt[i] = mt[(i + 397) % 624] ^ (y >> 1) ^ ((y & 1u) ? 0x9908b0dfu : 0u);
+    }
+}
+
+unsigned int orc_mt_next(unsigned int* st) {
+    if (st[624] >= 624) {
+        mt_twist(st);
+        st[624] = 0;
+    }
+    unsigned int y = st[st[624]++];
+    y ^= y >> 11;
+    y ^= (y << 7) & 0x9d2c5680u;
+    y ^= (y << 15) & 0xefc60000u;
+    y ^= y >> 18;
+    return y;
+}
+
+/* std::generate_canonical<double, 53> over a 32-bit engine, as libstdc++ computes it: two draws
+ * x0, x1; (x0 + x1 * 2^32) / 2^64 in double; a result that rounds to 1 becomes the largest double
+ * below 1. */
+double orc_canonical(unsigned int* st) {
+    double s = (double)orc_mt_next(st);
+    s += (double)orc_mt_next(st) * 4294967296.0;
+    double r = s / 18446744073709551616.0;
+    if (r >= 1.0) r = nextafter(1.0, 0.0);
+    return r;
+}
+
+static double dmin(double a, double b) { return a < b ? a : b; }
+
+/* Keeps the k largest values and sets the rest to -1e9f (apply_top_k, src/TextGenerator.cpp:41-63).
+ * Values tied at the k-th place are kept lowest index first (std::partial_sort leaves that order
+ * unspecified; *margin drops to 0 there). *margin also takes the gap between the k-th and the
+ * (k+1)-th largest value, relative to the k-th. */
+static void keep_top(float* x, int V, int k, double* margin) {
+    int* ord = (int*)malloc(sizeof(int) * V);
+    for (int j = 0; j < V; ++j) ord[j] = j;
+    /* selection by descending value, ascending index among equals */
+    for (int r = 0; r < k + 1 && r < V; ++r) {
+        int best = r;
+        for (int q = r + 1; q < V; ++q) {
+            const int a = ord[q], b = ord[best];
+            if (x[a] > x[b] || (x[a] == x[b] && a < b)) best = q;
+        }
+        const int t = ord[r]; ord[r] = ord[best]; ord[best] = t;
+    }
+    if (k < V) {
+        const double vk = x[ord[k - 1]], vn = x[ord[k]];
+        const double gap = (vk - vn) / (fabs(vk) > 1e-30 ? fabs(vk) : 1e-30);
+        *margin = dmin(*margin, gap);
+    }
+    unsigned char* keep = (unsigned char*)calloc(V, 1);
+    for (int r = 0; r < k; ++r) keep[ord[r]] = 1;
+    for (int j = 0; j < V; ++j)
+        if (!keep[j]) x[j] = -1e9f;
+    free(keep);
+    free(ord);
+}
+
+static const float* g_sort_key;
+static int by_prob_desc(const void* pa, const void* pb) {
+    const int a = *(const int*)pa, b = *(const int*)pb;
+    if (g_sort_key[a] > g_sort_key[b]) return -1;
+    if (g_sort_key[a] < g_sort_key[b]) return 1;
+    return a < b ? -1 : (a > b);
+}
+
+/* apply_top_p (src/TextGenerator.cpp:66-101): softmax, tokens by descending probability, a float
+ * running sum until it reaches p; the rest -1e9f. *margin takes the distance of the float64
+ * running sum from p on both sides of the cut, and 0 when the float and float64 sums cut at
+ * different places or when equal probabilities straddle the cut. */
+static void keep_nucleus(float* x, int V, float p, double* margin) {
+    float* pr = (float*)malloc(sizeof(float) * V);
+    int* ord = (int*)malloc(sizeof(int) * V);
+    orc_softmax_row(x, pr, V);
+    for (int j = 0; j < V; ++j) ord[j] = j;
+    g_sort_key = pr;
+    qsort(ord, V, sizeof(int), by_prob_desc);
+    float cum = 0.0f;
+    double dcum = 0.0;
+    int n_f = -1, n_d = -1;
+    for (int r = 0; r < V; ++r) {
+        const double prev = dcum;
+        cum += pr[ord[r]];
+        dcum += pr[ord[r]];
+        if (n_f < 0 && cum >= p) n_f = r;
+        if (n_d < 0 && dcum >= p) {
+            n_d = r;
+            *margin = dmin(*margin, dmin(dcum - p, p - prev));
+        }
+    }
+    if (n_f != n_d) *margin = 0.0;
+    const int last = n_f < 0 ? V - 1 : n_f;
+    if (last + 1 < V && pr[ord[last]] == pr[ord[last + 1]]) *margin = 0.0;
+    float* y = (float*)malloc(sizeof(float) * V);
+    for (int j = 0; j < V; ++j) y[j] = -1e9f;
+    for (int r = 0; r <= last; ++r) y[ord[r]] = x[ord[r]];
+    memcpy(x, y, sizeof(float) * V);
+    free(y);
+    free(ord);
+    free(pr);
+}
+
+int orc_sample_next(const float* logits, int V, const float* fcfg, const int* icfg,
+                    const unsigned char* seen, int new_tokens, unsigned int* st, double* margin_out) {
+    const float T = fcfg[0], top_p = fcfg[1], pen = fcfg[2];
+    const int top_k = icfg[0], min_len = icfg[1], eos = icfg[2], pad = icfg[3];
+    double margin = INFINITY;
+    int any_finite = 0;
+    for (int j = 0; j < V; ++j) {
+        if (isnan(logits[j]) || logits[j] == INFINITY) return -1;  /* next_logits :186-190 */
+        any_finite |= isfinite(logits[j]);
+    }
+    if (!any_finite) return -2;  /* :192-194 */
+    float* x = (float*)malloc(sizeof(float) * V);
+    memcpy(x, logits, sizeof(float) * V);
+    if (new_tokens < min_len) {  /* :197-203 */
+        if (eos >= 0 && eos < V) x[eos] = -INFINITY;
+        if (pad >= 0 && pad < V) x[pad] = -INFINITY;
+    }
+    if (pen != 1.0f)  /* apply_repetition_penalty :115-136, once per distinct token */
+        for (int j = 0; j < V; ++j)
+            if (seen[j]) x[j] = x[j] > 0 ? x[j] / pen : x[j] * pen;
+    if (T > 0.0f && T != 1.0f)  /* apply_temperature :26-38 */
+        for (int j = 0; j < V; ++j) x[j] = x[j] / T;
+    if (top_k > 0 && top_k < V) keep_top(x, V, top_k, &margin);
+    if (top_p < 1.0f) {
+        if (top_p <= 0.0f) keep_top(x, V, 1, &margin);
+        else keep_nucleus(x, V, top_p, &margin);
+    }
+    int tok;
+    if (T <= 0.0f) {  /* argmax (:151-153): first maximum */
+        tok = orc_argmax(x, V);
+        float second = -INFINITY;
+        for (int j = 0; j < V; ++j)
+            if (j != tok && x[j] > second) second = x[j];
+        const double top = x[tok];
+        margin = dmin(margin, (top - second) / (fabs(top) > 1e-30 ? fabs(top) : 1e-30));
+    } else {  /* sample_token (:145-148): std::discrete_distribution over softmax(x) */
+        float* pr = (float*)malloc(sizeof(float) * V);
+        double* cp = (double*)malloc(sizeof(double) * V);
+        orc_softmax_row(x, pr, V);
+        double sum = 0.0;
+        for (int j = 0; j < V; ++j) sum += (double)pr[j];
+        double acc = 0.0;
+        for (int j = 0; j < V; ++j) {
+            acc += (double)pr[j] / sum;
+            cp[j] = acc;
+        }
+        cp[V - 1] = 1.0;
+        const double u = orc_canonical(st);
+        int lo = 0, hi = V;  /* lower_bound: first cp >= u */
+        while (lo < hi) {
+            const int mid = (lo + hi) / 2;
+            if (cp[mid] < u) lo = mid + 1;
+            else hi = mid;
+        }
+        tok = lo;
+        const double below = tok > 0 ? cp[tok - 1] : 0.0;
+        margin = dmin(margin, dmin(u - below, cp[tok] - u));
+        free(cp);
+        free(pr);
+    }
+    free(x);
+    if (margin_out) *margin_out = margin;
+    return tok;
+}
+
+int orc_sample_generate(const float* logits, int V, int steps, const float* fcfg, const int* icfg,
+                        unsigned int seed, const int* prompt, int n_prompt, int* out, double* margins) {
+    const int bos = icfg[4], eos = icfg[2], pad = icfg[3];
+    unsigned int st[625];
+    orc_mt_seed(st, seed);
+    unsigned char* seen = (unsigned char*)calloc(V, 1);
+    int n = 0;
+    if (n_prompt > 0) {
+        for (int i = 0; i < n_prompt; ++i) out[n++] = prompt[i];
+    } else {
+        out[n++] = bos;
+    }
+    for (int i = 0; i < n; ++i)
+        if (out[i] >= 0 && out[i] < V) seen[out[i]] = 1;
+    for (int s = 0; s < steps; ++s) {
+        double m = 0.0;
+        const int tok = orc_sample_next(logits + (size_t)s * V, V, fcfg, icfg, seen, s, st, &m);
+        if (tok < 0) {
+            free(seen);
+            return tok;
+        }
+        if (margins) margins[s] = m;
+        out[n++] = tok;
+        seen[tok] = 1;
+        if (tok == eos || tok == pad) break;  /* is_stop_token, src/SpecialTokens.hpp:162-164 */
+    }
+    free(seen);
+    return n;
+}

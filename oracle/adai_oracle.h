@@ -60,6 +60,34 @@ int orc_encode(orc_model* m, const int* ids, int S, float* enc_out);
 int orc_generate(orc_model* m, const int* src, int S, int bos, int steps, const int* forced,
                  int* out_ids, float* logits);
 
+/* ---- sampling (TextGenerator::generate, src/TextGenerator.cpp:519-565) ----
+ * fcfg = {temperature, top_p, repetition_penalty}; icfg = {top_k, min_length, eos_token_id,
+ * pad_token_id, bos_token_id} (GenerationConfig, src/TextGenerator.hpp:65-82). */
+
+/* std::mt19937 state: st[0..623] and the read position st[624]. */
+void orc_mt_seed(unsigned int* st, unsigned int seed);
+unsigned int orc_mt_next(unsigned int* st);
+/* std::generate_canonical<double, 53>(mt19937) as libstdc++ computes it (two draws). */
+double orc_canonical(unsigned int* st);
+
+/* One token from one logits row [V]: next_logits' checks and min_length mask, the repetition
+ * penalty over seen[] (1 = token already in the sequence), temperature, top-k, top-p, then the
+ * argmax (temperature <= 0) or a draw from std::discrete_distribution. Returns the token, -1 for
+ * NaN/+inf logits, -2 when every logit is -inf. *margin (may be NULL) is how far the decision was
+ * from changing: the smallest of the relative gap at the top-k cut, the distance of the running
+ * probability sum from p at the top-p cut, the relative gap between the two best values (argmax),
+ * and the distance of the uniform draw from its interval's ends (sampling); 0 at ties whose order
+ * the reference leaves unspecified. */
+int orc_sample_next(const float* logits, int V, const float* fcfg, const int* icfg,
+                    const unsigned char* seen, int new_tokens, unsigned int* st, double* margin);
+
+/* TextGenerator(config, seed).generate(fn, prompt) where fn returns row (new tokens so far) of
+ * logits [steps, V]: stops after EOS or PAD. out (capacity max(n_prompt, 1) + steps) receives the
+ * start tokens and the new ones; margins[s] the margin of step s. Returns the length of out, or a
+ * negative orc_sample_next status. */
+int orc_sample_generate(const float* logits, int V, int steps, const float* fcfg, const int* icfg,
+                        unsigned int seed, const int* prompt, int n_prompt, int* out, double* margins);
+
 #ifdef __cplusplus
 }
 #endif

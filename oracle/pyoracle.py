@@ -35,6 +35,14 @@ def _ptr_array(ws):
     return arr
 
 
+def sampling_cfg(temperature=1.0, top_k=0, top_p=1.0, repetition_penalty=1.0, min_length=0,
+                 eos=3, pad=0, bos=2):
+    """GenerationConfig's sampling fields (src/TextGenerator.hpp:65-82) as the oracles take them:
+    fcfg = {temperature, top_p, repetition_penalty}, icfg = {top_k, min_length, eos, pad, bos}."""
+    return (np.array([temperature, top_p, repetition_penalty], np.float32),
+            np.array([top_k, min_length, eos, pad, bos], np.int32))
+
+
 class _Base:
     lib: C.CDLL
 
@@ -79,7 +87,58 @@ class Port(_Base):
         lib.orc_encode.argtypes = [C.c_void_p, _i32p, C.c_int, _f32p]
         lib.orc_generate.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                      _i32p, C.c_void_p]
+        _u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+        _u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+        _f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
+        lib.orc_mt_seed.argtypes = [_u32p, C.c_uint]
+        lib.orc_mt_next.argtypes = [_u32p]
+        lib.orc_mt_next.restype = C.c_uint
+        lib.orc_canonical.argtypes = [_u32p]
+        lib.orc_canonical.restype = C.c_double
+        lib.orc_sample_next.argtypes = [_f32p, C.c_int, _f32p, _i32p, _u8p, C.c_int, _u32p,
+                                        C.POINTER(C.c_double)]
+        lib.orc_sample_next.restype = C.c_int
+        lib.orc_sample_generate.argtypes = [_f32p, C.c_int, C.c_int, _f32p, _i32p, C.c_uint,
+                                            C.c_void_p, C.c_int, _i32p, _f64p]
+        lib.orc_sample_generate.restype = C.c_int
         self.lib = lib
+
+    # ---- sampling (TextGenerator::generate) ----
+    def mt_seed(self, seed):
+        st = np.zeros(625, np.uint32)
+        self.lib.orc_mt_seed(st, seed)
+        return st
+
+    def mt_next(self, st):
+        return int(self.lib.orc_mt_next(st))
+
+    def canonical(self, st):
+        return float(self.lib.orc_canonical(st))
+
+    def sample_next(self, row, cfg, seen, new_tokens, st):
+        """One token from a logits row; seen is a uint8 [V] mask; st an mt19937 state that the
+        call advances. Returns (token, margin); token < 0 for the next_logits errors."""
+        row = np.ascontiguousarray(row, np.float32)
+        m = C.c_double(0.0)
+        tok = self.lib.orc_sample_next(row, row.size, cfg[0], cfg[1],
+                                       np.ascontiguousarray(seen, np.uint8), int(new_tokens), st,
+                                       C.byref(m))
+        return int(tok), m.value
+
+    def sample_generate(self, logits, cfg, seed, prompt=None):
+        """TextGenerator(cfg, seed).generate over the rows of logits [steps, V]: (sequence with
+        its start tokens, per-step margins)."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        steps, V = logits.shape
+        pr = np.ascontiguousarray(prompt if prompt is not None else [], np.int32)
+        out = np.empty(max(pr.size, 1) + steps, np.int32)
+        margins = np.full(steps, np.nan)
+        n = self.lib.orc_sample_generate(logits, V, steps, cfg[0], cfg[1], seed,
+                                         pr.ctypes.data if pr.size else None, pr.size, out, margins)
+        if n < 0:
+            raise ValueError("sample_generate: non-finite logits" if n == -1 else
+                             "sample_generate: every logit is -inf")
+        return out[:n].copy(), margins
 
     def layernorm(self, x, g, b):
         x = np.ascontiguousarray(x, np.float32)
@@ -185,7 +244,21 @@ class Ref(_Base):
         lib.ref_generate.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                      _i32p, C.c_void_p, C.POINTER(C.c_double),
                                      C.POINTER(C.c_double)]
+        lib.ref_sample_generate.argtypes = [_f32p, C.c_int, C.c_int, _f32p, _i32p, C.c_uint,
+                                            C.c_void_p, C.c_int, _i32p, C.POINTER(C.c_int)]
         self.lib = lib
+
+    def sample_generate(self, logits, cfg, seed, prompt=None):
+        """The reference's TextGenerator(cfg, seed).generate over the rows of logits."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        steps, V = logits.shape
+        pr = np.ascontiguousarray(prompt if prompt is not None else [], np.int32)
+        out = np.empty(max(pr.size, 1) + steps, np.int32)
+        n = C.c_int(0)
+        self._check(self.lib.ref_sample_generate(logits, V, steps, cfg[0], cfg[1], seed,
+                                                 pr.ctypes.data if pr.size else None, pr.size,
+                                                 out, C.byref(n)))
+        return out[:n.value].copy()
 
     def _err(self):
         return self.lib.ref_last_error().decode()

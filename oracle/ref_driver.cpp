@@ -33,6 +33,7 @@
 #include "LayerNorm.hpp"
 #include "Matrix.hpp"
 #include "PositionalEncoding.hpp"
+#include "TextGenerator.hpp"
 #include "encoder.hpp"
 
 namespace {
@@ -291,6 +292,41 @@ int ref_attention_single(const float* q, const float* K, const float* Vv, int T,
             Matrix o = w * Vh;
             for (int j = 0; j < dk; ++j) out[h * dk + j] = o.data[0][j];
         }
+    });
+}
+
+// TextGenerator::generate (src/TextGenerator.cpp:519-565) with every filter, over logits the caller
+// supplies: the model function returns row (tokens generated so far) of logits [steps, V], so the
+// sampler sees exactly these rows. fcfg = {temperature, top_p, repetition_penalty};
+// icfg = {top_k, min_length, eos_token_id, pad_token_id, bos_token_id}. seed != 0 seeds the
+// generator's mt19937 as TextGenerator(config, seed) does. prompt (n_prompt tokens) are the start
+// tokens ({bos} when empty). out receives the whole generated sequence, start tokens included;
+// *n_out its length (capacity n_prompt + steps, or steps + 1 when the prompt is empty).
+int ref_sample_generate(const float* logits, int V, int steps, const float* fcfg, const int* icfg,
+                        unsigned int seed, const int* prompt, int n_prompt, int* out, int* n_out) {
+    return guarded([&] {
+        TextGenerator::GenerationConfig cfg;
+        cfg.max_length = steps;
+        cfg.temperature = fcfg[0];
+        cfg.top_p = fcfg[1];
+        cfg.repetition_penalty = fcfg[2];
+        cfg.top_k = icfg[0];
+        cfg.min_length = icfg[1];
+        cfg.eos_token_id = icfg[2];
+        cfg.pad_token_id = icfg[3];
+        cfg.bos_token_id = icfg[4];
+        cfg.num_beams = 1;
+        TextGenerator gen(cfg, seed);
+        const int start = n_prompt > 0 ? n_prompt : 1;
+        TextGenerator::ModelForwardFn fn = [&](const std::vector<int>& toks) {
+            const size_t step = toks.size() - static_cast<size_t>(start);
+            if (step >= static_cast<size_t>(steps)) throw std::runtime_error("past the last logits row");
+            return from_flat(logits + step * static_cast<size_t>(V), 1, V);
+        };
+        std::vector<int> p(prompt, prompt + std::max(n_prompt, 0));
+        std::vector<int> got = gen.generate(fn, p);
+        std::copy(got.begin(), got.end(), out);
+        *n_out = static_cast<int>(got.size());
     });
 }
 
