@@ -55,10 +55,25 @@ EXPORTS = [
     "adai_b200_checkpoint_read", "adai_b200_model_load", "adai_b200_gemm_strided",
     "adai_b200_softmax_rows", "adai_b200_layernorm_fwd", "adai_b200_add_row_bias",
     "adai_b200_activation", "adai_b200_embedding_gather_add_pe", "adai_b200_backend_bind",
+    "adai_b200_kv_set_sampling", "adai_b200_kv_sampling_state", "adai_b200_sample_logits",
 ]
 
 # Kernel classes of adai_b200_profile_step (adai_b200_kernel_class).
 KERNEL_CLASSES = ("gemm", "self_attention", "cross_attention", "norm", "lm_head", "other")
+
+
+class Sampling(C.Structure):
+    """adai_b200_sampling: GenerationConfig's sampling fields (src/TextGenerator.hpp:65-82) and the
+    generator seed (0: std::random_device)."""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float),
+                ("repetition_penalty", C.c_float), ("min_length", C.c_int),
+                ("eos_token_id", C.c_int), ("pad_token_id", C.c_int), ("seed", C.c_uint)]
+
+    @classmethod
+    def make(cls, temperature=1.0, top_k=0, top_p=1.0, repetition_penalty=1.0, min_length=0,
+             eos_token_id=3, pad_token_id=0, seed=0) -> "Sampling":
+        return cls(temperature, top_k, top_p, repetition_penalty, min_length, eos_token_id,
+                   pad_token_id, seed)
 
 
 class ModelDesc(C.Structure):
@@ -104,6 +119,9 @@ def load() -> C.CDLL:
     lib.adai_b200_encode.argtypes = [_vp, _vp, C.c_int, _vp, _vp, _vp, _vp]
     lib.adai_b200_decode_step.argtypes = [_vp, _vp, C.c_int, _vp, _vp, _vp, _vp]
     lib.adai_b200_generate.argtypes = [_vp, _vp, C.c_int, _vp, _vp, C.c_int, _vp]
+    lib.adai_b200_kv_set_sampling.argtypes = [_vp, _vp, C.c_int, C.POINTER(Sampling), _vp, C.c_int]
+    lib.adai_b200_kv_sampling_state.argtypes = [_vp, _vp, C.c_int, _vp, _vp]
+    lib.adai_b200_sample_logits.argtypes = [_vp, _vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp]
     lib.adai_b200_sgemm.argtypes = [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp]
     lib.adai_b200_weight_create.argtypes = [_vp, _vp, C.c_int, C.c_int, C.POINTER(_vp)]
     lib.adai_b200_weight_destroy.argtypes = [_vp, _vp]
@@ -376,6 +394,30 @@ class KVArena:
                                               _ptr(ln)))
         return {k: dict(ms=float(ms[i]), bytes=float(by[i]), flops=float(fl[i]),
                         launches=int(ln[i])) for i, k in enumerate(KERNEL_CLASSES)}
+
+    def set_sampling(self, slot: int, cfg: "Sampling | None", history=()) -> None:
+        """Configures slot for the reference's sampling rules (None: back to the argmax)."""
+        h = _i32(list(history))
+        check(self.lib.adai_b200_kv_set_sampling(self.ctx.h, self.h, slot,
+                                                 C.byref(cfg) if cfg is not None else None,
+                                                 _ptr(h) if h.size else None, h.size))
+
+    def sampling_state(self, slot: int) -> tuple[np.ndarray, int]:
+        """(std::mt19937 state words [625]: 624 state + read position, steps sampled)."""
+        st = np.zeros(625, np.uint32)
+        n = C.c_int()
+        check(self.lib.adai_b200_kv_sampling_state(self.ctx.h, self.h, slot, _ptr(st),
+                                                   C.byref(n)))
+        return st, n.value
+
+    def sample_logits(self, slots, logits_ptr, ld, fed_ids=None) -> np.ndarray:
+        """Tokens for device logits rows [B, ld] by each slot's sampling rules."""
+        slots = _i32(slots)
+        fed = _i32(fed_ids) if fed_ids is not None else None
+        nxt = np.empty(slots.size, np.int32)
+        check(self.lib.adai_b200_sample_logits(self.ctx.h, self.h, slots.size, _ptr(slots),
+                                               _ptr(fed), logits_ptr, ld, _ptr(nxt)))
+        return nxt
 
     def generate(self, slots, first_ids, steps):
         slots, first = _i32(slots), _i32(first_ids)

@@ -17,6 +17,7 @@
 #include <map>
 #include <memory>
 #include <mutex>
+#include <random>
 #include <set>
 #include <stdexcept>
 #include <string>
@@ -144,6 +145,14 @@ struct adai_b200_kv {
     int *d_self_len = nullptr, *d_cross_len = nullptr;
     int* d_hist = nullptr;  // [max_slots][self_cap]: the argmax produced at each position
     std::vector<int> self_len, cross_len;
+    // sampling state per slot (allocated on first use): configuration, std::mt19937, the set of
+    // token ids already in the sequence (one bit each), steps sampled since configured
+    SampleSlot* d_samp = nullptr;
+    unsigned* d_mt = nullptr;
+    unsigned* d_seen = nullptr;
+    int* d_new_tokens = nullptr;
+    int seen_words = 0, samp_vocab = 0;
+    std::vector<char> samp_on;
     long long self_slot_stride() const { return static_cast<long long>(H) * self_cap * dh; }
     long long cross_slot_stride() const { return static_cast<long long>(H) * cross_cap * dh; }
     float* self_k_layer(int l) const { return self_k + static_cast<size_t>(l) * max_slots * self_slot_stride(); }
@@ -167,7 +176,7 @@ struct GraphKey {
     }
 };
 
-enum StepFlags { kStepLogits = 1, kStepAdvanceIds = 2 };
+enum StepFlags { kStepLogits = 1, kStepAdvanceIds = 2, kStepSample = 4 };
 
 // Per-launch CUDA-event spans of a profiled (eager) decode step, with the algorithmic bytes and
 // flops of each launch, grouped by kernel class (adai_b200_kernel_class in the header).
@@ -203,6 +212,8 @@ struct adai_b200_ctx {
     size_t op_a_floats = 0;
     float* op_c = nullptr;  // packed output of op-level GEMMs whose C is not float4-aligned
     size_t op_c_floats = 0;
+    float* samp_park = nullptr;  // [rows, V]: top-p parks the filtered logits here
+    size_t samp_park_floats = 0;
     int* h_pin = nullptr;  // pinned staging for ids / slots / lengths
     size_t h_pin_ints = 0;
     std::map<GraphKey, cudaGraphExec_t> graphs;
@@ -346,6 +357,15 @@ struct adai_b200_ctx {
                 attn_tickets = dzalloc_t<int>(tk);
             }
         }
+    }
+
+    void ensure_sample_park(size_t floats) {
+        if (floats <= samp_park_floats) return;
+        cuda_ok(cudaStreamSynchronize(stream), "sync before scratch growth");
+        clear_graphs();
+        dfree(samp_park);
+        samp_park = dalloc_t<float>(floats);
+        samp_park_floats = floats;
     }
 
     void gemm(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e) {
@@ -544,6 +564,26 @@ TcActs acts(const float* hi, const float* lo, int K, int rows_alloc) {
     return a;
 }
 
+SampleArgs sample_args(adai_b200_ctx* c, adai_b200_kv* kv, int B, const float* logits, int ld,
+                       const int* fed, int* next, int* nonfinite) {
+    SampleArgs a;
+    a.logits = logits;
+    a.ld = ld;
+    a.slots = c->sb.slots;
+    a.fed = fed;
+    a.next = next;
+    a.nonfinite = nonfinite;
+    a.cfg = kv->d_samp;
+    a.mt = kv->d_mt;
+    a.seen = kv->d_seen;
+    a.seen_words = kv->seen_words;
+    a.new_tokens = kv->d_new_tokens;
+    a.scratch = c->samp_park;
+    a.B = B;
+    a.V = c->model->d.vocab;
+    return a;
+}
+
 // Enqueues one stacked decode step for rows 0..B-1 of the step buffers (ids in sb.ids, slots in
 // sb.slots). The graph captured from this is replayed by decode_step / generate.
 void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
@@ -690,7 +730,7 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
     }
     {  // logits = x W_out + b, first maximum per row
         GemmEpilogue e;
-        e.flags = kEpiBias | kEpiArgmax | ((flags & kStepLogits) ? kEpiStore : 0);
+        e.flags = kEpiBias | kEpiArgmax | ((flags & (kStepLogits | kStepSample)) ? kEpiStore : 0);
         e.bias = m.head_b;
         e.out = s.logits;
         e.ldo = m.d.vocab;
@@ -699,6 +739,11 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
         const double Vd = m.d.vocab;
         timed(c, ADAI_B200_KC_HEAD, 4.0 * (Bd * Dd + Dd * Vd), gemm_flops(Bd, Vd, Dd),
               [&] { c->gemm(a_nrm, B, m.head, e); });
+    }
+    if (flags & kStepSample) {  // rows whose slot samples replace the argmax (sample.cu)
+        const SampleArgs a = sample_args(c, kv, B, s.logits, m.d.vocab, s.ids, s.next, s.nonfinite);
+        timed(c, ADAI_B200_KC_OTHER, 4.0 * Bd * m.d.vocab, 0,
+              [&] { cuda_ok(launch_sample_rows(a, st), "sample launch"); });
     }
 }
 
@@ -720,8 +765,9 @@ __global__ void record_and_advance_kernel(const int* __restrict__ next, int* __r
 }
 
 // Sizes the scratch a decode step of B rows needs (allocation cannot happen inside a capture).
-void presize_step_scratch(adai_b200_ctx* c, adai_b200_kv* kv, int B) {
+void presize_step_scratch(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
     const Model& m = *c->model;
+    if (flags & kStepSample) c->ensure_sample_park(static_cast<size_t>(B) * m.d.vocab);
     const int D = m.d.d_model, F = m.d.d_ff;
     for (const auto& sh : {std::make_tuple(3 * D, D, 0), std::make_tuple(D, D, 0),
                            std::make_tuple(F, D, 0), std::make_tuple(D, F, 0),
@@ -734,7 +780,7 @@ cudaGraphExec_t get_graph(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) 
     const GraphKey key{kv, B, flags};
     auto it = c->graphs.find(key);
     if (it != c->graphs.end()) return it->second;
-    presize_step_scratch(c, kv, B);
+    presize_step_scratch(c, kv, B, flags);
     cuda_ok(cudaStreamSynchronize(c->stream), "sync before capture");
     cudaGraph_t g;
     cuda_ok(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
@@ -777,6 +823,14 @@ void check_kv(adai_b200_ctx* c, adai_b200_kv* kv) {
 
 void check_model(adai_b200_ctx* c) {
     if (!c->model) fail(ADAI_B200_ERR_STATE, "no model uploaded");
+}
+
+// kStepSample when a row of the batch belongs to a slot configured for sampling.
+int sample_flag(const adai_b200_kv* kv, int B, const int* slots) {
+    if (kv->samp_on.empty()) return 0;
+    for (int b = 0; b < B; ++b)
+        if (kv->samp_on[slots[b]]) return kStepSample;
+    return 0;
 }
 
 // Validates the batch of a decode step and stages slots/ids into the step buffers.
@@ -891,6 +945,8 @@ int adai_b200_model_upload(adai_b200_ctx* c, const adai_b200_model_desc* d,
         for (adai_b200_kv* kv : c->kvs)
             if (kv->L != d->dec_layers || kv->H != d->n_heads)
                 fail(ADAI_B200_ERR_STATE, "an existing KV arena does not match this model");
+        for (adai_b200_kv* kv : c->kvs)  // sampling state is per vocabulary: slots go back to argmax
+            if (kv->samp_vocab != d->vocab) std::fill(kv->samp_on.begin(), kv->samp_on.end(), 0);
         free_model(c);
         free_enc_bufs(c);
         free_step_bufs(c);
@@ -1078,7 +1134,8 @@ int adai_b200_kv_destroy(adai_b200_ctx* c, adai_b200_kv* kv) {
         c->clear_graphs();
         for (void* p : {(void*)kv->self_k, (void*)kv->self_v, (void*)kv->cross_k,
                         (void*)kv->cross_v, (void*)kv->d_self_len, (void*)kv->d_cross_len,
-                        (void*)kv->d_hist})
+                        (void*)kv->d_hist, (void*)kv->d_samp, (void*)kv->d_mt, (void*)kv->d_seen,
+                        (void*)kv->d_new_tokens})
             c->dfree(p);
         c->kvs.erase(kv);
         delete kv;
@@ -1094,6 +1151,10 @@ int adai_b200_kv_reset(adai_b200_ctx* c, adai_b200_kv* kv, int slot) {
         kv->cross_len[slot] = 0;
         cuda_ok(cudaMemsetAsync(kv->d_self_len + slot, 0, sizeof(int), c->stream), "memset");
         cuda_ok(cudaMemsetAsync(kv->d_cross_len + slot, 0, sizeof(int), c->stream), "memset");
+        if (kv->d_samp) {  // back to the fused argmax
+            kv->samp_on[slot] = 0;
+            cuda_ok(cudaMemsetAsync(kv->d_samp + slot, 0, sizeof(SampleSlot), c->stream), "memset");
+        }
         c->sync(wait_timeout_seconds());
     });
 }
@@ -1303,7 +1364,7 @@ int adai_b200_decode_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* 
         check_kv(c, kv);
         if (!next_ids) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null next_ids");
         stage_batch(c, kv, B, slots, ids, 1);
-        const int flags = logits ? kStepLogits : 0;
+        const int flags = (logits ? kStepLogits : 0) | sample_flag(kv, B, slots);
         cudaGraphExec_t g = get_graph(c, kv, B, flags);
         cuda_ok(cudaMemsetAsync(c->sb.nonfinite_any, 0, sizeof(int), c->stream), "memset");
         cuda_ok(cudaGraphLaunch(g, c->stream), "graph launch");
@@ -1330,7 +1391,8 @@ int adai_b200_generate(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slo
         stage_batch(c, kv, B, slots, first_ids, steps);
         std::vector<int> pos0(B);
         for (int b = 0; b < B; ++b) pos0[b] = kv->self_len[slots[b]];
-        cudaGraphExec_t g = get_graph(c, kv, B, kStepAdvanceIds);
+        const int flags = kStepAdvanceIds | sample_flag(kv, B, slots);
+        cudaGraphExec_t g = get_graph(c, kv, B, flags);
         cuda_ok(cudaMemsetAsync(c->sb.nonfinite_any, 0, sizeof(int), c->stream), "memset");
         cudaEvent_t e0, e1;
         cuda_ok(cudaEventCreate(&e0), "cudaEventCreate");
@@ -1344,7 +1406,7 @@ int adai_b200_generate(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slo
         cudaEventDestroy(e0);
         cudaEventDestroy(e1);
         c->last_decode_ms = ms;
-        c->last_kernels_per_step = c->graph_kernels[GraphKey{kv, B, kStepAdvanceIds}];
+        c->last_kernels_per_step = c->graph_kernels[GraphKey{kv, B, flags}];
         for (int b = 0; b < B; ++b) kv->self_len[slots[b]] += steps;
         int nf = 0;
         cuda_ok(cudaMemcpy(&nf, c->sb.nonfinite_any, sizeof(int), cudaMemcpyDeviceToHost), "D2H flag");
@@ -1353,6 +1415,163 @@ int adai_b200_generate(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slo
                                kv->d_hist + static_cast<size_t>(slots[b]) * kv->self_cap + pos0[b],
                                steps * sizeof(int), cudaMemcpyDeviceToHost), "D2H ids");
         if (nf) fail(ADAI_B200_ERR_NONFINITE, "the model returned non-finite logits");
+    });
+}
+
+}  // extern "C"
+
+// ---- sampling ----------------------------------------------------------------------------------
+namespace {
+
+// std::mt19937(seed): the published MT19937 initialisation; the read position starts past the
+// end, so the first draw refreshes the state (as the standard engine does).
+void mt_seed_host(unsigned seed, unsigned* st) {
+    st[0] = seed;
+    for (unsigned i = 1; i < 624; ++i) st[i] = 1812433253u * (st[i - 1] ^ (st[i - 1] >> 30)) + i;
+    st[624] = 624;
+}
+
+void ensure_kv_sampling(adai_b200_ctx* c, adai_b200_kv* kv) {
+    const int V = c->model->d.vocab;
+    if (kv->d_samp && kv->samp_vocab == V) return;
+    cuda_ok(cudaStreamSynchronize(c->stream), "sync");
+    c->clear_graphs();
+    for (void* p : {(void*)kv->d_samp, (void*)kv->d_mt, (void*)kv->d_seen, (void*)kv->d_new_tokens})
+        c->dfree(p);
+    kv->d_samp = nullptr;
+    kv->d_mt = kv->d_seen = nullptr;
+    kv->d_new_tokens = nullptr;
+    const size_t n = kv->max_slots;
+    kv->seen_words = (V + 31) / 32;
+    kv->d_samp = c->dzalloc_t<SampleSlot>(n);
+    kv->d_mt = c->dzalloc_t<unsigned>(n * kMtWords);
+    kv->d_seen = c->dzalloc_t<unsigned>(n * kv->seen_words);
+    kv->d_new_tokens = c->dzalloc_t<int>(n);
+    kv->samp_vocab = V;
+    kv->samp_on.assign(n, 0);
+}
+
+void check_slot(const adai_b200_kv* kv, int slot) {
+    if (slot < 0 || slot >= kv->max_slots)
+        fail(ADAI_B200_ERR_OUT_OF_RANGE, "slot " + std::to_string(slot) + " out of range");
+}
+
+}  // namespace
+
+extern "C" {
+
+int adai_b200_kv_set_sampling(adai_b200_ctx* c, adai_b200_kv* kv, int slot,
+                              const adai_b200_sampling* cfg, const int* history, int n_history) {
+    return guarded([&] {
+        check_ctx(c);
+        check_model(c);
+        check_kv(c, kv);
+        check_slot(kv, slot);
+        if (!cfg) {
+            if (kv->d_samp) {
+                kv->samp_on[slot] = 0;
+                cuda_ok(cudaMemsetAsync(kv->d_samp + slot, 0, sizeof(SampleSlot), c->stream), "memset");
+                c->sync(wait_timeout_seconds());
+            }
+            return;
+        }
+        if (n_history < 0 || (n_history > 0 && !history))
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "history must hold n_history >= 0 ids");
+        if (!std::isfinite(cfg->temperature) || !std::isfinite(cfg->top_p))
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "temperature and top_p must be finite");
+        if (!std::isfinite(cfg->repetition_penalty) || !(cfg->repetition_penalty > 0.0f))
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "repetition_penalty must be finite and positive");
+        const int V = c->model->d.vocab;
+        if (V > sample_max_vocab())
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "vocabulary of " + std::to_string(V) +
+                                                     " exceeds the device sampler's " +
+                                                     std::to_string(sample_max_vocab()));
+        ensure_kv_sampling(c, kv);
+        SampleSlot h;
+        h.temperature = cfg->temperature;
+        h.top_p = cfg->top_p;
+        h.penalty = cfg->repetition_penalty;
+        h.top_k = cfg->top_k;
+        h.min_length = cfg->min_length;
+        h.eos = cfg->eos_token_id;
+        h.pad = cfg->pad_token_id;
+        h.enabled = 1;
+        const unsigned seed = cfg->seed ? cfg->seed : std::random_device{}();
+        std::vector<unsigned> mt(kMtWords, 0u);
+        mt_seed_host(seed, mt.data());
+        std::vector<unsigned> seen(kv->seen_words, 0u);
+        for (int i = 0; i < n_history; ++i)
+            if (history[i] >= 0 && history[i] < V) seen[history[i] >> 5] |= 1u << (history[i] & 31);
+        cudaStream_t st = c->stream;
+        cuda_ok(cudaMemcpyAsync(kv->d_samp + slot, &h, sizeof(h), cudaMemcpyHostToDevice, st), "H2D");
+        cuda_ok(cudaMemcpyAsync(kv->d_mt + static_cast<size_t>(slot) * kMtWords, mt.data(),
+                                kMtWords * sizeof(unsigned), cudaMemcpyHostToDevice, st), "H2D");
+        cuda_ok(cudaMemcpyAsync(kv->d_seen + static_cast<size_t>(slot) * kv->seen_words, seen.data(),
+                                seen.size() * sizeof(unsigned), cudaMemcpyHostToDevice, st), "H2D");
+        cuda_ok(cudaMemsetAsync(kv->d_new_tokens + slot, 0, sizeof(int), st), "memset");
+        c->sync(wait_timeout_seconds());
+        kv->samp_on[slot] = 1;
+    });
+}
+
+int adai_b200_kv_sampling_state(adai_b200_ctx* c, adai_b200_kv* kv, int slot, unsigned* mt_state,
+                                int* new_tokens) {
+    return guarded([&] {
+        check_ctx(c);
+        check_kv(c, kv);
+        check_slot(kv, slot);
+        if (kv->samp_on.empty() || !kv->samp_on[slot])
+            fail(ADAI_B200_ERR_STATE, "slot " + std::to_string(slot) + " is not configured for sampling");
+        c->sync(wait_timeout_seconds());
+        if (mt_state)
+            cuda_ok(cudaMemcpy(mt_state, kv->d_mt + static_cast<size_t>(slot) * kMtWords,
+                               625 * sizeof(unsigned), cudaMemcpyDeviceToHost), "D2H");
+        if (new_tokens)
+            cuda_ok(cudaMemcpy(new_tokens, kv->d_new_tokens + slot, sizeof(int), cudaMemcpyDeviceToHost), "D2H");
+    });
+}
+
+int adai_b200_sample_logits(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slots,
+                            const int* fed_ids, const float* logits, int ld, int* next_ids) {
+    return guarded([&] {
+        check_ctx(c);
+        check_model(c);
+        check_kv(c, kv);
+        const int V = c->model->d.vocab;
+        if (B <= 0 || B > kv->max_slots) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "batch must be in [1, max_slots]");
+        if (!slots || !logits || !next_ids || ld < V)
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "need slots, logits with ld >= vocab, next_ids");
+        std::vector<char> dup(kv->max_slots, 0);
+        for (int b = 0; b < B; ++b) {
+            check_slot(kv, slots[b]);
+            if (dup[slots[b]]) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "slot repeated in one batch");
+            dup[slots[b]] = 1;
+            if (kv->samp_on.empty() || !kv->samp_on[slots[b]])
+                fail(ADAI_B200_ERR_STATE, "slot " + std::to_string(slots[b]) + " is not configured for sampling");
+            if (fed_ids && (fed_ids[b] < 0 || fed_ids[b] >= V))
+                fail(ADAI_B200_ERR_OUT_OF_RANGE, "Token ID " + std::to_string(fed_ids[b]) + " out of range");
+        }
+        if (kv->samp_vocab != V) fail(ADAI_B200_ERR_STATE, "sampling state was made for another vocabulary");
+        ensure_step_bufs(c, B);
+        c->ensure_sample_park(static_cast<size_t>(B) * V);
+        int* pin = c->pinned(3 * static_cast<size_t>(B));
+        std::memcpy(pin, slots, B * sizeof(int));
+        if (fed_ids) std::memcpy(pin + B, fed_ids, B * sizeof(int));
+        cudaStream_t st = c->stream;
+        cuda_ok(cudaMemcpyAsync(c->sb.slots, pin, B * sizeof(int), cudaMemcpyHostToDevice, st), "H2D slots");
+        if (fed_ids)
+            cuda_ok(cudaMemcpyAsync(c->sb.ids, pin + B, B * sizeof(int), cudaMemcpyHostToDevice, st), "H2D ids");
+        cuda_ok(cudaMemsetAsync(c->sb.nonfinite, 0, B * sizeof(int), st), "memset");
+        const SampleArgs a = sample_args(c, kv, B, logits, ld, fed_ids ? c->sb.ids : nullptr,
+                                         c->sb.next, c->sb.nonfinite);
+        cuda_ok(launch_sample_rows(a, st), "sample launch");
+        cuda_ok(cudaMemcpyAsync(pin, c->sb.next, B * sizeof(int), cudaMemcpyDeviceToHost, st), "D2H");
+        cuda_ok(cudaMemcpyAsync(pin + 2 * B, c->sb.nonfinite, B * sizeof(int), cudaMemcpyDeviceToHost, st), "D2H");
+        c->sync(wait_timeout_seconds());
+        std::memcpy(next_ids, pin, B * sizeof(int));
+        for (int b = 0; b < B; ++b)
+            if (pin[2 * B + b])
+                fail(ADAI_B200_ERR_NONFINITE, "TextGenerator: the model returned non-finite logits");
     });
 }
 
@@ -1600,7 +1819,8 @@ int adai_b200_profile_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int*
         if (n_classes < ADAI_B200_KC_COUNT || !ms || !bytes || !flops || !launches)
             fail(ADAI_B200_ERR_INVALID_ARGUMENT, "need ADAI_B200_KC_COUNT entries in every output array");
         stage_batch(c, kv, B, slots, ids, 1);
-        presize_step_scratch(c, kv, B);
+        const int flags = sample_flag(kv, B, slots);
+        presize_step_scratch(c, kv, B, flags);
         Profiler prof;
         for (int b = 0; b < B; ++b) {
             prof.sum_self_rows += kv->self_len[slots[b]] + 1;
@@ -1608,7 +1828,7 @@ int adai_b200_profile_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int*
         }
         c->prof = &prof;
         try {
-            record_step(c, kv, B, 0);
+            record_step(c, kv, B, flags);
             timed(c, ADAI_B200_KC_OTHER, 0, 0, [&] {
                 record_and_advance_kernel<<<(B + 127) / 128, 128, 0, c->stream>>>(
                     c->sb.next, c->sb.ids, c->sb.slots, kv->d_self_len, kv->d_hist, kv->self_cap,

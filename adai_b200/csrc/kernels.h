@@ -222,4 +222,30 @@ void launch_prefill_attention(const float* qkv, int D, int H, const int* offsets
 void launch_advance(const int* next, int* ids, const int* slots, int* len_by_slot, int B,
                     cudaStream_t st);
 
+// ---- token selection with the reference's sampling rules (sample.cu) ----
+// Per-slot configuration (GenerationConfig's sampling fields, src/TextGenerator.hpp:65-82).
+struct SampleSlot {
+    float temperature = 1.0f, top_p = 1.0f, penalty = 1.0f;
+    int top_k = 0, min_length = 0, eos = 3, pad = 0;
+    int enabled = 0;  // 0: the row keeps the step's fused argmax
+};
+constexpr int kMtWords = 640;  // per slot: std::mt19937 state [624] + read position, padded
+struct SampleArgs {
+    const float* logits = nullptr;  // [B, ld]
+    int ld = 0;
+    const int* slots = nullptr;     // [B]
+    const int* fed = nullptr;       // [B] token fed this step (counts as seen), or null
+    int* next = nullptr;            // [B] chosen token (rows whose slot is disabled untouched)
+    int* nonfinite = nullptr;       // [B] set to 1 for NaN / +inf / all -inf rows, or null
+    const SampleSlot* cfg = nullptr;  // [slots]
+    unsigned* mt = nullptr;         // [slots][kMtWords]
+    unsigned* seen = nullptr;       // [slots][seen_words] bit per token id
+    int seen_words = 0;
+    int* new_tokens = nullptr;      // [slots] steps sampled since the slot was configured
+    float* scratch = nullptr;       // [B, V] (top-p parks the filtered row here)
+    int B = 0, V = 0;
+};
+int sample_max_vocab();
+cudaError_t launch_sample_rows(const SampleArgs& a, cudaStream_t st);
+
 }  // namespace adai_b200

@@ -158,6 +158,54 @@ ADAI_B200_API int adai_b200_decode_step(adai_b200_ctx* ctx, adai_b200_kv* kv, in
 ADAI_B200_API int adai_b200_generate(adai_b200_ctx* ctx, adai_b200_kv* kv, int B, const int* slots,
                        const int* first_ids, int steps, int* out_ids);
 
+/* ---- sampling (TextGenerator::generate, src/TextGenerator.cpp:519-565; GenerationConfig,
+ * src/TextGenerator.hpp:65-82) ----
+ * A slot configured with adai_b200_kv_set_sampling picks its tokens, in adai_b200_decode_step and
+ * adai_b200_generate alike, by the reference's rules instead of the plain argmax: min_length keeps
+ * EOS and PAD out while fewer new tokens exist (:197-203); the repetition penalty divides positive
+ * and multiplies other logits of every distinct token already in the sequence (:115-136); then
+ * temperature (:26-38), top-k (:41-63), top-p (:66-101); temperature <= 0 takes the first maximum
+ * of the filtered logits, otherwise the token is drawn from their softmax with the slot's own
+ * std::mt19937 through std::discrete_distribution as GCC's libstdc++ computes it (:145-148).
+ * Every strategy of the reference is a setting of these fields: generate_greedy (:209) is
+ * temperature <= 0, generate_sampling (:398) top_k 0 and top_p 1, generate_top_k (:438) top_p 1,
+ * generate_nucleus (:475) top_k 0. Exactly tied values at the top-k / top-p cut are kept lowest
+ * index first (the reference's std::partial_sort / std::sort leave that order unspecified). */
+typedef struct adai_b200_sampling {
+    float temperature;        /* <= 0: argmax of the filtered logits; 1: unscaled */
+    int top_k;                /* <= 0 or >= vocab: off */
+    float top_p;              /* >= 1: off; <= 0: the single most likely token */
+    float repetition_penalty; /* 1: off; must be finite and positive */
+    int min_length;           /* new tokens before EOS / PAD may be chosen */
+    int eos_token_id;         /* masked while below min_length (3 in the reference) */
+    int pad_token_id;         /* masked while below min_length (0 in the reference) */
+    unsigned int seed;        /* std::mt19937 seed; 0 draws one from std::random_device */
+} adai_b200_sampling;
+
+/* Configures slot `slot` for sampling (cfg NULL: back to the fused argmax, as after
+ * adai_b200_kv_reset), seeds its generator and resets its count of new tokens. history holds the
+ * ids already in the sequence before the first token fed (the reference's start tokens beyond the
+ * one fed first; may be NULL when n_history is 0). Each step then counts the id fed as part of the
+ * sequence, so after the usual BOS feed the penalty set is exactly the reference's `generated`.
+ * The whole logits row is held in shared memory: vocab is limited to about 57 000. */
+ADAI_B200_API int adai_b200_kv_set_sampling(adai_b200_ctx* ctx, adai_b200_kv* kv, int slot,
+                                            const adai_b200_sampling* cfg, const int* history,
+                                            int n_history);
+
+/* The slot's generator state (625 words: std::mt19937's 624 state words, then the read position)
+ * and its count of sampled steps. Either output may be NULL. */
+ADAI_B200_API int adai_b200_kv_sampling_state(adai_b200_ctx* ctx, adai_b200_kv* kv, int slot,
+                                              unsigned int* mt_state, int* new_tokens);
+
+/* Op level: picks one token per row of device logits [B, ld] (ld >= vocab) for slots[b] (each
+ * configured for sampling), with fed_ids[b] (host; may be NULL) counted into the sequence first,
+ * exactly as a decode step does after its LM head. Advances the slots' generators and counts.
+ * next_ids: host. Fails with ADAI_B200_ERR_NONFINITE for a NaN / +inf row or one without a finite
+ * value (TextGenerator::next_logits, :177-206). */
+ADAI_B200_API int adai_b200_sample_logits(adai_b200_ctx* ctx, adai_b200_kv* kv, int B,
+                                          const int* slots, const int* fed_ids,
+                                          const float* logits, int ld, int* next_ids);
+
 /* ---- op level: stacked GEMM (Matrix::operator*, src/Matrix.cpp:212-277; matrix_multiply_gpu,
  * src/gpu/MatrixGPU.hpp:100 and src/gpu/MatrixGPU.cu:351-370) ----
  * C[m,n] = A[m,k] B[k,n], fp32 in and out, 3xTF32 on the tensor cores. Device pointers on the

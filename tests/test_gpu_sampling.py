@@ -1,0 +1,339 @@
+"""Token selection with the reference's sampling rules on the device (adai_b200_kv_set_sampling,
+adai_b200_sample_logits, and sampled slots inside the decode step and the device-side generate
+loop), against the sampler restatement (oracle/adai_oracle.c, orc_sample_next) run in lockstep:
+each slot's std::mt19937 and token set are mirrored on the host and fed the same tokens.
+
+Parity rule (as for the restatement against the reference build): tokens are equal at every step
+whose decision margin exceeds MARGIN. Below it float-rounding differences may legitimately move the
+choice. The generator states must agree word for word after every run, so the draws consumed match.
+The reference's own sampler tests (tests/textgenerator_test.cpp) are replayed on the device.
+"""
+import numpy as np
+import pytest
+
+from adai_b200.api import Context, Sampling
+from adai_b200.config import TINY
+from adai_b200.synth import make_sources, make_weights
+from oracle.pyoracle import sampling_cfg
+
+pytestmark = pytest.mark.gpu
+
+MARGIN = 1e-6
+BOS = 2
+
+CONFIGS = [
+    dict(),
+    dict(temperature=0.7),
+    dict(temperature=1.3, top_k=40),
+    dict(temperature=0.9, top_p=0.9),
+    dict(temperature=1.0, top_k=200, top_p=0.8, repetition_penalty=1.3),
+    dict(temperature=0.0, repetition_penalty=1.5),
+    dict(temperature=0.0, top_k=5, min_length=6),
+    dict(temperature=1.1, top_p=0.0),
+    dict(temperature=2.0, top_p=0.97, min_length=3, repetition_penalty=0.8),
+    dict(temperature=-0.5, top_p=0.5),
+    dict(temperature=0.5, top_k=1),
+    dict(temperature=1.0, top_p=0.999),
+]
+
+
+class Mirror:
+    """One slot's sampling state on the host: generator, tokens in the sequence, step count."""
+
+    def __init__(self, port, kw, seed, V, history=()):
+        self.port, self.cfg = port, sampling_cfg(**kw)
+        self.st = port.mt_seed(seed)
+        self.seen = np.zeros(V, np.uint8)
+        self.seen[list(history)] = 1
+        self.n = 0
+
+    def step(self, row, fed):
+        self.seen[fed] = 1
+        tok, m = self.port.sample_next(row, self.cfg, self.seen, self.n, self.st)
+        self.n += 1
+        return tok, m
+
+
+@pytest.fixture(scope="module")
+def sctx():
+    c = Context(0)
+    c.upload(TINY, make_weights(TINY, 0, affine=True))
+    yield c
+    c.close()
+
+
+def dev(torch, a):
+    t = torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+    torch.cuda.synchronize()
+    return t
+
+
+def test_sample_logits_lockstep_with_oracle(sctx, port, torch_cuda):
+    V, B = TINY.vocab, len(CONFIGS)
+    kv = sctx.kv_arena(B, 8, 8)
+    slots = list(range(B))
+    mirrors = []
+    for i, kw in enumerate(CONFIGS):
+        kv.set_sampling(i, Sampling.make(**kw, seed=100 + i))
+        mirrors.append(Mirror(port, kw, 100 + i, V))
+    rng = np.random.default_rng(11)
+    fed = np.full(B, BOS, np.int32)
+    checked = total = 0
+    for step in range(60):
+        scale = rng.uniform(1.0, 5.0, size=(B, 1))
+        logits = (rng.standard_normal((B, V)) * scale).astype(np.float32)
+        d = dev(torch_cuda, logits)
+        got = kv.sample_logits(slots, d.data_ptr(), V, fed_ids=fed)
+        for b in range(B):
+            tok, m = mirrors[b].step(logits[b], int(fed[b]))
+            total += 1
+            if got[b] != tok:
+                assert m <= MARGIN, (b, step, got[b], tok, m)
+            elif m > MARGIN:
+                checked += 1
+        fed = got.astype(np.int32)
+    assert checked >= 0.9 * total, (checked, total)
+    for b in range(B):
+        st, n = kv.sampling_state(b)
+        assert n == 60
+        np.testing.assert_array_equal(st, mirrors[b].st)
+    kv.close()
+
+
+def test_generator_state_across_refreshes(sctx, port, torch_cuda):
+    # 400 sampled steps draw 800 numbers: the 624-word state is refreshed twice on the device.
+    V = TINY.vocab
+    kv = sctx.kv_arena(2, 8, 8)
+    kv.set_sampling(0, Sampling.make(temperature=1.0, seed=5489))
+    kv.set_sampling(1, Sampling.make(temperature=0.8, top_k=64, seed=7))
+    mir = [Mirror(port, dict(temperature=1.0), 5489, V),
+           Mirror(port, dict(temperature=0.8, top_k=64), 7, V)]
+    rng = np.random.default_rng(3)
+    logits = (rng.standard_normal((2, V)) * 2).astype(np.float32)
+    d = dev(torch_cuda, logits)
+    fed = np.full(2, BOS, np.int32)
+    for step in range(400):
+        got = kv.sample_logits([0, 1], d.data_ptr(), V, fed_ids=fed)
+        for b in range(2):
+            tok, m = mir[b].step(logits[b], int(fed[b]))
+            assert got[b] == tok or m <= MARGIN, (b, step)
+        fed = got.astype(np.int32)
+    for b in range(2):
+        st, n = kv.sampling_state(b)
+        np.testing.assert_array_equal(st, mir[b].st)
+        assert n == 400
+    kv.close()
+
+
+def test_crafted_rows_ties_masks_and_extremes(sctx, port, torch_cuda):
+    # Exact ties at the top-k / top-p cut, -inf and -1e9 entries, min_length masking EOS/PAD, one
+    # finite logit. Where tied values straddle a cut the margin is 0 (the reference's order is
+    # unspecified there); the device's documented rule, lowest index first, is checked directly.
+    V = TINY.vocab
+    rows = []
+    r = np.full(V, -5.0, np.float32)
+    r[[5, 10, 15]] = [2.0, 1.5, 1.0]
+    rows.append(r)                                 # 4093 tied values below the top 3
+    rows.append(np.zeros(V, np.float32))           # everything tied
+    r = np.full(V, -np.inf, np.float32)
+    r[[0, 3, 17]] = [4.0, 3.0, -2.0]
+    rows.append(r)                                 # EOS/PAD best, masked by min_length
+    r = np.full(V, -1e9, np.float32)
+    r[100] = 0.0
+    rows.append(r)                                 # one real candidate
+    r = np.linspace(-3, 3, V).astype(np.float32)
+    r[::7] = 3.0
+    rows.append(r)                                 # many tied maxima
+    cfgs = [dict(temperature=0.9, top_k=50), dict(temperature=1.0, top_k=7, top_p=0.5),
+            dict(min_length=2, top_p=0.95), dict(temperature=0.0), dict(top_p=0.3),
+            dict(temperature=0.0, top_k=3), dict(temperature=1.5, top_k=4000, top_p=0.95)]
+    kv = sctx.kv_arena(len(rows), 8, 8)
+    d = dev(torch_cuda, np.stack(rows))
+    seen_tokens = {}
+    for ci, kw in enumerate(cfgs):
+        for seed in (1, 2):
+            mirrors = []
+            for i in range(len(rows)):
+                kv.set_sampling(i, Sampling.make(**kw, seed=seed * 31 + i))
+                mirrors.append(Mirror(port, kw, seed * 31 + i, V))
+            fed = np.full(len(rows), BOS, np.int32)
+            for step in range(4):
+                got = kv.sample_logits(list(range(len(rows))), d.data_ptr(), V, fed_ids=fed)
+                for i in range(len(rows)):
+                    tok, m = mirrors[i].step(rows[i], int(fed[i]))
+                    assert got[i] == tok or m <= MARGIN, (kw, seed, i, step, got[i], tok, m)
+                    seen_tokens.setdefault((ci, i), []).append(int(got[i]))
+                fed = got.astype(np.int32)
+            for i in range(len(rows)):
+                np.testing.assert_array_equal(kv.sampling_state(i)[0], mirrors[i].st)
+    # lowest index first among ties
+    assert all(t < 50 for t in seen_tokens[(0, 1)])           # top-50 of a flat row: ids 0..49
+    assert all(t < 4 for t in seen_tokens[(1, 1)])            # then top-p 0.5 of 7 equal: 0..3
+    assert all(t == 0 for t in seen_tokens[(3, 1)] + seen_tokens[(3, 4)])   # first maximum
+    assert all(t < 3 for t in seen_tokens[(5, 1)])
+    # masks and single candidates
+    for k in (0, 4):  # per seed: two steps below min_length pick 17, then EOS or PAD (top-p 0.95)
+        run = seen_tokens[(2, 2)][k:k + 4]
+        assert run[:2] == [17, 17] and set(run[2:]) <= {0, 3}, run
+    assert all(t == 100 for ci in range(len(cfgs)) for t in seen_tokens[(ci, 3)])
+    kv.close()
+
+
+def test_non_finite_rows_raise(sctx, torch_cuda):
+    # textgenerator_test.cpp:1027-1055: NaN / +inf anywhere, or no finite value, is an error.
+    from adai_b200.api import NonFiniteLogits
+    V = TINY.vocab
+    kv = sctx.kv_arena(1, 8, 8)
+    kv.set_sampling(0, Sampling.make(seed=1))
+    for bad in (np.nan, np.inf):
+        r = np.full((1, V), 0.5, np.float32)
+        r[0, 7] = bad
+        d = dev(torch_cuda, r)
+        with pytest.raises(NonFiniteLogits):
+            kv.sample_logits([0], d.data_ptr(), V, fed_ids=[BOS])
+    d = dev(torch_cuda, np.full((1, V), -np.inf, np.float32))
+    with pytest.raises(NonFiniteLogits):
+        kv.sample_logits([0], d.data_ptr(), V, fed_ids=[BOS])
+    with pytest.raises(ValueError):
+        kv.set_sampling(0, Sampling.make(repetition_penalty=0.0))
+    with pytest.raises(ValueError):
+        kv.set_sampling(0, Sampling.make(temperature=float("nan")))
+    kv.close()
+
+
+# ---- tests/textgenerator_test.cpp on the device (MockLanguageModel widened to the vocabulary) ----
+
+def mock_row(tokens, V):
+    row = np.full(V, -5.0, np.float32)
+    row[5], row[10], row[15] = 2.0, 1.5, 1.0
+    if len(tokens) >= 5:
+        row[3] = 3.0
+    if len(tokens) >= 2 and tokens[-2] == 5:
+        row[10] = 2.5
+    return row
+
+
+def dev_run(kv, torch, fn, kw, seed, prompt=(BOS,), max_length=8):
+    """TextGenerator::generate on the device, one adai_b200_sample_logits call per step."""
+    V = TINY.vocab
+    kv.set_sampling(0, Sampling.make(**kw, seed=seed), history=prompt[:-1])
+    toks = list(prompt)
+    for _ in range(max_length):
+        d = dev(torch, fn(toks)[None, :])
+        tok = int(kv.sample_logits([0], d.data_ptr(), V, fed_ids=[toks[-1]])[0])
+        toks.append(tok)
+        if tok in (kw.get("eos", 3), 0):
+            break
+    return toks
+
+
+def test_reference_sampler_cases_on_device(sctx, torch_cuda):
+    V = TINY.vocab
+    kv = sctx.kv_arena(1, 8, 8)
+    fn = lambda t: mock_row(t, V)  # noqa: E731
+    # :929-955 temperature <= 0 is greedy for every strategy
+    for T in (0.0, -0.5):
+        greedy = dev_run(kv, torch_cuda, fn, dict(temperature=T), 1)
+        for seed in (1, 7, 19):
+            for kw in (dict(top_k=50), dict(top_p=0.9), dict()):
+                assert dev_run(kv, torch_cuda, fn, dict(temperature=T, **kw), seed) == greedy
+    # :957-971 positive temperature still samples
+    outs = {tuple(dev_run(kv, torch_cuda, fn, dict(top_p=0.9), s)) for s in range(1, 11)}
+    assert len(outs) > 1
+    # :1129-1140 top_p <= 0 is top-1
+    greedy = dev_run(kv, torch_cuda, fn, dict(temperature=0.0), 1)
+    for seed in (1, 2, 3):
+        assert dev_run(kv, torch_cuda, fn, dict(top_p=0.0), seed) == greedy
+
+    # :1004-1025 min_length keeps EOS/PAD out
+    def eos_first(t):
+        r = mock_row(t, V)
+        r[3] = 10.0
+        return r
+    for kw in (dict(), dict(top_k=5), dict(top_p=0.9)):
+        out = dev_run(kv, torch_cuda, eos_first, dict(temperature=0.0, min_length=4, **kw), 42,
+                      max_length=20)
+        assert len(out) == 6 and out[-1] == 3 and all(t not in (0, 3) for t in out[1:5])
+
+    # :598-632 the penalty applies once per distinct token
+    def fixed(t):
+        r = np.full(V, -100.0, np.float32)
+        r[5], r[6] = 10.0, 8.0
+        return r
+    out = dev_run(kv, torch_cuda, fixed, dict(temperature=0.0, repetition_penalty=1.15), 42,
+                  max_length=10)
+    assert out[1:] == [5] * 10
+    # :1114-1127 the penalty runs before top-k (5 is in the prompt)
+    out = dev_run(kv, torch_cuda, fn, dict(repetition_penalty=10.0, top_k=1), 42, prompt=(2, 5),
+                  max_length=1)
+    assert len(out) == 3 and out[-1] != 5
+    kv.close()
+
+
+# ---- sampled slots inside the decode step ----
+
+def test_sampled_decode_lockstep_with_oracle(sctx, port):
+    V = TINY.vocab
+    srcs = make_sources(TINY, 8, (24, 40), 3)
+    slots = list(range(8))
+    kws = [CONFIGS[0], CONFIGS[2], CONFIGS[3], CONFIGS[4], CONFIGS[5], CONFIGS[8], None, None]
+    kv = sctx.kv_arena(8, 48, 48)
+    kv.encode(slots, srcs)
+    mirrors = {}
+    for i, kw in enumerate(kws):
+        if kw is not None:
+            kv.set_sampling(i, Sampling.make(**kw, seed=900 + i))
+            mirrors[i] = Mirror(port, kw, 900 + i, V)
+    feed = np.full(8, BOS, np.int32)
+    checked = total = 0
+    for t in range(32):
+        nxt, lg = kv.decode_step(slots, feed, want_logits=True)
+        for i in slots:
+            if i in mirrors:
+                tok, m = mirrors[i].step(lg[i], int(feed[i]))
+                total += 1
+                if nxt[i] != tok:
+                    assert m <= MARGIN, (i, t, nxt[i], tok, m)
+                elif m > MARGIN:
+                    checked += 1
+            else:  # greedy rows keep the fused first maximum of the same logits
+                assert nxt[i] == int(np.argmax(lg[i])), (i, t)
+        feed = nxt.astype(np.int32)
+    assert checked >= 0.9 * total
+    for i, mir in mirrors.items():
+        st, n = kv.sampling_state(i)
+        np.testing.assert_array_equal(st, mir.st)
+        assert n == 32
+    kv.close()
+
+
+def test_device_generate_with_sampling_equals_step_by_step(sctx):
+    srcs = make_sources(TINY, 6, (16, 48), 5)
+    slots = list(range(6))
+    kws = [CONFIGS[1], CONFIGS[3], None, CONFIGS[4], CONFIGS[6], CONFIGS[9]]
+
+    def arena():
+        kv = sctx.kv_arena(6, 40, 48)
+        kv.encode(slots, srcs)
+        for i, kw in enumerate(kws):
+            if kw is not None:
+                kv.set_sampling(i, Sampling.make(**kw, seed=77 + i))
+        return kv
+    a, b = arena(), arena()
+    feed = np.full(6, BOS, np.int32)
+    steps = []
+    for _ in range(24):
+        nxt, _ = a.decode_step(slots, feed)
+        steps.append(nxt.copy())
+        feed = nxt.astype(np.int32)
+    out = b.generate(slots, np.full(6, BOS, np.int32), 24)
+    np.testing.assert_array_equal(out, np.stack(steps, axis=1))
+    for i, kw in enumerate(kws):
+        if kw is not None:
+            np.testing.assert_array_equal(a.sampling_state(i)[0], b.sampling_state(i)[0])
+    # back to greedy after reset: slot 0 no longer samples
+    b.reset(0)
+    with pytest.raises(Exception):
+        b.sampling_state(0)
+    a.close()
+    b.close()
