@@ -255,6 +255,9 @@ def main():
     ap.add_argument("--attn-batch", type=int, default=256)
     ap.add_argument("--attn-lens", default="256,2047")
     ap.add_argument("--attn-append", type=int, default=1)
+    ap.add_argument("--sampling", default="",
+                    help="every slot samples, e.g. 'temperature=0.8,top_k=50,top_p=0.95,"
+                         "repetition_penalty=1.1' (default: greedy)")
     args = ap.parse_args()
     if args.warmup < 1 or args.steps < 1:
         ap.error("--steps and --warmup must be positive")
@@ -299,6 +302,18 @@ def main():
                       else wl.src_len[1])
     slots = np.arange(B, dtype=np.int32)
     bos = np.full(B, BOS, np.int32)
+    sampling = {}
+    for kv_pair in filter(None, args.sampling.split(",")):
+        k, v = kv_pair.split("=")
+        sampling[k.strip()] = int(v) if k.strip() in ("top_k", "min_length") else float(v)
+
+    def restart():
+        """Every slot back to position 0; a sampled slot also gets its generator re-seeded."""
+        from adai_b200.api import Sampling
+        for s in slots:
+            kv.clear_self(int(s))
+            if sampling:
+                kv.set_sampling(int(s), Sampling.make(**sampling, seed=1000 + lo + int(s)))
 
     barrier()
     t0 = time.perf_counter()
@@ -306,9 +321,9 @@ def main():
     prefill_s = reduce_max(time.perf_counter() - t0)
 
     # ---- device-resident decode: W warm-up steps, restart, K timed steps ----
+    restart()
     kv.generate(slots, bos, W)
-    for s in slots:
-        kv.clear_self(int(s))
+    restart()
     barrier()
     with ClockSampler(local) as clk:
         ids_dev = kv.generate(slots, bos, K)
@@ -317,11 +332,9 @@ def main():
     value = world * B * K / (ms_max / 1000.0)
 
     # ---- end to end through the per-step C-ABI call with host buffers ----
-    for s in slots:
-        kv.clear_self(int(s))
+    restart()
     kv.decode_step(slots, bos)          # captures the per-step graph outside the timed region
-    for s in slots:
-        kv.clear_self(int(s))
+    restart()
     feed = bos.copy()
     barrier()
     t0 = time.perf_counter()
@@ -332,8 +345,7 @@ def main():
     e2e_value = world * B * K / e2e_s
 
     # ---- per-kernel device times of a profiled step at mid-generation (roofline) ----
-    for s in slots:
-        kv.clear_self(int(s))
+    restart()
     if K >= 2:
         kv.generate(slots, bos, K // 2)
     prof = None
@@ -382,7 +394,9 @@ def main():
                        "src_len": list(wl.src_len), "decode_positions": [0, K - 1],
                        "parallelism": f"batch-sharded x{world}, no collectives",
                        "l2": "per-step working set ~9 GB >> 126 MB L2 (no flush needed)",
-                       "prefill_s": prefill_s},
+                       "prefill_s": prefill_s,
+                       "token_selection": ({"sampling": sampling} if sampling
+                                           else "greedy (fused argmax)")},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 8 * B,
                     "d2h_bytes_per_step": 4 * B + 4, "ids_match_device_loop": e2e_match},
             "gpu_launches": kernels_per_step * K,

@@ -13,6 +13,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <optional>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -118,6 +119,13 @@ class KVArena {
                                     ids.data(), next.data(), logits ? logits->data() : nullptr));
         return next;
     }
+    // Per-slot sampling (TextGenerator::generate's rules, adai_b200_kv_set_sampling); nullptr
+    // returns the slot to the fused argmax.
+    void set_sampling(int slot, const adai_b200_sampling* cfg, const std::vector<int>& history = {}) {
+        check(adai_b200_kv_set_sampling(ctx_.get(), kv_, slot, cfg,
+                                        history.empty() ? nullptr : history.data(),
+                                        static_cast<int>(history.size())));
+    }
     int max_slots() const { return max_slots_; }
     adai_b200_kv* get() const { return kv_; }
 
@@ -128,17 +136,20 @@ class KVArena {
 };
 
 // A generation request: source ids, the number of new tokens at most (TextGenerator's
-// max_length, src/TextGenerator.cpp:213-214) and the ids that end it — EOS and PAD, as
-// adai::is_stop_token decides (src/SpecialTokens.hpp:162-164).
+// max_length, src/TextGenerator.cpp:213-214), the ids that end it — EOS and PAD, as
+// adai::is_stop_token decides (src/SpecialTokens.hpp:162-164) — and, optionally, its sampling
+// configuration (InferenceRequest::gen_config, src/BatchedInferenceEngine.hpp:120) with its own
+// generator seed; without one the request is greedy.
 struct Request {
     std::vector<int> source;
     int max_length = 32;
     int bos = 2;
     std::vector<int> stop_ids = {3, 0};
+    std::optional<adai_b200_sampling> sampling;
 };
 
-// As generate_greedy returns it (src/TextGenerator.cpp:209-233): the start token, then every
-// generated id, the stop id included when one ended the request.
+// As TextGenerator::generate returns it (src/TextGenerator.cpp:519-565): the start token, then
+// every generated id, the stop id included when one ended the request.
 struct Result {
     std::vector<int> tokens;
     std::string error;  // set when this request failed; the other requests are unaffected
@@ -148,8 +159,11 @@ struct Result {
 // batch and continuous admission (the engine's v2 plan: admit and retire sequences between decode
 // steps). Up to max_slots requests decode together, one stacked step at a time. A request leaves
 // at a stop id or at its max_length, and its slot goes to the next waiting request before the next
-// step. A request that cannot be admitted (bad ids, source too long) gets its error, and the
-// others proceed. The tokens of a request do not depend on which requests share its steps.
+// step. A request that cannot be admitted (bad ids, source too long, a rejected sampling
+// configuration) gets its error, and the others proceed. Each request samples from its own
+// generator, so its tokens do not depend on the requests around it (the reference engine shares
+// one generator among all requests, src/BatchedInferenceEngine.hpp:214-217); the batch size only
+// changes how the GEMMs split their sums, which moves logits by float rounding.
 class BatchGenerator {
    public:
     explicit BatchGenerator(KVArena& kv) : kv_(kv) {}
@@ -217,6 +231,16 @@ class BatchGenerator {
                     out[who[j]].error = e.what();
                     ok[j] = false;
                 }
+            }
+        }
+        for (size_t j = 0; j < slots.size(); ++j) {
+            if (!ok[j]) continue;
+            const Request& rq = reqs[who[j]];
+            try {  // the slot's previous occupant may have sampled: always (re)configure
+                kv_.set_sampling(slots[j], rq.sampling ? &*rq.sampling : nullptr);
+            } catch (const std::exception& e) {
+                out[who[j]].error = e.what();
+                ok[j] = false;
             }
         }
         for (size_t j = 0; j < slots.size(); ++j) {

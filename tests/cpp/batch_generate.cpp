@@ -3,7 +3,10 @@
 //
 // Input (little-endian): int32 vocab, d_model, n_heads, d_ff, enc_layers, dec_layers, max_seq,
 // n_tensors; per tensor int64 count + float32[count]; int32 slots, n_requests; per request int32
-// max_length, int32 src_len, int32[src_len] ids. Output: one line per request, "i: id id ..." or
+// max_length, int32 src_len, int32[src_len] ids, int32 sampled, and when sampled is 1 the
+// adai_b200_sampling fields in order (float temperature, int32 top_k, float top_p, float
+// repetition_penalty, int32 min_length, int32 eos, int32 pad, uint32 seed). Output: one line per
+// request, "i: id id ..." or
 // "i: error: <message>". With no arguments it only checks that a context can be created and
 // prints the exception that refused it ("no-device: <type>: <message>").
 #include <cstdio>
@@ -55,6 +58,18 @@ int main(int argc, char** argv) {
         r.max_length = rd<int>(f);
         r.source.resize(static_cast<size_t>(rd<int>(f)));
         f.read(reinterpret_cast<char*>(r.source.data()), static_cast<std::streamsize>(r.source.size() * 4));
+        if (rd<int>(f)) {
+            adai_b200_sampling s{};
+            s.temperature = rd<float>(f);
+            s.top_k = rd<int>(f);
+            s.top_p = rd<float>(f);
+            s.repetition_penalty = rd<float>(f);
+            s.min_length = rd<int>(f);
+            s.eos_token_id = rd<int>(f);
+            s.pad_token_id = rd<int>(f);
+            s.seed = rd<unsigned>(f);
+            r.sampling = s;
+        }
     }
     adai_b200::Context ctx(0);
     ctx.upload(d, ptrs);

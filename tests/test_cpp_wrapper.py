@@ -45,9 +45,18 @@ def _write_requests(path, cfg, weights, slots, reqs):
             np.asarray([w.size], np.int64).tofile(f)
             np.ascontiguousarray(w, np.float32).tofile(f)
         np.asarray([slots, len(reqs)], np.int32).tofile(f)
-        for max_len, src in reqs:
+        for rq in reqs:
+            max_len, src = rq[0], rq[1]
+            smp = rq[2] if len(rq) > 2 else None
             np.asarray([max_len, len(src)], np.int32).tofile(f)
             np.asarray(src, np.int32).tofile(f)
+            np.asarray([0 if smp is None else 1], np.int32).tofile(f)
+            if smp is not None:
+                np.asarray([smp["temperature"]], np.float32).tofile(f)
+                np.asarray([smp["top_k"]], np.int32).tofile(f)
+                np.asarray([smp["top_p"], smp["repetition_penalty"]], np.float32).tofile(f)
+                np.asarray([smp["min_length"], 3, 0], np.int32).tofile(f)
+                np.asarray([smp["seed"]], np.uint32).tofile(f)
 
 
 def _greedy(model, src, max_len):
@@ -82,3 +91,65 @@ def test_batch_generator_matches_oracle(driver, tmp_path, port):
         got = [int(t) for t in rest.split()]
         want = _greedy(model, src, max_len) if max_len > 0 else [2]
         assert got == want, (i, got, want)
+
+
+def _smp(temperature=1.0, top_k=0, top_p=1.0, repetition_penalty=1.0, min_length=0, seed=1):
+    return dict(temperature=temperature, top_k=top_k, top_p=top_p,
+                repetition_penalty=repetition_penalty, min_length=min_length, seed=seed)
+
+
+@pytest.mark.gpu
+def test_batch_generator_sampled_requests(driver, tmp_path, port):
+    """Sampled and greedy requests mixed in one continuously admitted batch. Each sampled request
+    is replayed alone through the Python API with the same configuration and seed, feeding the
+    tokens the C++ run produced: the device must choose the same tokens (its own generator per
+    request), and the sampler restatement must agree on them wherever its margin allows."""
+    from adai_b200.api import Context, Sampling
+    from oracle.pyoracle import sampling_cfg
+    w = make_weights(TINY, 4, affine=True)
+    srcs = make_sources(TINY, 6, (8, 40), 4)
+    cfgs = [_smp(temperature=0.8, top_k=40, seed=11), None,
+            _smp(temperature=1.2, top_p=0.9, repetition_penalty=1.3, seed=12),
+            _smp(temperature=0.0, repetition_penalty=1.5, min_length=4, seed=13),
+            _smp(temperature=1.0, min_length=30, seed=14), _smp(temperature=0.6, seed=15)]
+    lens = [16, 10, 24, 12, 30, 20]
+    reqs = [(lens[i], srcs[i], cfgs[i]) for i in range(6)]
+    path = str(tmp_path / "req.bin")
+    _write_requests(path, TINY, w, 3, reqs)
+    out = subprocess.run([driver, path], check=True, capture_output=True, text=True,
+                         timeout=300).stdout.splitlines()
+    got = [[int(t) for t in line.split(":", 1)[1].split()] for line in out]
+    model = port.model(TINY, w)
+    assert got[1] == _greedy(model, srcs[1], lens[1])
+    ctx = Context(0)
+    ctx.upload(TINY, w)
+    kv = ctx.kv_arena(1, 48, 64)
+    checked = total = 0
+    for i, c in enumerate(cfgs):
+        if c is None:
+            continue
+        seq = got[i]
+        assert seq[0] == 2 and len(seq) >= 2
+        stopped = seq[-1] in STOP
+        assert len(seq) - 1 == lens[i] or stopped
+        assert all(t not in STOP for t in seq[1:-1])
+        if stopped:  # min_length keeps EOS / PAD out of the first min_length new tokens
+            assert len(seq) - 1 > c["min_length"]
+        kv.reset(0)
+        kv.encode([0], [srcs[i]])
+        kv.set_sampling(0, Sampling.make(**c))
+        fcfg, icfg = sampling_cfg(**{k: v for k, v in c.items() if k != "seed"})
+        st = port.mt_seed(c["seed"])
+        seen = np.zeros(TINY.vocab, np.uint8)
+        for s in range(len(seq) - 1):
+            nxt, lg = kv.decode_step([0], [seq[s]], want_logits=True)
+            assert nxt[0] == seq[s + 1], (i, s)
+            seen[seq[s]] = 1
+            tok, m = port.sample_next(lg[0], (fcfg, icfg), seen, s, st)
+            total += 1
+            if m > 1e-6:
+                assert tok == seq[s + 1], (i, s, tok, seq[s + 1], m)
+                checked += 1
+    assert checked >= 0.8 * total, (checked, total)
+    kv.close()
+    ctx.close()
