@@ -56,6 +56,7 @@ EXPORTS = [
     "adai_b200_softmax_rows", "adai_b200_layernorm_fwd", "adai_b200_add_row_bias",
     "adai_b200_activation", "adai_b200_embedding_gather_add_pe", "adai_b200_backend_bind",
     "adai_b200_kv_set_sampling", "adai_b200_kv_sampling_state", "adai_b200_sample_logits",
+    "adai_b200_checkpoint_special_tokens",
 ]
 
 # Kernel classes of adai_b200_profile_step (adai_b200_kernel_class).
@@ -110,6 +111,7 @@ def load() -> C.CDLL:
     lib.adai_b200_model_upload.argtypes = [_vp, C.POINTER(ModelDesc), C.POINTER(_vp), _vp]
     lib.adai_b200_checkpoint_config.argtypes = [C.c_char_p, C.POINTER(ModelDesc)]
     lib.adai_b200_checkpoint_read.argtypes = [C.c_char_p, C.POINTER(ModelDesc), C.POINTER(_vp)]
+    lib.adai_b200_checkpoint_special_tokens.argtypes = [C.c_char_p, _ip, _ip, _ip]
     lib.adai_b200_model_load.argtypes = [_vp, C.c_char_p, C.POINTER(ModelDesc)]
     lib.adai_b200_kv_create.argtypes = [_vp, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]
     lib.adai_b200_kv_destroy.argtypes = [_vp, _vp]
@@ -169,11 +171,20 @@ def check(rc: int) -> None:
 
 
 def checkpoint_config(directory: str) -> ModelConfig:
-    """The model shape of a SafeTensors checkpoint directory (host only)."""
+    """The model shape of a checkpoint: a SafeTensors directory or a save_model prefix (host
+    only)."""
     d = ModelDesc()
     check(load().adai_b200_checkpoint_config(os.fsencode(directory), C.byref(d)))
     return ModelConfig(d.vocab, d.d_model, d.n_heads, d.d_ff, d.enc_layers, d.dec_layers,
                        d.max_seq)
+
+
+def checkpoint_special_tokens(path: str) -> tuple[int, int, int]:
+    """(BOS, EOS, PAD) of a checkpoint (host only)."""
+    b, e, p = C.c_int(), C.c_int(), C.c_int()
+    check(load().adai_b200_checkpoint_special_tokens(os.fsencode(path), C.byref(b), C.byref(e),
+                                                     C.byref(p)))
+    return b.value, e.value, p.value
 
 
 def read_checkpoint(directory: str, cfg: ModelConfig | None = None) -> list[np.ndarray]:

@@ -8,6 +8,7 @@
 #include "checkpoint.h"
 
 #include <algorithm>
+#include <cmath>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
@@ -306,7 +307,7 @@ class SafeTensors {
 
 }  // namespace
 
-adai_b200_model_desc read_checkpoint_config(const std::string& dir) {
+adai_b200_model_desc read_safetensors_config(const std::string& dir) {
     const std::string path = dir + "/config.json";
     const std::string text = read_file(path);
     const Json cfg = JsonReader(text.data(), text.data() + text.size(), path).document();
@@ -342,8 +343,8 @@ std::vector<size_t> upload_tensor_sizes(const adai_b200_model_desc& d) {
     return n;
 }
 
-void read_checkpoint_tensors(const std::string& dir, const adai_b200_model_desc& d,
-                             const std::vector<float*>& out) {
+void read_safetensors_tensors(const std::string& dir, const adai_b200_model_desc& d,
+                              const std::vector<float*>& out) {
     const std::vector<size_t> sizes = upload_tensor_sizes(d);
     if (out.size() != sizes.size())
         throw std::invalid_argument("need " + std::to_string(sizes.size()) + " output buffers");
@@ -400,6 +401,291 @@ void read_checkpoint_tensors(const std::string& dir, const adai_b200_model_desc&
     mat("lm_head.weight", V, D);
     vec("lm_head.bias", V);
     if (k != sizes.size()) throw std::logic_error("checkpoint tensor order out of step");
+}
+
+// ---------------------------------------------------------------------------------------------
+// The reference's own checkpoint: EncoderDecoderModel::save_model(P) (src/EncoderDecoderModel.cpp:
+// 960-985) writes P.config, P.encoder, P.decoder and P.lm_head, and the encoder and decoder write
+// one file per component next to them (src/LLMEncoder.cpp:271-292, src/Decoder.cpp:396-416,
+// src/EncoderBlock.cpp:207-229, src/DecoderBlock.cpp:567-621). Every file is a sequence of
+// native-endian int32 / float / uint8 values and row-major float matrices with nothing between
+// them (adai::binio, src/BinaryIO.cpp); the reference's loaders check each shape and that nothing
+// follows the last value.
+namespace {
+
+constexpr int32_t kBinaryConfigMarker = -20260721;  // src/EncoderDecoderModel.cpp:128
+constexpr int32_t kBinaryConfigVersion = 2;         // :129, pre-LN blocks
+
+struct BinaryConfig {
+    adai_b200_model_desc d{};
+    int bos = 2, eos = 3, pad = 0;
+};
+
+bool file_exists(const std::string& path) {
+    std::ifstream f(path, std::ios::binary);
+    return static_cast<bool>(f);
+}
+
+class BinFile {
+   public:
+    explicit BinFile(const std::string& path) : path_(path), f_(path, std::ios::binary) {
+        if (!f_) throw CheckpointIoError("Failed to open file for reading: " + path);
+    }
+    template <class T>
+    T value(const char* what) {
+        T v{};
+        bytes(&v, sizeof v, what);
+        return v;
+    }
+    void floats(float* dst, size_t n, const char* what) { bytes(dst, n * sizeof(float), what); }
+    // Matches an int32 field against the model's value (the reference's dimension checks).
+    void expect_int(int want, const char* what) {
+        const int got = value<int32_t>(what);
+        if (got != want)
+            throw std::invalid_argument("Dimension mismatch in " + path_ + ": " + what + " is " +
+                                        std::to_string(got) + ", the model has " + std::to_string(want));
+    }
+    void expect_end() {
+        if (f_.peek() != std::char_traits<char>::eof())
+            throw std::invalid_argument("Unexpected trailing data in " + path_ +
+                                        " (the file doesn't match this model's shapes)");
+    }
+
+   private:
+    void bytes(void* dst, size_t n, const char* what) {
+        f_.read(static_cast<char*>(dst), static_cast<std::streamsize>(n));
+        if (static_cast<size_t>(f_.gcount()) != n)
+            throw CheckpointIoError("Truncated or unreadable file " + path_ + " (reading " + what + ")");
+    }
+    std::string path_;
+    std::ifstream f_;
+};
+
+BinaryConfig read_binary_config(const std::string& prefix) {
+    BinFile f(prefix + ".config");
+    if (f.value<int32_t>("format marker") != kBinaryConfigMarker)
+        throw std::invalid_argument(prefix + ".config: checkpoint format marker missing/invalid "
+                                    "(a checkpoint saved before the pre-LN blocks)");
+    const int32_t version = f.value<int32_t>("format version");
+    if (version < kBinaryConfigVersion)
+        throw std::invalid_argument(prefix + ".config: unsupported older checkpoint format_version " +
+                                    std::to_string(version));
+    BinaryConfig c;
+    c.d.vocab = f.value<int32_t>("architecture");
+    c.d.d_model = f.value<int32_t>("architecture");
+    c.d.enc_layers = f.value<int32_t>("architecture");
+    c.d.dec_layers = f.value<int32_t>("architecture");
+    c.d.n_heads = f.value<int32_t>("architecture");
+    c.d.d_ff = f.value<int32_t>("architecture");
+    c.d.max_seq = f.value<int32_t>("architecture");
+    c.bos = f.value<int32_t>("architecture");
+    c.eos = f.value<int32_t>("architecture");
+    c.pad = f.value<int32_t>("architecture");
+    f.expect_end();
+    return c;
+}
+
+// LayerNorm::load_weights (src/LayerNorm.cpp:277-301): dim, epsilon, gamma, beta. The device
+// kernels normalise with epsilon 1e-5, the reference's default (src/LayerNorm.hpp:70).
+void read_norm_file(const std::string& path, int D, float* g, float* b) {
+    BinFile f(path);
+    f.expect_int(D, "dim");
+    const float eps = f.value<float>("eps");
+    if (!(eps > 0.0f) || !std::isfinite(eps))
+        throw std::invalid_argument(path + ": epsilon " + std::to_string(eps) +
+                                    " is not a positive finite number");
+    if (eps != 1e-5f)
+        throw std::invalid_argument(path + ": LayerNorm epsilon " + std::to_string(eps) +
+                                    " differs from the 1e-5 the device kernels use");
+    f.floats(g, D, "gamma");
+    f.floats(b, D, "beta");
+    f.expect_end();
+}
+
+// TokenEmbedding::load_pretrained (src/TokenEmbedding.cpp:158-178).
+void read_embedding_file(const std::string& path, int V, int D, float* out) {
+    BinFile f(path);
+    f.expect_int(V, "vocab_size");
+    f.expect_int(D, "d_model");
+    f.floats(out, static_cast<size_t>(V) * D, "embedding matrix");
+    f.expect_end();
+}
+
+// MultiHeadAttention::load_weights (src/MultiHeadAttention.cpp:682-708).
+void read_attention_file(const std::string& path, int D, int H, float* const* w) {
+    BinFile f(path);
+    f.expect_int(D, "d_model");
+    f.expect_int(H, "num_heads");
+    for (int i = 0; i < 4; ++i) f.floats(w[i], static_cast<size_t>(D) * D, "W_q / W_k / W_v / W_o");
+    f.expect_end();
+}
+
+// CrossAttention::load (src/CrossAttention.cpp:811-836).
+void read_cross_attention_file(const std::string& path, int D, int H, float* const* w) {
+    BinFile f(path);
+    f.expect_int(D, "d_model");
+    f.expect_int(H, "num_heads");
+    f.value<float>("learning_rate");
+    for (int i = 0; i < 4; ++i) f.floats(w[i], static_cast<size_t>(D) * D, "W_q / W_k / W_v / W_o");
+    f.expect_end();
+}
+
+// FeedForward::load_weights (src/FeedForward.cpp:296-320): W1 [D,F], W2 [F,D], b1, b2 — stored in
+// that order; the upload order is W1 b1 W2 b2.
+void read_ffn_file(const std::string& path, int D, int F, float* w1, float* b1, float* w2, float* b2) {
+    BinFile f(path);
+    f.expect_int(D, "d_model");
+    f.expect_int(F, "d_ff");
+    f.floats(w1, static_cast<size_t>(D) * F, "W1");
+    f.floats(w2, static_cast<size_t>(F) * D, "W2");
+    f.floats(b1, F, "b1");
+    f.floats(b2, D, "b2");
+    f.expect_end();
+}
+
+// LLMEncoder / LLMDecoder header: vocab, d_model, layers, heads, d_ff, max_seq_length (which the
+// reference does not check: no weight depends on it).
+void read_stack_header(const std::string& path, const adai_b200_model_desc& d, int layers) {
+    BinFile f(path);
+    f.expect_int(d.vocab, "vocab_size");
+    f.expect_int(d.d_model, "d_model");
+    f.expect_int(layers, "num_layers");
+    f.expect_int(d.n_heads, "num_heads");
+    f.expect_int(d.d_ff, "d_ff");
+    f.value<int32_t>("max_seq_length");
+    f.expect_end();
+}
+
+std::string strip_ext(const std::string& p) { return p.substr(0, p.find_last_of('.')); }
+
+void read_binary_tensors(const std::string& prefix, const adai_b200_model_desc& d,
+                         const std::vector<float*>& out) {
+    const int V = d.vocab, D = d.d_model, H = d.n_heads, F = d.d_ff;
+    size_t k = 0;
+    // encoder (src/LLMEncoder.cpp:296-350); base strips ".encoder"
+    read_stack_header(prefix + ".encoder", d, d.enc_layers);
+    const std::string base = strip_ext(prefix + ".encoder");
+    // pre-TD-538 checkpoints hold only the shared names (the decoder's copies), which the
+    // reference then loads for the encoder too
+    auto enc_part = [&](const std::string& name) {
+        const std::string cur = base + "_encoder_" + name;
+        return file_exists(cur) ? cur : base + "_" + name;
+    };
+    read_embedding_file(enc_part("token_emb.bin"), V, D, out[k++]);
+    for (int i = 0; i < d.enc_layers; ++i) {
+        const std::string blk = base + "_encoder_block_" + std::to_string(i) + ".bin";
+        {  // EncoderBlock::load_weights (src/EncoderBlock.cpp:231-259)
+            BinFile f(blk);
+            f.expect_int(D, "d_model");
+            f.expect_int(H, "num_heads");
+            f.expect_int(F, "d_ff");
+            f.value<float>("dropout_rate");
+            f.floats(out[k], D, "norm1 gamma");
+            f.floats(out[k + 1], D, "norm1 beta");
+            f.floats(out[k + 6], D, "norm2 gamma");
+            f.floats(out[k + 7], D, "norm2 beta");
+            f.expect_end();
+        }
+        const std::string bb = strip_ext(blk);
+        read_attention_file(bb + "_attention.bin", D, H, &out[k + 2]);
+        read_ffn_file(bb + "_feedforward.bin", D, F, out[k + 8], out[k + 9], out[k + 10], out[k + 11]);
+        k += 12;
+    }
+    read_norm_file(enc_part("final_norm.bin"), D, out[k], out[k + 1]);
+    k += 2;
+    // decoder (src/Decoder.cpp:418-452)
+    read_stack_header(prefix + ".decoder", d, d.dec_layers);
+    const std::string dbase = strip_ext(prefix + ".decoder");
+    read_embedding_file(dbase + "_token_emb.bin", V, D, out[k++]);
+    for (int i = 0; i < d.dec_layers; ++i) {
+        const std::string blk = dbase + "_decoder_block_" + std::to_string(i) + ".bin";
+        {  // DecoderBlock::load (src/DecoderBlock.cpp:623-689)
+            BinFile f(blk);
+            f.expect_int(D, "d_model");
+            f.expect_int(H, "num_heads");
+            f.expect_int(F, "d_ff");
+            f.value<float>("dropout_rate");
+            f.value<float>("learning_rate");
+            f.floats(out[k], D, "norm1 gamma");
+            f.floats(out[k + 1], D, "norm1 beta");
+            f.floats(out[k + 6], D, "norm2 gamma");
+            f.floats(out[k + 7], D, "norm2 beta");
+            f.floats(out[k + 12], D, "norm3 gamma");
+            f.floats(out[k + 13], D, "norm3 beta");
+            for (const char* what : {"world-model flag", "hippocampal flag"}) {
+                if (f.value<uint8_t>(what) != 0)
+                    throw std::invalid_argument(
+                        blk + ": the block has a gated " +
+                        std::string(what).substr(0, std::string(what).size() - 5) +
+                        " cross-attention path, which the device decode step does not run");
+            }
+            f.expect_end();
+        }
+        read_attention_file(blk + ".self_attn", D, H, &out[k + 2]);
+        read_cross_attention_file(blk + ".cross_attn", D, H, &out[k + 8]);
+        read_ffn_file(blk + ".ff", D, F, out[k + 14], out[k + 15], out[k + 16], out[k + 17]);
+        k += 18;
+    }
+    read_norm_file(dbase + "_final_norm.bin", D, out[k], out[k + 1]);
+    k += 2;
+    {  // LanguageModelHead::load (src/LanguageModelHead.cpp:128-143)
+        BinFile f(prefix + ".lm_head");
+        f.expect_int(D, "d_model");
+        f.expect_int(V, "vocab_size");
+        f.floats(out[k++], static_cast<size_t>(D) * V, "W_output");
+        f.floats(out[k++], V, "bias");
+        f.expect_end();
+    }
+    if (k != out.size()) throw std::logic_error("binary checkpoint tensor order out of step");
+}
+
+bool is_safetensors_dir(const std::string& path) { return file_exists(path + "/config.json"); }
+
+void require_checkpoint(const std::string& path) {
+    if (!is_safetensors_dir(path) && !file_exists(path + ".config"))
+        throw CheckpointIoError("no checkpoint at " + path + " (neither " + path +
+                                "/config.json nor " + path + ".config)");
+}
+
+}  // namespace
+
+adai_b200_model_desc read_checkpoint_config(const std::string& path) {
+    require_checkpoint(path);
+    return is_safetensors_dir(path) ? read_safetensors_config(path) : read_binary_config(path).d;
+}
+
+void read_checkpoint_tensors(const std::string& path, const adai_b200_model_desc& d,
+                             const std::vector<float*>& out) {
+    require_checkpoint(path);
+    if (out.size() != upload_tensor_sizes(d).size())
+        throw std::invalid_argument("need " + std::to_string(upload_tensor_sizes(d).size()) +
+                                    " output buffers");
+    if (is_safetensors_dir(path)) {
+        read_safetensors_tensors(path, d, out);
+        return;
+    }
+    const BinaryConfig c = read_binary_config(path);
+    if (std::memcmp(&c.d, &d, sizeof d) != 0)
+        throw std::invalid_argument("Model architecture mismatch between " + path +
+                                    ".config and the requested model");
+    read_binary_tensors(path, d, out);
+}
+
+void read_checkpoint_special_tokens(const std::string& path, int* bos, int* eos, int* pad) {
+    require_checkpoint(path);
+    if (is_safetensors_dir(path)) {
+        const std::string cfg_path = path + "/config.json";
+        const std::string text = read_file(cfg_path);
+        const Json cfg = JsonReader(text.data(), text.data() + text.size(), cfg_path).document();
+        *bos = config_int(cfg, "decoder_start_token_id", cfg_path);
+        *eos = config_int(cfg, "eos_token_id", cfg_path);
+        *pad = config_int(cfg, "pad_token_id", cfg_path);
+        return;
+    }
+    const BinaryConfig c = read_binary_config(path);
+    *bos = c.bos;
+    *eos = c.eos;
+    *pad = c.pad;
 }
 
 }  // namespace adai_b200

@@ -1040,6 +1040,17 @@ int adai_b200_checkpoint_config(const char* dir, adai_b200_model_desc* out) {
     });
 }
 
+int adai_b200_checkpoint_special_tokens(const char* path, int* bos, int* eos, int* pad) {
+    return guarded([&] {
+        if (!path) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null argument");
+        int b = 0, e = 0, p = 0;
+        read_checkpoint_special_tokens(path, &b, &e, &p);
+        if (bos) *bos = b;
+        if (eos) *eos = e;
+        if (pad) *pad = p;
+    });
+}
+
 int adai_b200_checkpoint_read(const char* dir, const adai_b200_model_desc* d, float* const* t) {
     return guarded([&] {
         if (!dir || !t) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null argument");
@@ -1059,7 +1070,7 @@ int adai_b200_model_load(adai_b200_ctx* c, const char* dir, const adai_b200_mode
         const adai_b200_model_desc d = read_checkpoint_config(dir);
         if (expect && std::memcmp(expect, &d, sizeof d) != 0)
             fail(ADAI_B200_ERR_INVALID_ARGUMENT,
-                 "architecture mismatch between " + std::string(dir) + "/config.json (vocab " +
+                 "architecture mismatch between the checkpoint " + std::string(dir) + " (vocab " +
                      std::to_string(d.vocab) + ", d_model " + std::to_string(d.d_model) + ", heads " +
                      std::to_string(d.n_heads) + ", d_ff " + std::to_string(d.d_ff) + ", layers " +
                      std::to_string(d.enc_layers) + "+" + std::to_string(d.dec_layers) +

@@ -98,23 +98,40 @@ ADAI_B200_API int adai_b200_model_tensor_count(const adai_b200_model_desc* desc)
 ADAI_B200_API int adai_b200_model_upload(adai_b200_ctx* ctx, const adai_b200_model_desc* desc,
                            const float* const* tensors, const float* pe_table);
 
-/* ---- checkpoints: the reference's SafeTensors directories (ModelSerializer::export_safetensors /
- * import_safetensors, src/ModelSerializer.cpp:243-391 and :395-579): <dir>/config.json and
- * <dir>/model.safetensors, T5-style tensor names, projections stored [out, in], F32 ----
- * Reads the model shape from <dir>/config.json. Host only (no device needed). */
-ADAI_B200_API int adai_b200_checkpoint_config(const char* dir, adai_b200_model_desc* out);
-/* Reads <dir>/model.safetensors into caller buffers, in the order and layouts of
- * adai_b200_model_upload (projections back to W[in, out]). A file with no
- * model.decoder.embed_tokens.weight gives the decoder model.shared.weight, and one with no final
- * LayerNorm gives gamma 1 / beta 0, as the reference's import does. Tensors not used here are
- * ignored. Host only. Errors: ADAI_B200_ERR_INVALID_ARGUMENT naming the tensor (missing, wrong
- * shape, dtype other than F32, malformed header), ADAI_B200_ERR_IO (unreadable file). */
-ADAI_B200_API int adai_b200_checkpoint_read(const char* dir, const adai_b200_model_desc* desc,
+/* ---- checkpoints (host only, no device needed unless stated). `path` is either
+ * (1) a SafeTensors directory (ModelSerializer::export_safetensors / import_safetensors,
+ *     src/ModelSerializer.cpp:243-391 and :395-579): path/config.json and path/model.safetensors,
+ *     T5-style tensor names, projections stored [out, in], F32; or
+ * (2) the prefix given to the reference's EncoderDecoderModel::save_model (src/EncoderDecoderModel.cpp:
+ *     960-985): path.config, path.encoder, path.decoder, path.lm_head and the per-component files
+ *     the encoder and decoder write beside them, in the adai::binio layout (src/BinaryIO.cpp).
+ * The format is told by which of path/config.json and path.config exists. ----
+ * Reads the model shape. */
+ADAI_B200_API int adai_b200_checkpoint_config(const char* path, adai_b200_model_desc* out);
+/* The checkpoint's BOS, EOS and PAD ids (config.json: decoder_start_token_id, eos_token_id,
+ * pad_token_id; path.config: its last three fields). Any output may be NULL. */
+ADAI_B200_API int adai_b200_checkpoint_special_tokens(const char* path, int* bos, int* eos,
+                                                      int* pad);
+/* Reads the tensors into caller buffers, in the order and layouts of adai_b200_model_upload.
+ * SafeTensors: projections back to W[in, out]; a file with no model.decoder.embed_tokens.weight
+ * gives the decoder model.shared.weight, and one with no final LayerNorm gives gamma 1 / beta 0,
+ * as the reference's import does; tensors not used here are ignored.
+ * save_model files: every file is checked as the reference's loaders check it (each dimension,
+ * no trailing bytes); an encoder without its own token_emb / final_norm files takes the shared
+ * path_token_emb.bin / path_final_norm.bin, as the reference does for older checkpoints
+ * (src/LLMEncoder.cpp:326-349). Final LayerNorm files must hold epsilon 1e-5 (the kernels' value,
+ * the reference's default), and decoder blocks with a gated world-model or hippocampal path are
+ * refused.
+ * Errors: ADAI_B200_ERR_INVALID_ARGUMENT naming the tensor or file (missing tensor, wrong shape or
+ * dimension, dtype other than F32, trailing data, bad format marker), ADAI_B200_ERR_IO (a file that
+ * is missing, unreadable or cut short). */
+ADAI_B200_API int adai_b200_checkpoint_read(const char* path, const adai_b200_model_desc* desc,
                                             float* const* tensors);
 /* adai_b200_checkpoint_config + adai_b200_checkpoint_read + adai_b200_model_upload. When expect
- * is non-NULL the checkpoint's shape must equal it (the reference's architecture check,
- * src/ModelSerializer.cpp:410-432), else ADAI_B200_ERR_INVALID_ARGUMENT. */
-ADAI_B200_API int adai_b200_model_load(adai_b200_ctx* ctx, const char* dir,
+ * is non-NULL the checkpoint's shape must equal it (the reference's architecture checks,
+ * src/ModelSerializer.cpp:410-432, src/EncoderDecoderModel.cpp:1030-1047), else
+ * ADAI_B200_ERR_INVALID_ARGUMENT. */
+ADAI_B200_API int adai_b200_model_load(adai_b200_ctx* ctx, const char* path,
                                        const adai_b200_model_desc* expect);
 
 /* ---- KV cache arena (replaces GPUDecoderKVCache, src/gpu/MatrixGPU.hpp:563-623, and the CPU

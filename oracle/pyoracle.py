@@ -246,6 +246,7 @@ class Ref(_Base):
                                      C.POINTER(C.c_double)]
         lib.ref_sample_generate.argtypes = [_f32p, C.c_int, C.c_int, _f32p, _i32p, C.c_uint,
                                             C.c_void_p, C.c_int, _i32p, C.POINTER(C.c_int)]
+        lib.ref_model_save.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_int, C.c_int]
         self.lib = lib
 
     def sample_generate(self, logits, cfg, seed, prompt=None):
@@ -322,6 +323,10 @@ class _RefModel:
         out = np.empty((ids.size, self.cfg.d_model), np.float32)
         self.ref._check(self.ref.lib.ref_encode(self.h, ids, ids.size, out))
         return out
+
+    def save(self, prefix, bos=2, eos=3, pad=0):
+        """The reference's own checkpoint files (EncoderDecoderModel::save_model layout)."""
+        self.ref._check(self.ref.lib.ref_model_save(self.h, os.fsencode(prefix), bos, eos, pad))
 
     def generate_timed(self, src, steps, bos=2):
         """Greedy decode; returns (ids, per-step wall seconds, encoder seconds)."""

@@ -27,6 +27,7 @@
 #include <vector>
 
 #include "Activation.hpp"
+#include "BinaryIO.hpp"
 #include "Decoder.hpp"
 #include "KVCache.hpp"
 #include "LanguageModelHead.hpp"
@@ -292,6 +293,27 @@ int ref_attention_single(const float* q, const float* K, const float* Vv, int T,
             Matrix o = w * Vh;
             for (int j = 0; j < dk; ++j) out[h * dk + j] = o.data[0][j];
         }
+    });
+}
+
+// The model's weights in the reference's own checkpoint files, as EncoderDecoderModel::save_model
+// (src/EncoderDecoderModel.cpp:960-985) writes them: prefix.config through adai::binio with the
+// format marker and version that save_model writes, then the encoder's, decoder's and head's own
+// save_weights (which write their per-component files). The tokenizer's prefix.vocab is not
+// written (it is not part of the decode arithmetic).
+int ref_model_save(void* h, const char* prefix, int bos, int eos, int pad) {
+    return guarded([&] {
+        auto* m = static_cast<RefModel*>(h);
+        const std::string p(prefix);
+        adai::binio::Writer cfg(p + ".config");
+        cfg.value(static_cast<int32_t>(-20260721), "format marker");
+        cfg.value(static_cast<int32_t>(2), "format version");
+        for (int field : {m->V, m->D, m->Le, m->L, m->H, m->F, m->max_seq, bos, eos, pad})
+            cfg.value(field, "architecture");
+        cfg.close();
+        m->enc->save_weights(p + ".encoder");
+        m->dec->save_weights(p + ".decoder");
+        m->head->save_weights(p + ".lm_head");
     });
 }
 
