@@ -4,10 +4,18 @@
 // temperature, top-k, top-p, then the argmax (temperature <= 0) or one draw from the slot's own
 // std::mt19937 through std::discrete_distribution, as libstdc++ computes both (:145-148).
 //
-// One CTA of 1024 threads per row. The row is held in shared memory; warp w owns the contiguous
-// index range [w*span, (w+1)*span) and reads it 32 consecutive elements at a time, so every pass is
-// coalesced and free of bank conflicts and the index order needed for tie ranks and the
-// cumulative sum is the (warp, iteration, lane) order.
+// One CTA of 1024 threads per row. The row is held in shared memory, padded to 32 equal warp
+// ranges: warp w owns the contiguous index range [w*span, (w+1)*span) and reads it 32 consecutive
+// elements at a time, so every pass is coalesced and free of bank conflicts, and the index order
+// needed for tie ranks and the cumulative sum is the (warp, iteration, lane) order. The padding
+// holds values that no pass can select (-inf logits, key 0, probability 0), so the inner loops
+// carry no bounds test.
+//
+// The two cuts are found by bisection over 32-bit patterns: top-k over an order-preserving key of
+// the logit, top-p over the bit pattern of the probability (which orders like the value, as it is
+// never negative). Each step is one pass over the row and one block reduction with a single
+// barrier. Before a bisection the row is rewritten in place as those patterns, so a pass is a
+// load, a compare and an add.
 //
 // Where the reference works in float and the device in double (the top-p running sum, the
 // cumulative distribution), the two agree except when the decision lies within rounding distance
@@ -26,119 +34,90 @@ constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
 constexpr unsigned kFull = 0xffffffffu;
 
+// Elements per warp range: a multiple of 32, kWarps ranges cover the vocabulary.
+__host__ __device__ inline int span_of(int V) { return ((V + kWarps - 1) / kWarps + 31) & ~31; }
+
 // Order-preserving key of a non-NaN float (larger float, larger key); -0 and +0 share one key, as
-// they compare equal.
+// they compare equal. Every key of a float is at least 0x007fffff (that of -inf), so key 0 can
+// mark padding.
 __device__ __forceinline__ unsigned fkey(float f) {
     if (f == 0.0f) f = 0.0f;
     const unsigned u = __float_as_uint(f);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
+__device__ __forceinline__ float key_value(unsigned k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
 
+// Reduction slots are double-buffered: a reduction writes one buffer, passes one barrier and reads
+// it back; the next reduction writes the other buffer, so a write never meets a read still in
+// progress (the barrier of the reduction in between orders them).
 struct Smem {
-    double red_d[kWarps];
-    int red_i[kWarps];
-    int red_j[kWarps];
-    float red_f[kWarps];
+    double rd[2][kWarps];
+    int ri[2][kWarps];
+    int rj[2][kWarps];
+    float rf[2][kWarps];
     int tie_base[kWarps];
     unsigned mt[624];
     unsigned draw[2];
-    double bcast_d;
     int bcast_i;
-    float bcast_f;
 };
 
-__device__ __forceinline__ double block_sum_d(double v, Smem& s) {
+template <class T, class Op>
+__device__ __forceinline__ T warp_all(T v, Op op) {
 #pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    __syncthreads();
-    if (l == 0) s.red_d[w] = v;
-    __syncthreads();
-    if (w == 0) {
-        // fixed order: warp sums added lane 0 .. 31 by a tree whose shape does not depend on data
-        double t = s.red_d[l];
-#pragma unroll
-        for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(kFull, t, o);
-        if (l == 0) s.bcast_d = t;
-    }
-    __syncthreads();
-    return s.bcast_d;
+    for (int o = 16; o; o >>= 1) v = op(v, __shfl_xor_sync(kFull, v, o));
+    return v;
 }
 
-__device__ __forceinline__ int block_sum_i(int v, Smem& s) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+// Block reductions, one barrier each; every warp folds the 32 warp results itself in a fixed
+// order, so all threads return the same value.
+__device__ __forceinline__ double bsum_d(double v, Smem& s, int& ph) {
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    auto add = [](double a, double b) { return a + b; };
+    v = warp_all(v, add);
+    if (l == 0) s.rd[ph][w] = v;
     __syncthreads();
-    if (l == 0) s.red_i[w] = v;
-    __syncthreads();
-    if (w == 0) {
-        int t = s.red_i[l];
-#pragma unroll
-        for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(kFull, t, o);
-        if (l == 0) s.bcast_i = t;
-    }
-    __syncthreads();
-    return s.bcast_i;
+    const double t = warp_all(s.rd[ph][l], add);
+    ph ^= 1;
+    return t;
 }
-
-__device__ __forceinline__ float block_max_f(float v, Smem& s) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+__device__ __forceinline__ int bsum_i(int v, Smem& s, int& ph) {
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    auto add = [](int a, int b) { return a + b; };
+    v = warp_all(v, add);
+    if (l == 0) s.ri[ph][w] = v;
     __syncthreads();
-    if (l == 0) s.red_f[w] = v;
-    __syncthreads();
-    if (w == 0) {
-        float t = s.red_f[l];
-#pragma unroll
-        for (int o = 16; o; o >>= 1) t = fmaxf(t, __shfl_xor_sync(kFull, t, o));
-        if (l == 0) s.bcast_f = t;
-    }
-    __syncthreads();
-    return s.bcast_f;
+    const int t = warp_all(s.ri[ph][l], add);
+    ph ^= 1;
+    return t;
 }
-
+__device__ __forceinline__ float bmax_f(float v, Smem& s, int& ph) {
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    auto mx = [](float a, float b) { return fmaxf(a, b); };
+    v = warp_all(v, mx);
+    if (l == 0) s.rf[ph][w] = v;
+    __syncthreads();
+    const float t = warp_all(s.rf[ph][l], mx);
+    ph ^= 1;
+    return t;
+}
 // Float sum of the block in a fixed tree order (the reference sums left to right; the difference
 // is a common factor of every probability and cancels in the normalised distribution).
-__device__ __forceinline__ float block_sum_f(float v, Smem& s) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+__device__ __forceinline__ float bsum_f(float v, Smem& s, int& ph) {
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    auto add = [](float a, float b) { return a + b; };
+    v = warp_all(v, add);
+    if (l == 0) s.rf[ph][w] = v;
     __syncthreads();
-    if (l == 0) s.red_f[w] = v;
-    __syncthreads();
-    if (w == 0) {
-        float t = s.red_f[l];
-#pragma unroll
-        for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(kFull, t, o);
-        if (l == 0) s.bcast_f = t;
-    }
-    __syncthreads();
-    return s.bcast_f;
+    const float t = warp_all(s.rf[ph][l], add);
+    ph ^= 1;
+    return t;
 }
-
-// First index of the maximum over the block (value, index) pairs.
-__device__ __forceinline__ int block_argmax(float v, int j, Smem& s) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        const float ov = __shfl_xor_sync(kFull, v, o);
-        const int oj = __shfl_xor_sync(kFull, j, o);
-        if (ov > v || (ov == v && oj < j)) {
-            v = ov;
-            j = oj;
-        }
-    }
+// First index of the maximum over the block's (value, index) pairs.
+__device__ __forceinline__ int bargmax(float v, int j, Smem& s, int& ph) {
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    __syncthreads();
-    if (l == 0) {
-        s.red_f[w] = v;
-        s.red_j[w] = j;
-    }
-    __syncthreads();
-    if (w == 0) {
-        v = s.red_f[l];
-        j = s.red_j[l];
+    auto fold = [&]() {
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
             const float ov = __shfl_xor_sync(kFull, v, o);
@@ -148,15 +127,23 @@ __device__ __forceinline__ int block_argmax(float v, int j, Smem& s) {
                 j = oj;
             }
         }
-        if (l == 0) s.bcast_i = j;
+    };
+    fold();
+    if (l == 0) {
+        s.rf[ph][w] = v;
+        s.rj[ph][w] = j;
     }
     __syncthreads();
-    return s.bcast_i;
+    v = s.rf[ph][l];
+    j = s.rj[ph][l];
+    fold();
+    ph ^= 1;
+    return j;
 }
 
-// MT19937 state refresh (the published recurrence) in three data-parallel phases: entries
-// [0,227) read only old words; [227,454) read the new words 227 places back; [454,623) likewise;
-// 623 reads the new word 0. Each phase reads into registers before anyone writes.
+// MT19937 state refresh (the published recurrence) in data-parallel phases: entries [0,227) read
+// only old words; [227,454) read the new words 227 places back; [454,623) likewise; 623 reads the
+// new word 0. Each phase reads into registers before anyone writes.
 __device__ void mt_twist_block(unsigned* g, Smem& s) {
     const int t = threadIdx.x;
     for (int i = t; i < 624; i += kThreads) s.mt[i] = g[i];
@@ -211,72 +198,68 @@ __device__ double draw_canonical(unsigned* g, Smem& s) {
     return r;
 }
 
-// Keeps the elements whose key is above `thr`, and of those equal to it the first `need` by index;
-// the others become -1e9f. keys(j) computes the key of element j.
-template <class KeyFn>
-__device__ void keep_above(float* x, int V, int span, unsigned thr, int need, int n_eq, KeyFn keys,
-                           Smem& s) {
+// Largest pattern t with count(pattern >= t) >= k (the k-th largest pattern), by bisection over
+// the 32 bits; patterns are the row rewritten in place, padding 0.
+__device__ unsigned kth_pattern(const unsigned* xu, int span, int k, Smem& s, int& ph) {
+    const int base = (threadIdx.x >> 5) * span + (threadIdx.x & 31);
+    unsigned thr = 0;
+    for (int bit = 31; bit >= 0; --bit) {
+        const unsigned cand = thr | (1u << bit);
+        int c = 0;
+#pragma unroll 8
+        for (int i = 0; i < span; i += 32) c += xu[base + i] >= cand ? 1 : 0;
+        if (bsum_i(c, s, ph) >= k) thr = cand;
+    }
+    return thr;
+}
+
+// The exclusive prefix over warps of each warp's count of patterns equal to thr (tie ranks in
+// index order), left in s.tie_base.
+__device__ void tie_prefix(const unsigned* xu, int span, unsigned thr, Smem& s) {
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    const int base = w * span;
-    if (need >= n_eq) {  // no tie to break
-        for (int i = 0; i < span; i += 32) {
-            const int j = base + i + l;
-            if (j < V && keys(j) < thr) x[j] = -1e9f;
-        }
-        __syncthreads();
-        return;
-    }
+    const int base = w * span + l;
     int cnt = 0;
-    for (int i = 0; i < span; i += 32) {
-        const int j = base + i + l;
-        cnt += __popc(__ballot_sync(kFull, j < V && keys(j) == thr));
-    }
-    __syncthreads();
+    for (int i = 0; i < span; i += 32) cnt += __popc(__ballot_sync(kFull, xu[base + i] == thr));
     if (l == 0) s.tie_base[w] = cnt;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int acc = 0;
-        for (int q = 0; q < kWarps; ++q) {
-            const int c = s.tie_base[q];
-            s.tie_base[q] = acc;
-            acc += c;
+    if (w == 0) {  // exclusive scan of the 32 warp counts
+        const int v = s.tie_base[l];
+        int incl = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(kFull, incl, o);
+            if (l >= o) incl += n;
         }
-    }
-    __syncthreads();
-    int run = s.tie_base[w];
-    const unsigned below = (1u << l) - 1u;
-    for (int i = 0; i < span; i += 32) {
-        const int j = base + i + l;
-        const unsigned k = j < V ? keys(j) : 0u;
-        const bool eq = j < V && k == thr;
-        const unsigned bal = __ballot_sync(kFull, eq);
-        const int rank = run + __popc(bal & below);
-        run += __popc(bal);
-        if (j < V && (k < thr || (eq && rank >= need))) x[j] = -1e9f;
+        s.tie_base[l] = incl - v;
     }
     __syncthreads();
 }
 
-// apply_top_k (src/TextGenerator.cpp:41-63): the k-th largest key by bisection over the key bits.
-__device__ void top_k_block(float* x, int V, int span, int k, Smem& s) {
+// Keeps, of the row's patterns, those above thr and the first `need` (in index order) equal to
+// it; writes value(j) for kept elements and -1e9f for the others (-inf on the padding).
+template <class ValueFn>
+__device__ void keep_cut(float* x, const unsigned* xu, int V, int span, unsigned thr, int need,
+                         int n_eq, ValueFn value, Smem& s) {
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    const int base = w * span;
-    auto count_ge = [&](unsigned t) {
-        int c = 0;
-        for (int i = 0; i < span; i += 32) {
-            const int j = base + i + l;
-            c += (j < V && fkey(x[j]) >= t) ? 1 : 0;
+    const int base = w * span + l;
+    const bool ties = need < n_eq;
+    if (ties) tie_prefix(xu, span, thr, s);
+    int run = ties ? s.tie_base[w] : 0;
+    const unsigned below = (1u << l) - 1u;
+#pragma unroll 8
+    for (int i = 0; i < span; i += 32) {
+        const int j = base + i;
+        const unsigned kk = xu[j];
+        bool keep = kk > thr || (kk == thr && !ties);
+        if (ties) {  // the whole warp takes this branch: the ballot is over all 32 lanes
+            const unsigned bal = __ballot_sync(kFull, kk == thr);
+            if (kk == thr) keep = run + __popc(bal & below) < need;
+            run += __popc(bal);
         }
-        return block_sum_i(c, s);
-    };
-    unsigned thr = 0;
-    for (int bit = 31; bit >= 0; --bit) {
-        const unsigned cand = thr | (1u << bit);
-        if (count_ge(cand) >= k) thr = cand;
+        const float v = keep ? value(j, kk) : -1e9f;
+        x[j] = j >= V ? -INFINITY : v;
     }
-    const int n_ge = count_ge(thr);
-    const int n_gt = thr == 0xffffffffu ? 0 : count_ge(thr + 1);
-    keep_above(x, V, span, thr, k - n_gt, n_ge - n_gt, [&](int j) { return fkey(x[j]); }, s);
+    __syncthreads();
 }
 
 }  // namespace
@@ -285,6 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(SampleArgs a) 
     pdl_trigger();
     pdl_wait();
     extern __shared__ __align__(16) float x[];
+    unsigned* xu = reinterpret_cast<unsigned*>(x);
     __shared__ Smem s;
     const int b = blockIdx.x;
     const int slot = a.slots[b];
@@ -292,28 +276,32 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(SampleArgs a) 
     if (!cfg.enabled) return;
     const int V = a.V;
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    const int span = ((V + kWarps - 1) / kWarps + 31) & ~31;
-    const int base = w * span;
+    const int span = span_of(V);
+    const int base = w * span + l;  // this thread's element of iteration i is base + i
     const float* row = a.logits + static_cast<size_t>(b) * a.ld;
     const unsigned* seen = a.seen + static_cast<size_t>(slot) * a.seen_words;
     const int fed = a.fed ? a.fed[b] : -1;
     const bool mask_stop = a.new_tokens[slot] < cfg.min_length;
     const bool penalize = cfg.penalty != 1.0f;
     const bool scale = cfg.temperature > 0.0f && cfg.temperature != 1.0f;
+    int ph = 0;
 
     // next_logits (:177-206): NaN / +inf or no finite value is an error; then the min_length
     // mask, the repetition penalty (:115-136) and the temperature (:26-38), element by element.
     int bad = 0, finite = 0;
+#pragma unroll 8
     for (int i = 0; i < span; i += 32) {
-        const int j = base + i + l;
-        if (j >= V) continue;
-        float v = row[j];
-        bad |= (isnan(v) || v == INFINITY) ? 1 : 0;
-        finite |= isfinite(v) ? 1 : 0;
-        if (mask_stop && (j == cfg.eos || j == cfg.pad)) v = -INFINITY;
-        if (penalize && (j == fed || ((seen[j >> 5] >> (j & 31)) & 1u)))
-            v = v > 0.0f ? v / cfg.penalty : v * cfg.penalty;
-        if (scale) v = v / cfg.temperature;
+        const int j = base + i;
+        float v = -INFINITY;  // padding
+        if (j < V) {
+            v = row[j];
+            bad |= (isnan(v) || v == INFINITY) ? 1 : 0;
+            finite |= isfinite(v) ? 1 : 0;
+            if (mask_stop && (j == cfg.eos || j == cfg.pad)) v = -INFINITY;
+            if (penalize && (j == fed || ((seen[j >> 5] >> (j & 31)) & 1u)))
+                v = v > 0.0f ? v / cfg.penalty : v * cfg.penalty;
+            if (scale) v = v / cfg.temperature;
+        }
         x[j] = v;
     }
     bad = __syncthreads_or(bad);
@@ -326,161 +314,173 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(SampleArgs a) 
         return;
     }
 
-    if (cfg.top_k > 0 && cfg.top_k < V) top_k_block(x, V, span, cfg.top_k, s);
+    // apply_top_k (:41-63), then apply_top_p's p <= 0 case, which is top-1 (:71-73)
+    for (int pass = 0; pass < 2; ++pass) {
+        const int k = pass == 0 ? ((cfg.top_k > 0 && cfg.top_k < V) ? cfg.top_k : 0)
+                                : (cfg.top_p <= 0.0f ? 1 : 0);
+        if (k == 0) continue;
+        for (int i = 0; i < span; i += 32) {
+            const int j = base + i;
+            xu[j] = j < V ? fkey(x[j]) : 0u;
+        }
+        __syncthreads();
+        const unsigned thr = kth_pattern(xu, span, k, s, ph);
+        int gt = 0, eq = 0;
+        for (int i = 0; i < span; i += 32) {
+            const unsigned kk = xu[base + i];
+            gt += kk > thr ? 1 : 0;
+            eq += kk == thr ? 1 : 0;
+        }
+        const int n_gt = bsum_i(gt, s, ph);
+        const int n_eq = bsum_i(eq, s, ph);
+        keep_cut(x, xu, V, span, thr, k - n_gt, n_eq,
+                 [](int, unsigned kk) { return key_value(kk); }, s);
+    }
 
-    if (cfg.top_p < 1.0f) {
-        if (cfg.top_p <= 0.0f) {
-            top_k_block(x, V, span, 1, s);
+    if (cfg.top_p > 0.0f && cfg.top_p < 1.0f) {
+        // apply_top_p (:66-101): softmax, then the smallest set of most likely tokens whose
+        // probability reaches p. The filtered logits are parked in global scratch while the
+        // probabilities occupy shared memory.
+        float* park = a.scratch + static_cast<size_t>(b) * a.V;
+        float mx = -INFINITY;
+        for (int i = 0; i < span; i += 32) mx = fmaxf(mx, x[base + i]);
+        mx = bmax_f(mx, s, ph);
+        float part = 0.0f;
+#pragma unroll 8
+        for (int i = 0; i < span; i += 32) {
+            const int j = base + i;
+            const float v = x[j];
+            if (j < V) park[j] = v;
+            const float e = expf(v - mx);  // padding: exp(-inf) = 0
+            x[j] = e;
+            part += e;
+        }
+        const float sum = bsum_f(part, s, ph);
+        if (sum > 0.0f)
+            for (int i = 0; i < span; i += 32) x[base + i] = x[base + i] / sum;
+        __syncthreads();
+        // largest probability pattern t with mass(q >= t) >= p (bit 31 is the sign, always 0)
+        const double p = cfg.top_p;
+        unsigned thr = 0;
+        for (int bit = 30; bit >= 0; --bit) {
+            const unsigned cand = thr | (1u << bit);
+            double m = 0.0;
+#pragma unroll 8
+            for (int i = 0; i < span; i += 32) {
+                const unsigned qb = xu[base + i];
+                m += qb >= cand ? static_cast<double>(__uint_as_float(qb)) : 0.0;
+            }
+            if (bsum_d(m, s, ph) >= p) thr = cand;
+        }
+        int ce = 0;
+        double mg = 0.0;
+        for (int i = 0; i < span; i += 32) {
+            const unsigned qb = xu[base + i];
+            if (qb > thr) mg += static_cast<double>(__uint_as_float(qb));
+            ce += qb == thr ? 1 : 0;
+        }
+        const int n_eq = bsum_i(ce, s, ph);
+        const double m_gt = bsum_d(mg, s, ph);
+        if (thr == 0) {  // the running sum never reached p: everything is kept
+#pragma unroll 8
+            for (int i = 0; i < span; i += 32) {
+                const int j = base + i;
+                x[j] = j < V ? park[j] : -INFINITY;
+            }
+            __syncthreads();
         } else {
-            // apply_top_p (:66-101): softmax, then the smallest set of most likely tokens whose
-            // probability reaches p. The filtered logits are parked in global scratch while the
-            // probabilities occupy shared memory.
-            float* park = a.scratch + static_cast<size_t>(b) * a.V;
-            float mx = -INFINITY;
-            for (int i = 0; i < span; i += 32) {
-                const int j = base + i + l;
-                if (j < V) mx = fmaxf(mx, x[j]);
-            }
-            mx = block_max_f(mx, s);
-            float part = 0.0f;
-            for (int i = 0; i < span; i += 32) {
-                const int j = base + i + l;
-                if (j < V) {
-                    park[j] = x[j];
-                    const float e = expf(x[j] - mx);
-                    x[j] = e;
-                    part += e;
-                }
-            }
-            const float sum = block_sum_f(part, s);
-            for (int i = 0; i < span; i += 32) {
-                const int j = base + i + l;
-                if (j < V && sum > 0.0f) x[j] = x[j] / sum;
-            }
-            __syncthreads();
-            // largest probability q (bit pattern; q >= 0) with mass(q_j >= q) >= p
-            const double p = cfg.top_p;
-            auto mass_ge = [&](unsigned t) {
-                double m = 0.0;
-                for (int i = 0; i < span; i += 32) {
-                    const int j = base + i + l;
-                    if (j < V && __float_as_uint(x[j]) >= t) m += static_cast<double>(x[j]);
-                }
-                return block_sum_d(m, s);
-            };
-            unsigned thr = 0;
-            for (int bit = 30; bit >= 0; --bit) {
-                const unsigned cand = thr | (1u << bit);
-                if (mass_ge(cand) >= p) thr = cand;
-            }
-            int n_eq = 0;
-            double m_gt = 0.0;
-            {
-                int ce = 0;
-                double mg = 0.0;
-                for (int i = 0; i < span; i += 32) {
-                    const int j = base + i + l;
-                    if (j >= V) continue;
-                    const unsigned u = __float_as_uint(x[j]);
-                    if (u > thr) mg += static_cast<double>(x[j]);
-                    else if (u == thr) ++ce;
-                }
-                n_eq = block_sum_i(ce, s);
-                m_gt = block_sum_d(mg, s);
-            }
-            int need = n_eq;  // thr == 0: the running sum never reached p, everything is kept
-            if (thr != 0) {
-                const double q = __uint_as_float(thr);
-                const double want = ceil((p - m_gt) / q);
-                need = want >= static_cast<double>(n_eq) ? n_eq : max(1, static_cast<int>(want));
-            }
-            keep_above(x, V, span, thr, need, n_eq,
-                       [&](int j) { return __float_as_uint(x[j]); }, s);
-            // x holds probabilities with -1e9f where dropped: put the kept logits back
-            for (int i = 0; i < span; i += 32) {
-                const int j = base + i + l;
-                if (j < V && x[j] != -1e9f) x[j] = park[j];
-            }
-            __syncthreads();
+            const double q = __uint_as_float(thr);
+            const double want = ceil((p - m_gt) / q);
+            const int need = want >= static_cast<double>(n_eq) ? n_eq : max(1, static_cast<int>(want));
+            keep_cut(x, xu, V, span, thr, need, n_eq, [&](int j, unsigned) { return park[j]; }, s);
         }
     }
 
     int tok;
     if (cfg.temperature <= 0.0f) {
-        float bv = -INFINITY;
-        int bj = 0x7fffffff;
-        for (int i = 0; i < span; i += 32) {
-            const int j = base + i + l;
-            if (j < V && (x[j] > bv || bj == 0x7fffffff)) {
-                bv = x[j];
-                bj = j;
+        // argmax (:151-153): first maximum; padding (-inf, higher index) never wins
+        float bv = x[base];
+        int bj = base;
+        for (int i = 32; i < span; i += 32)
+            if (x[base + i] > bv) {
+                bv = x[base + i];
+                bj = base + i;
             }
-        }
-        tok = block_argmax(bv, bj, s);
+        tok = bargmax(bv, bj, s, ph);
     } else {
         // sample_token (:145-148): softmax (Activation::softmax_row), then the first index whose
         // cumulative probability reaches the uniform draw; the last index takes what remains.
         float mx = -INFINITY;
-        for (int i = 0; i < span; i += 32) {
-            const int j = base + i + l;
-            if (j < V) mx = fmaxf(mx, x[j]);
-        }
-        mx = block_max_f(mx, s);
+        for (int i = 0; i < span; i += 32) mx = fmaxf(mx, x[base + i]);
+        mx = bmax_f(mx, s, ph);
         float part = 0.0f;
         for (int i = 0; i < span; i += 32) {
-            const int j = base + i + l;
-            if (j < V) {
-                const float e = expf(x[j] - mx);
-                x[j] = e;
-                part += e;
-            }
+            const float e = expf(x[base + i] - mx);
+            x[base + i] = e;
+            part += e;
         }
-        const float sum = block_sum_f(part, s);
+        const float sum = bsum_f(part, s, ph);
         double dpart = 0.0;
         for (int i = 0; i < span; i += 32) {
-            const int j = base + i + l;
-            if (j < V) {
-                if (sum > 0.0f) x[j] = x[j] / sum;
-                dpart += static_cast<double>(x[j]);
-            }
+            float q = x[base + i];
+            if (sum > 0.0f) q = q / sum;
+            x[base + i] = q;
+            dpart += static_cast<double>(q);
         }
         // warp totals in index order, then the warp holding the crossing walks its range
-        double wsum = dpart;
-#pragma unroll
-        for (int o = 16; o; o >>= 1) wsum += __shfl_xor_sync(kFull, wsum, o);
+        const double wsum = warp_all(dpart, [](double u, double v) { return u + v; });
+        if (l == 0) s.rd[ph][w] = wsum;
         __syncthreads();
-        if (l == 0) s.red_d[w] = wsum;
-        __syncthreads();
-        double total = 0.0;
-        for (int q = 0; q < kWarps; ++q) total += s.red_d[q];
+        double total = 0.0, before = 0.0;
+        for (int q = 0; q < kWarps; ++q) {
+            const double t = s.rd[ph][q];
+            if (q < w) before += t;
+            total += t;
+        }
+        const double after = before + s.rd[ph][w];
+        ph ^= 1;
         const double u = draw_canonical(a.mt + static_cast<size_t>(slot) * kMtWords, s);
         const double target = u * total;
-        if (threadIdx.x == 0) s.bcast_i = V - 1;
+        if (threadIdx.x == 0) s.bcast_i = target <= 0.0 ? 0 : V - 1;
         __syncthreads();
-        double before = 0.0;
-        for (int q = 0; q < w; ++q) before += s.red_d[q];
-        const double after = before + s.red_d[w];
         if (before < target && after >= target) {  // at most one warp
-            double run = before;
-            bool done = false;
-            for (int i = 0; i < span && !done; i += 32) {
-                const int j = base + i + l;
-                double v = j < V ? static_cast<double>(x[j]) : 0.0;
-                // inclusive scan across the 32 lanes
+            // The warp's range is span / 32 chunks of 32 consecutive elements, taken 32 at a
+            // time: lane l sums chunk g0 + l (reading element (t + l) & 31 at step t, so the 32
+            // lanes hit 32 different banks), a scan over the chunk sums finds the chunk of the
+            // crossing, and a scan inside it the element.
+            const int wbase = w * span;
+            const int nchunk = span / 32;
+            double run0 = before;
+            for (int g0 = 0; g0 < nchunk; g0 += 32) {
+                const int c = g0 + l;
+                double csum = 0.0;
+                if (c < nchunk) {
+                    const float* c0 = x + wbase + c * 32;
+                    for (int t = 0; t < 32; ++t) csum += static_cast<double>(c0[(t + l) & 31]);
+                }
+                double incl = csum;
 #pragma unroll
                 for (int o = 1; o < 32; o <<= 1) {
-                    const double n = __shfl_up_sync(kFull, v, o);
-                    if (l >= o) v += n;
+                    const double n = __shfl_up_sync(kFull, incl, o);
+                    if (l >= o) incl += n;
                 }
-                const unsigned hit = __ballot_sync(kFull, j < V && run + v >= target);
-                if (hit) {
-                    if (l == 0) s.bcast_i = min(base + i + __ffs(hit) - 1, V - 1);
-                    done = true;
+                const unsigned chit = __ballot_sync(kFull, c < nchunk && run0 + incl >= target);
+                if (chit) {
+                    const int cl = __ffs(chit) - 1;
+                    const double run = run0 + __shfl_sync(kFull, incl - csum, cl);
+                    const int j0 = wbase + (g0 + cl) * 32;
+                    double v = static_cast<double>(x[j0 + l]);
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const double n = __shfl_up_sync(kFull, v, o);
+                        if (l >= o) v += n;
+                    }
+                    const unsigned hit = __ballot_sync(kFull, j0 + l < V && run + v >= target);
+                    if (hit && l == 0) s.bcast_i = min(j0 + __ffs(hit) - 1, V - 1);
+                    break;
                 }
-                run += __shfl_sync(kFull, v, 31);
+                run0 += __shfl_sync(kFull, incl, 31);
             }
-        } else if (w == 0 && target <= 0.0 && l == 0) {
-            s.bcast_i = 0;
         }
         __syncthreads();
         tok = s.bcast_i;
@@ -495,7 +495,9 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(SampleArgs a) 
     }
 }
 
-size_t sample_smem_bytes(int V) { return static_cast<size_t>(V) * sizeof(float); }
+size_t sample_smem_bytes(int V) {
+    return static_cast<size_t>(kWarps) * span_of(V) * sizeof(float);
+}
 
 int sample_max_vocab() {
     static int max_v = [] {
@@ -503,7 +505,9 @@ int sample_max_vocab() {
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
         const int avail = optin - static_cast<int>(sizeof(Smem)) - 1024;
-        return avail > 0 ? avail / static_cast<int>(sizeof(float)) : 0;
+        // the padded row is kWarps ranges of a multiple of 32 elements
+        return avail > 0 ? avail / static_cast<int>(sizeof(float)) / (kWarps * 32) * (kWarps * 32)
+                         : 0;
     }();
     return max_v;
 }

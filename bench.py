@@ -171,6 +171,15 @@ DECODE_GEMMS = [(128, 3072, 1024), (128, 1024, 1024), (128, 4096, 1024), (128, 1
                 (128, 32000, 1024)]
 
 
+def parse_sampling(text):
+    """'temperature=0.8,top_k=50' -> {'temperature': 0.8, 'top_k': 50} (adai_b200_sampling)."""
+    out = {}
+    for pair in filter(None, text.split(",")):
+        k, v = (x.strip() for x in pair.split("="))
+        out[k] = int(v) if k in ("top_k", "min_length") else float(v)
+    return out
+
+
 def run_op(args):
     """Op-level cases, one JSON line each (not the headline metric): `--op gemm` times the
     prepared-weight product C = A B for each M,N,K of --shapes (default: the large model's
@@ -213,6 +222,31 @@ def run_op(args):
                               "TFLOP/s": flops / ms / 1e9,
                               "algorithmic_GB/s": 4.0 * (M * K + K * N + M * N) / ms / 1e6,
                               "note": "per call: A split into tf32 hi/lo + the GEMM"}), flush=True)
+    elif args.op == "sample":
+        # token selection alone: --sample-batch rows of --sample-vocab random logits, every slot
+        # configured with --sampling; one adai_b200_sample_logits call per iteration (the host
+        # copies of its slots, fed ids and chosen ids are inside the timed region)
+        from adai_b200.api import Sampling
+        from adai_b200.config import ModelConfig
+        B, V = args.sample_batch, args.sample_vocab
+        cfg = ModelConfig(vocab=V, d_model=128, n_heads=2, d_ff=256, enc_layers=1, dec_layers=1,
+                          max_seq=16)
+        ctx.upload(cfg, make_weights(cfg, seed=0))
+        kv = ctx.kv_arena(B, 8, 8)
+        spec = parse_sampling(args.sampling) or {"temperature": 1.0}
+        for s in range(B):
+            kv.set_sampling(s, Sampling.make(**spec, seed=1 + s))
+        scale = torch.rand((B, 1), generator=g, device="cuda") * 4 + 1
+        logits = torch.randn((B, V), generator=g, device="cuda") * scale
+        torch.cuda.synchronize()
+        slots = np.arange(B, dtype=np.int32)
+        fed = np.full(B, BOS, np.int32)
+        ms = timed(lambda: kv.sample_logits(slots, logits.data_ptr(), V, fed_ids=fed), args.steps)
+        print(json.dumps({"op": "sample", "batch": B, "vocab": V, "sampling": spec,
+                          "us": ms * 1e3, "GB/s": 4.0 * B * V / ms / 1e6,
+                          "note": "per call: slots/ids H2D, sampler kernel, ids D2H"}),
+              flush=True)
+        kv.close()
     else:
         B, H, dh = args.attn_batch, 16, 64
         lo, hi = (int(x) for x in args.attn_lens.split(","))
@@ -250,7 +284,9 @@ def main():
     ap.add_argument("--cpu-baseline-steps", type=int, default=12)
     ap.add_argument("--reference-max-steps", type=int, default=48)
     ap.add_argument("--profile-steps", type=int, default=3)
-    ap.add_argument("--op", choices=["gemm", "attention"], default=None)
+    ap.add_argument("--op", choices=["gemm", "attention", "sample"], default=None)
+    ap.add_argument("--sample-batch", type=int, default=128)
+    ap.add_argument("--sample-vocab", type=int, default=32000)
     ap.add_argument("--shapes", default="", help="--op gemm: 'M,N,K;M,N,K;...'")
     ap.add_argument("--attn-batch", type=int, default=256)
     ap.add_argument("--attn-lens", default="256,2047")
@@ -302,10 +338,7 @@ def main():
                       else wl.src_len[1])
     slots = np.arange(B, dtype=np.int32)
     bos = np.full(B, BOS, np.int32)
-    sampling = {}
-    for kv_pair in filter(None, args.sampling.split(",")):
-        k, v = kv_pair.split("=")
-        sampling[k.strip()] = int(v) if k.strip() in ("top_k", "min_length") else float(v)
+    sampling = parse_sampling(args.sampling)
 
     def restart():
         """Every slot back to position 0; a sampled slot also gets its generator re-seeded."""

@@ -204,7 +204,7 @@ typedef struct adai_b200_sampling {
  * ids already in the sequence before the first token fed (the reference's start tokens beyond the
  * one fed first; may be NULL when n_history is 0). Each step then counts the id fed as part of the
  * sequence, so after the usual BOS feed the penalty set is exactly the reference's `generated`.
- * The whole logits row is held in shared memory: vocab is limited to about 57 000. */
+ * The whole logits row is held in shared memory: vocab is limited to 56 320 (55 Ki). */
 ADAI_B200_API int adai_b200_kv_set_sampling(adai_b200_ctx* ctx, adai_b200_kv* kv, int slot,
                                             const adai_b200_sampling* cfg, const int* history,
                                             int n_history);

@@ -337,3 +337,42 @@ def test_device_generate_with_sampling_equals_step_by_step(sctx):
         b.sampling_state(0)
     a.close()
     b.close()
+
+
+@pytest.mark.parametrize("V", [40000, 56320])
+def test_large_vocabularies(port, torch_cuda, V):
+    # 40000 ids: each warp range holds more than 32 chunks of 32 (the cumulative walk goes in two
+    # groups); 56320: the largest row the kernel's shared memory takes.
+    from adai_b200.config import ModelConfig
+    cfg = ModelConfig(vocab=V, d_model=128, n_heads=2, d_ff=256, enc_layers=1, dec_layers=1,
+                      max_seq=16)
+    kws = [dict(), dict(temperature=0.9, top_k=100), dict(top_p=0.9),
+           dict(temperature=0.8, top_k=2000, top_p=0.95, repetition_penalty=1.2)]
+    with Context(0) as c:
+        c.upload(cfg, make_weights(cfg, 0))
+        kv = c.kv_arena(len(kws), 8, 8)
+        mirrors = []
+        for i, kw in enumerate(kws):
+            kv.set_sampling(i, Sampling.make(**kw, seed=50 + i))
+            mirrors.append(Mirror(port, kw, 50 + i, V))
+        rng = np.random.default_rng(V)
+        fed = np.full(len(kws), BOS, np.int32)
+        for step in range(8):
+            logits = (rng.standard_normal((len(kws), V)) * rng.uniform(1, 4)).astype(np.float32)
+            d = dev(torch_cuda, logits)
+            got = kv.sample_logits(list(range(len(kws))), d.data_ptr(), V, fed_ids=fed)
+            for i in range(len(kws)):
+                tok, m = mirrors[i].step(logits[i], int(fed[i]))
+                assert got[i] == tok or m <= MARGIN, (V, i, step, got[i], tok, m)
+            fed = got.astype(np.int32)
+        for i in range(len(kws)):
+            np.testing.assert_array_equal(kv.sampling_state(i)[0], mirrors[i].st)
+        kv.close()
+        if V == 56320:  # one more row of 32 ids no longer fits
+            big = ModelConfig(vocab=V + 32, d_model=128, n_heads=2, d_ff=256, enc_layers=1,
+                              dec_layers=1, max_seq=16)
+            c.upload(big, make_weights(big, 0))
+            kv = c.kv_arena(1, 8, 8)
+            with pytest.raises(ValueError, match="exceeds"):
+                kv.set_sampling(0, Sampling.make(seed=1))
+            kv.close()
