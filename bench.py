@@ -247,6 +247,28 @@ def run_op(args):
                           "note": "per call: slots/ids H2D, sampler kernel, ids D2H"}),
               flush=True)
         kv.close()
+    elif args.op == "prefill":
+        # encoder prefill of --prefill-batch sources of --prefill-len ids through one encoder
+        # layer of the large model's width (d_model 1024, 16 heads of 64, d_ff 4096), plus the
+        # cross K/V of one decoder layer: GEMMs and the tensor-core prefill attention
+        from adai_b200.config import ModelConfig
+        B, S = args.prefill_batch, args.prefill_len
+        cfg = ModelConfig(vocab=4096, d_model=1024, n_heads=16, d_ff=4096, enc_layers=1,
+                          dec_layers=1, max_seq=max(S, 16))
+        ctx.upload(cfg, make_weights(cfg, seed=0))
+        kv = ctx.kv_arena(B, 8, S)
+        srcs = make_sources(cfg, B, (S, S), seed=0)
+        slots = np.arange(B, dtype=np.int32)
+        ms = timed(lambda: kv.encode(slots, srcs), args.steps)
+        D, F = cfg.d_model, cfg.d_ff
+        attn_flops = 4.0 * B * S * S * D             # Q K^T and P V, all heads
+        gemm_flops = 2.0 * B * S * (4 * D * D + 2 * D * F + 2 * D * D)
+        print(json.dumps({"op": "prefill", "batch": B, "src_len": S, "d_model": D, "heads": 16,
+                          "us": ms * 1e3, "tokens/s": B * S / ms * 1e3,
+                          "attention_TFLOP": attn_flops / 1e12, "gemm_TFLOP": gemm_flops / 1e12,
+                          "note": "per call: ids H2D, one encoder layer + final norm, cross K/V "
+                                  "of one decoder layer"}), flush=True)
+        kv.close()
     else:
         B, H, dh = args.attn_batch, 16, 64
         lo, hi = (int(x) for x in args.attn_lens.split(","))
@@ -284,7 +306,9 @@ def main():
     ap.add_argument("--cpu-baseline-steps", type=int, default=12)
     ap.add_argument("--reference-max-steps", type=int, default=48)
     ap.add_argument("--profile-steps", type=int, default=3)
-    ap.add_argument("--op", choices=["gemm", "attention", "sample"], default=None)
+    ap.add_argument("--op", choices=["gemm", "attention", "sample", "prefill"], default=None)
+    ap.add_argument("--prefill-batch", type=int, default=16)
+    ap.add_argument("--prefill-len", type=int, default=512)
     ap.add_argument("--sample-batch", type=int, default=128)
     ap.add_argument("--sample-vocab", type=int, default=32000)
     ap.add_argument("--shapes", default="", help="--op gemm: 'M,N,K;M,N,K;...'")
