@@ -56,7 +56,7 @@ EXPORTS = [
     "adai_b200_softmax_rows", "adai_b200_layernorm_fwd", "adai_b200_add_row_bias",
     "adai_b200_activation", "adai_b200_embedding_gather_add_pe", "adai_b200_backend_bind",
     "adai_b200_kv_set_sampling", "adai_b200_kv_sampling_state", "adai_b200_sample_logits",
-    "adai_b200_checkpoint_special_tokens",
+    "adai_b200_checkpoint_special_tokens", "adai_b200_ctx_check_wait_timeout",
 ]
 
 # Kernel classes of adai_b200_profile_step (adai_b200_kernel_class).
@@ -105,6 +105,7 @@ def load() -> C.CDLL:
     lib.adai_b200_ctx_destroy.argtypes = [_vp]
     lib.adai_b200_ctx_synchronize.argtypes = [_vp, C.c_double]
     lib.adai_b200_ctx_memory.argtypes = [_vp, C.POINTER(C.c_ulonglong)]
+    lib.adai_b200_ctx_check_wait_timeout.argtypes = [_vp, C.POINTER(C.c_double)]
     lib.adai_b200_ctx_stream.argtypes = [_vp]
     lib.adai_b200_ctx_stream.restype = _vp
     lib.adai_b200_model_tensor_count.argtypes = [C.POINTER(ModelDesc)]
@@ -241,6 +242,17 @@ class Context:
 
     def synchronize(self, timeout_s: float = 0.0) -> None:
         check(self.lib.adai_b200_ctx_synchronize(self.h, timeout_s))
+
+    def check_wait_timeout(self) -> float:
+        """Makes one bounded device wait run out on purpose and returns the wall seconds the call
+        took. The expected outcome is the library's timeout status, after which this context is
+        unusable; any other status raises."""
+        t = C.c_double()
+        rc = self.lib.adai_b200_ctx_check_wait_timeout(self.h, C.byref(t))
+        if rc != TIMEOUT:
+            check(rc)
+            raise AdaiError("the device wait did not report a timeout")
+        return t.value
 
     def memory_bytes(self) -> int:
         v = C.c_ulonglong()

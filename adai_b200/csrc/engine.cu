@@ -923,6 +923,28 @@ int adai_b200_ctx_synchronize(adai_b200_ctx* c, double timeout_seconds) {
     });
 }
 
+int adai_b200_ctx_check_wait_timeout(adai_b200_ctx* c, double* waited_seconds) {
+    return guarded([&] {
+        check_ctx(c);
+        int* gave_up = c->dzalloc_t<int>(1);
+        const auto t0 = std::chrono::steady_clock::now();
+        try {
+            launch_wait_selftest(c->d_err, gave_up, c->stream);
+            cuda_ok(cudaGetLastError(), "wait self-test launch");
+            int h = 0;
+            cuda_ok(cudaMemcpyAsync(&h, gave_up, sizeof(int), cudaMemcpyDeviceToHost, c->stream), "D2H");
+            c->sync(wait_timeout_seconds());  // reads the error word: fails with the timeout
+            fail(ADAI_B200_ERR_STATE, "the device wait did not report its timeout (gave_up " +
+                                          std::to_string(h) + ")");
+        } catch (...) {
+            if (waited_seconds)
+                *waited_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+            c->dfree(gave_up);
+            throw;
+        }
+    });
+}
+
 int adai_b200_ctx_memory(adai_b200_ctx* c, unsigned long long* bytes) {
     return guarded([&] {
         if (!c || !bytes) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null argument");

@@ -556,4 +556,21 @@ void launch_advance(const int* next, int* ids, const int* slots, int* len_by_slo
                   len_by_slot, B);
 }
 
+// Two bounded waits on an mbarrier that nothing arrives at: the first runs out after the spin
+// deadline and records its code in the error word; the second sees the word already set and
+// gives up at once. Nothing asynchronous is in flight, so the CTA exits cleanly.
+__global__ void wait_selftest_kernel(int* err, int* gave_up) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    const bool first = mbar_wait(&bar, 0, err, kDevTimeoutAccum);
+    const bool second = mbar_wait(&bar, 0, err, kDevTimeoutTmaFull);
+    *gave_up = (first ? 0 : 1) + (second ? 0 : 2);
+}
+
+void launch_wait_selftest(int* err, int* gave_up, cudaStream_t st) {
+    launch_kernel(wait_selftest_kernel, dim3(1), dim3(32), 0, st, err, gave_up);
+}
+
 }  // namespace adai_b200

@@ -222,6 +222,10 @@ void launch_prefill_attention(const float* qkv, int D, int H, const int* offsets
 void launch_advance(const int* next, int* ids, const int* slots, int* len_by_slot, int B,
                     cudaStream_t st);
 
+// Diagnostic: one CTA makes a bounded device wait run out (error code kDevTimeoutAccum in *err)
+// and a second wait return at once because the error word is set; *gave_up = 3 when both gave up.
+void launch_wait_selftest(int* err, int* gave_up, cudaStream_t st);
+
 // ---- token selection with the reference's sampling rules (sample.cu) ----
 // Per-slot configuration (GenerationConfig's sampling fields, src/TextGenerator.hpp:65-82).
 struct SampleSlot {

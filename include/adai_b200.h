@@ -69,6 +69,13 @@ ADAI_B200_API int adai_b200_ctx_destroy(adai_b200_ctx* ctx);
  * src/gpu/GPUDebugSync.cpp:236-244). On expiry returns ADAI_B200_ERR_TIMEOUT and marks the
  * context unusable (the reference marks the device lost). */
 ADAI_B200_API int adai_b200_ctx_synchronize(adai_b200_ctx* ctx, double timeout_seconds);
+/* Diagnostic of the timeout path (GPU_WAIT_TIMEOUT_SECONDS semantics, src/gpu/GPUDebugSync.cpp):
+ * runs one device-side bounded wait on a barrier that nothing completes. The wait gives up after
+ * its 2 s limit and records its code, a second wait returns at once because the error is already
+ * recorded, and the kernel ends normally (no fault). The call then returns ADAI_B200_ERR_TIMEOUT
+ * and the context is unusable, as after any device timeout; any other status means the path is
+ * broken. waited_seconds (may be NULL) receives the host's wall time for the call. */
+ADAI_B200_API int adai_b200_ctx_check_wait_timeout(adai_b200_ctx* ctx, double* waited_seconds);
 /* Device bytes this context holds. */
 ADAI_B200_API int adai_b200_ctx_memory(adai_b200_ctx* ctx, unsigned long long* bytes);
 /* The CUDA stream (as void*) the context launches on. */

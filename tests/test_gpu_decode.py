@@ -219,3 +219,22 @@ def test_decoding_past_the_positional_table(port):
         assert worst <= 1.0, worst
         assert all(tie for _, _, tie in mism), mism
         kv.close()
+
+
+def test_device_wait_timeout_reaches_the_host():
+    # A device-side bounded wait on a barrier nothing completes gives up after its 2 s limit and
+    # records its code; the host reports the timeout and refuses further work on that context
+    # (GPU_WAIT_TIMEOUT_SECONDS semantics). No fault is involved: the kernel ends normally, and a
+    # new context on the same device works.
+    c = Context(0)
+    waited = c.check_wait_timeout()
+    assert 1.5 < waited < 30.0, waited         # one 2 s deadline; the second wait returns at once
+    with pytest.raises(StateError, match="unusable"):
+        c.upload(TINY, make_weights(TINY, 0))
+    c.close()
+    with Context(0) as fresh:
+        fresh.upload(TINY, make_weights(TINY, 0))
+        kv = fresh.kv_arena(1, 4, 8)
+        kv.encode([0], make_sources(TINY, 1, (8, 8), 0))
+        assert kv.generate([0], [BOS], 2).shape == (1, 2)
+        kv.close()
