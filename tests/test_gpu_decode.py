@@ -238,3 +238,15 @@ def test_device_wait_timeout_reaches_the_host():
         kv.encode([0], make_sources(TINY, 1, (8, 8), 0))
         assert kv.generate([0], [BOS], 2).shape == (1, 2)
         kv.close()
+
+
+def test_wide_batch_one_attention_cta_per_head(ctx, port, tiny):
+    # 160 sequences x 4 heads: enough (sequence, head) pairs that each attention CTA takes every
+    # cached row of its pair (no split-KV merge); ragged sources, lockstep with the oracle.
+    B = 160
+    srcs = make_sources(TINY, B, (4, 48), 13)
+    kv = ctx.kv_arena(B, 12, 48)
+    worst, mismatch = lockstep(kv, TINY, port.model(TINY, tiny), list(range(B)), srcs, 6)
+    kv.close()
+    assert worst <= 1.0, worst
+    assert all(tie for _, _, tie in mismatch), mismatch
