@@ -11,16 +11,15 @@
 // holds values that no pass can select (-inf logits, key 0, probability 0), so the inner loops
 // carry no bounds test.
 //
-// The two cuts are found by bisection over 32-bit patterns: top-k over an order-preserving key of
-// the logit, top-p over the bit pattern of the probability (which orders like the value, as it is
-// never negative). Each step is one pass over the row and one block reduction with a single
-// barrier. Before a bisection the row is rewritten in place as those patterns, so a pass is a
-// load, a compare and an add.
+// The two cuts are found by radix selection over 32-bit patterns, a byte per pass: top-k over an
+// order-preserving key of the logit, top-p over the bit pattern of the probability (which orders
+// like the value, as it is never negative), with the mass of each bin summed in fixed point.
+// Before a selection the row is rewritten in place as those patterns.
 //
-// Where the reference works in float and the device in double (the top-p running sum, the
-// cumulative distribution), the two agree except when the decision lies within rounding distance
-// of its threshold. Ties at the top-k and top-p cut are kept lowest index first (std::partial_sort
-// and std::sort leave their order unspecified).
+// Where the reference works in float and the device in double or fixed point (the top-p running
+// sum, the cumulative distribution), the two agree except when the decision lies within rounding
+// distance of its threshold. Ties at the top-k and top-p cut are kept lowest index first
+// (std::partial_sort and std::sort leave their order unspecified).
 #include <cfloat>
 #include <cmath>
 
@@ -58,9 +57,18 @@ struct Smem {
     int rj[2][kWarps];
     float rf[2][kWarps];
     int tie_base[kWarps];
-    unsigned mt[624];
+    // the filters' radix histograms and the generator refresh are never live at the same time
+    union {
+        unsigned mt[624];
+        struct {
+            unsigned c[256];
+            unsigned long long m[256];
+        } hist;
+    };
     unsigned draw[2];
     int bcast_i;
+    unsigned long long sel_rem;  // radix selection: the bin one pass picked
+    int sel_bin, sel_cnt, sel_ok;
 };
 
 template <class T, class Op>
@@ -198,19 +206,98 @@ __device__ double draw_canonical(unsigned* g, Smem& s) {
     return r;
 }
 
-// Largest pattern t with count(pattern >= t) >= k (the k-th largest pattern), by bisection over
-// the 32 bits; patterns are the row rewritten in place, padding 0.
-__device__ unsigned kth_pattern(const unsigned* xu, int span, int k, Smem& s, int& ph) {
-    const int base = (threadIdx.x >> 5) * span + (threadIdx.x & 31);
-    unsigned thr = 0;
-    for (int bit = 31; bit >= 0; --bit) {
-        const unsigned cand = thr | (1u << bit);
-        int c = 0;
-#pragma unroll 8
-        for (int i = 0; i < span; i += 32) c += xu[base + i] >= cand ? 1 : 0;
-        if (bsum_i(c, s, ph) >= k) thr = cand;
+// Radix selection over the row's 32-bit patterns (padding 0), most significant byte first. Each
+// of four passes histograms the 8-bit digit of the patterns that share the prefix chosen so far
+// (counts aggregated per warp with __match_any_sync) and warp 0 walks the 256 bins from the top.
+// With kMass a bin also holds the probability mass of its patterns (each pattern is then a
+// non-negative float) in fixed point, units of 2^-40, so the sums do not depend on the order of
+// the atomic adds. The walk stops at the first bin whose running total reaches `target` (a count,
+// or a fixed-point mass). Returns the cut pattern: the target-th largest pattern, or the largest t
+// whose mass of patterns >= t reaches target. rem: what is still needed from the patterns equal to
+// the cut; n_eq: how many patterns equal it. found is false when the row's total stays below
+// target (possible only for masses).
+constexpr float kMassScale = 1099511627776.0f;  // 2^40
+template <bool kMass>
+__device__ unsigned radix_select(const unsigned* xu, int span, unsigned long long target, Smem& s,
+                                 unsigned long long& rem, int& n_eq, bool& found) {
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    const int base = w * span + l;
+    unsigned prefix = 0;
+    rem = target;
+    n_eq = 0;
+    found = true;
+    for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        for (int i = threadIdx.x; i < 256; i += kThreads) {
+            s.hist.c[i] = 0;
+            if (kMass) s.hist.m[i] = 0;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int i = 0; i < span; i += 32) {
+            const unsigned kk = xu[base + i];
+            // (masses: a pattern without mass cannot move the walk, so it takes no part)
+            const bool in = (pass == 0 || (kk >> (shift + 8)) == prefix) &&
+                            (!kMass || __uint_as_float(kk) * kMassScale >= 1.0f);
+            const unsigned inmask = __ballot_sync(kFull, in);
+            if (in) {
+                const unsigned digit = (kk >> shift) & 255u;
+                const unsigned peers = __match_any_sync(inmask, digit);
+                const bool leader = l == __ffs(peers) - 1;
+                if (leader) atomicAdd(&s.hist.c[digit], static_cast<unsigned>(__popc(peers)));
+                if (kMass) {
+                    // the group's mass in two 32-bit sums that cannot overflow (fx <= 2^40: 20 low
+                    // bits and at most 21 high bits per lane, 32 lanes), then one atomic per group
+                    const auto fx = static_cast<unsigned long long>(__uint_as_float(kk) * kMassScale);
+                    const unsigned lo = __reduce_add_sync(peers, static_cast<unsigned>(fx & 0xFFFFFull));
+                    const unsigned hi = __reduce_add_sync(peers, static_cast<unsigned>(fx >> 20));
+                    const unsigned long long tot = (static_cast<unsigned long long>(hi) << 20) + lo;
+                    if (leader && tot) atomicAdd(&s.hist.m[digit], tot);
+                }
+            }
+        }
+        __syncthreads();
+        if (w == 0) {  // lane l holds bins 255 - 8l down to 248 - 8l
+            unsigned long long v8[8], tot = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int bin = 255 - 8 * l - j;
+                v8[j] = kMass ? s.hist.m[bin] : s.hist.c[bin];
+                tot += v8[j];
+            }
+            unsigned long long incl = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned long long n = __shfl_up_sync(kFull, incl, o);
+                if (l >= o) incl += n;
+            }
+            const unsigned hit = __ballot_sync(kFull, incl >= rem);
+            if (l == 0) s.sel_ok = hit ? 1 : 0;
+            if (hit && l == __ffs(hit) - 1) {
+                unsigned long long cum = incl - tot;
+                for (int j = 0; j < 8; ++j) {
+                    if (cum + v8[j] >= rem) {
+                        const int bin = 255 - 8 * l - j;
+                        s.sel_bin = bin;
+                        s.sel_rem = rem - cum;
+                        s.sel_cnt = static_cast<int>(s.hist.c[bin]);
+                        break;
+                    }
+                    cum += v8[j];
+                }
+            }
+        }
+        __syncthreads();
+        if (!s.sel_ok) {
+            found = false;
+            return 0;
+        }
+        prefix = (prefix << 8) | static_cast<unsigned>(s.sel_bin);
+        rem = s.sel_rem;
+        n_eq = s.sel_cnt;
+        __syncthreads();  // the next pass rewrites the histogram and the selection
     }
-    return thr;
+    return prefix;
 }
 
 // The exclusive prefix over warps of each warp's count of patterns equal to thr (tie ranks in
@@ -315,6 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(SampleArgs a) 
     }
 
     // apply_top_k (:41-63), then apply_top_p's p <= 0 case, which is top-1 (:71-73)
+    const int k_top = (cfg.top_k > 0 && cfg.top_k < V) ? cfg.top_k : 0;
     for (int pass = 0; pass < 2; ++pass) {
         const int k = pass == 0 ? ((cfg.top_k > 0 && cfg.top_k < V) ? cfg.top_k : 0)
                                 : (cfg.top_p <= 0.0f ? 1 : 0);
@@ -324,16 +412,12 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(SampleArgs a) 
             xu[j] = j < V ? fkey(x[j]) : 0u;
         }
         __syncthreads();
-        const unsigned thr = kth_pattern(xu, span, k, s, ph);
-        int gt = 0, eq = 0;
-        for (int i = 0; i < span; i += 32) {
-            const unsigned kk = xu[base + i];
-            gt += kk > thr ? 1 : 0;
-            eq += kk == thr ? 1 : 0;
-        }
-        const int n_gt = bsum_i(gt, s, ph);
-        const int n_eq = bsum_i(eq, s, ph);
-        keep_cut(x, xu, V, span, thr, k - n_gt, n_eq,
+        unsigned long long need = 0;
+        int n_eq = 0;
+        bool found = true;
+        const unsigned thr = radix_select<false>(xu, span, static_cast<unsigned long long>(k), s,
+                                                 need, n_eq, found);
+        keep_cut(x, xu, V, span, thr, static_cast<int>(need), n_eq,
                  [](int, unsigned kk) { return key_value(kk); }, s);
     }
 
@@ -359,29 +443,52 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(SampleArgs a) 
         if (sum > 0.0f)
             for (int i = 0; i < span; i += 32) x[base + i] = x[base + i] / sum;
         __syncthreads();
-        // largest probability pattern t with mass(q >= t) >= p (bit 31 is the sign, always 0)
-        const double p = cfg.top_p;
+        // The cut: the largest probability pattern t with mass(q >= t) >= p. After top-k at most
+        // k tokens carry mass, and a radix selection over them (fixed-point masses, at least one
+        // unit so a p below the resolution still keeps the most likely token) takes four cheap
+        // passes. Over the whole vocabulary bisection over the pattern's 31 bits with float64
+        // block sums is faster.
         unsigned thr = 0;
-        for (int bit = 30; bit >= 0; --bit) {
-            const unsigned cand = thr | (1u << bit);
-            double m = 0.0;
-#pragma unroll 8
-            for (int i = 0; i < span; i += 32) {
-                const unsigned qb = xu[base + i];
-                m += qb >= cand ? static_cast<double>(__uint_as_float(qb)) : 0.0;
+        int n_eq = 0, need = 0;
+        bool found = true;
+        if (k_top > 0) {
+            const auto target = max(1ull, static_cast<unsigned long long>(
+                                              static_cast<double>(cfg.top_p) * static_cast<double>(kMassScale)));
+            unsigned long long rem = 0;
+            thr = radix_select<true>(xu, span, target, s, rem, n_eq, found);
+            if (found) {
+                const auto unit = static_cast<unsigned long long>(__uint_as_float(thr) * kMassScale);
+                const unsigned long long want = (rem + unit - 1) / unit;  // unit >= 1 here
+                need = want >= static_cast<unsigned long long>(n_eq) ? n_eq : max(1, static_cast<int>(want));
             }
-            if (bsum_d(m, s, ph) >= p) thr = cand;
+        } else {
+            const double p = cfg.top_p;
+            for (int bit = 30; bit >= 0; --bit) {
+                const unsigned cand = thr | (1u << bit);
+                double m = 0.0;
+#pragma unroll 8
+                for (int i = 0; i < span; i += 32) {
+                    const unsigned qb = xu[base + i];
+                    m += qb >= cand ? static_cast<double>(__uint_as_float(qb)) : 0.0;
+                }
+                if (bsum_d(m, s, ph) >= p) thr = cand;
+            }
+            found = thr != 0;
+            if (found) {
+                int ce = 0;
+                double mg = 0.0;
+                for (int i = 0; i < span; i += 32) {
+                    const unsigned qb = xu[base + i];
+                    if (qb > thr) mg += static_cast<double>(__uint_as_float(qb));
+                    ce += qb == thr ? 1 : 0;
+                }
+                n_eq = bsum_i(ce, s, ph);
+                const double m_gt = bsum_d(mg, s, ph);
+                const double want = ceil((p - m_gt) / static_cast<double>(__uint_as_float(thr)));
+                need = want >= static_cast<double>(n_eq) ? n_eq : max(1, static_cast<int>(want));
+            }
         }
-        int ce = 0;
-        double mg = 0.0;
-        for (int i = 0; i < span; i += 32) {
-            const unsigned qb = xu[base + i];
-            if (qb > thr) mg += static_cast<double>(__uint_as_float(qb));
-            ce += qb == thr ? 1 : 0;
-        }
-        const int n_eq = bsum_i(ce, s, ph);
-        const double m_gt = bsum_d(mg, s, ph);
-        if (thr == 0) {  // the running sum never reached p: everything is kept
+        if (!found) {  // the running sum never reached p: everything is kept
 #pragma unroll 8
             for (int i = 0; i < span; i += 32) {
                 const int j = base + i;
@@ -389,9 +496,6 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(SampleArgs a) 
             }
             __syncthreads();
         } else {
-            const double q = __uint_as_float(thr);
-            const double want = ceil((p - m_gt) / q);
-            const int need = want >= static_cast<double>(n_eq) ? n_eq : max(1, static_cast<int>(want));
             keep_cut(x, xu, V, span, thr, need, n_eq, [&](int j, unsigned) { return park[j]; }, s);
         }
     }
