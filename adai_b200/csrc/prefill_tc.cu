@@ -8,8 +8,12 @@
 // (V^T [head * DH + d][column]) whose sequences start at 32-column boundaries, so that every box
 // starts on a 16-byte boundary. P is written by the softmax warps in the same swizzled layout.
 //
-// Warp roles (192 threads): warp 0 issues the TMA loads, warp 1 the MMAs, warps 2-5 own 32 query
-// rows each (their TMEM lane quarter) for the softmax and the output. Every wait is bounded.
+// Warp roles (320 threads): warp 0 issues the TMA loads, warp 1 the MMAs, warps 2-9 run the
+// softmax and the output, two warps per TMEM lane quarter (32 query rows): each reads the whole S
+// block of its rows and takes the row maximum (both halves get the same value), then half h
+// exponentiates key columns [32h, 32h + 32), writes that 32-column atom of P and folds output
+// dimensions [h DH/2, (h+1) DH/2). The two halves' row sums are added once at the end. Every wait
+// is bounded.
 #include <mutex>
 
 #include "common.cuh"
@@ -20,7 +24,7 @@ namespace {
 
 constexpr int kPBM = 128;       // queries per CTA
 constexpr int kPBN = 64;        // keys per block
-constexpr int kPThreads = 192;
+constexpr int kPThreads = 320;
 constexpr uint32_t kAtomRows128 = 128 * 128;  // bytes of a [128 rows x 32 floats] swizzled atom
 
 struct __align__(64) PrefillParams {
@@ -75,7 +79,8 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attention_tc_kernel(cons
     uint64_t* o_full = bars + 12;
     uint64_t* o_empty = bars + 13;
     uint64_t* done = bars + 14;
-    constexpr int kBars = 15;
+    uint64_t* pair_end = bars + 15;  // [4] both halves of a lane quarter have left their row sums
+    constexpr int kBars = 19;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBars);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -84,11 +89,13 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attention_tc_kernel(cons
         tma_prefetch_desc(&p.k_hi);
         tma_prefetch_desc(&p.v_hi);
         // arrivals per phase: the producer (expect_tx) or one tcgen05.commit, except the barriers
-        // the four softmax warps arrive on
+        // the eight softmax warps arrive on (one arrival per warp) and the quarters' end-of-row
+        // exchanges (one per thread of the two warps)
         for (int i = 0; i < kBars; ++i) {
             const bool softmax = (bars + i == s_empty || bars + i == s_empty + 1 || bars + i == p_full ||
                                   bars + i == o_empty);
-            mbar_init(&bars[i], softmax ? 4 : 1);
+            const bool pair = bars + i >= pair_end;
+            mbar_init(&bars[i], pair ? 64 : (softmax ? 8 : 1));
         }
         fence_barrier_init();
     }
@@ -204,13 +211,16 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attention_tc_kernel(cons
             mbar_wait_drain(done, 0, p.err, kDevTimeoutAccum);
         }
     } else {
-        // ---- warps 2..5: one query row per thread ----
+        // ---- warps 2..9: one query row per thread, two warps (halves) per row ----
         const int qq = warp & 3;
+        const int hf = (warp - 2) >> 2;
+        constexpr int HD = DH / 2;     // output dimensions of this half
+        constexpr int HC = kPBN / 2;   // key columns of this half (one 32-float P atom)
         const int row = qq * 32 + lane;  // row within the query block = TMEM lane
         const uint32_t lane_off = static_cast<uint32_t>(qq * 32) << 16;
-        float o[DH];
+        float o[HD];
 #pragma unroll
-        for (int d = 0; d < DH; ++d) o[d] = 0.f;
+        for (int d = 0; d < HD; ++d) o[d] = 0.f;
         float m = -INFINITY, l = 0.f, corr_prev = 0.f;
         bool ok = true;
         const uint32_t ps = smem_u32(p_s);
@@ -227,29 +237,29 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attention_tc_kernel(cons
                 break;
             }
             tc_fence_after();
-            float sc[kPBN];
+            // the block maximum over all kPBN columns; this half's columns kept for the exponentials
+            const int kvalid = S - j * kPBN;  // keys of this block inside the sequence
             const uint32_t t_big = tmem + lane_off + b * 2 * kPBN;
+            float mx = m;
+            float sc[HC];
 #pragma unroll
             for (int c0 = 0; c0 < kPBN; c0 += 16) {
                 float vb[16], vsm[16];
                 tmem_ld_16x2(t_big + c0, t_big + kPBN + c0, vb, vsm);
 #pragma unroll
-                for (int i = 0; i < 16; ++i) sc[c0 + i] = (vb[i] + vsm[i]) * p.scale;
+                for (int i = 0; i < 16; ++i) {
+                    const float v = (c0 + i < kvalid) ? (vb[i] + vsm[i]) * p.scale : -INFINITY;
+                    mx = fmaxf(mx, v);
+                    if (c0 / HC == hf) sc[(c0 % HC) + i] = v;
+                }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(s_empty + b);
-            const int kvalid = S - j * kPBN;  // keys of this block inside the sequence
-            float mx = m;
-#pragma unroll
-            for (int i = 0; i < kPBN; ++i) {
-                if (i >= kvalid) sc[i] = -INFINITY;
-                mx = fmaxf(mx, sc[i]);
-            }
             const float corr = (m == -INFINITY) ? 0.f : expf(m - mx);
             float psum = 0.f;
 #pragma unroll
-            for (int i = 0; i < kPBN; ++i) {
+            for (int i = 0; i < HC; ++i) {
                 sc[i] = (sc[i] == -INFINITY) ? 0.f : expf(sc[i] - mx);
                 psum += sc[i];
             }
@@ -265,9 +275,9 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attention_tc_kernel(cons
                 }
                 tc_fence_after();
 #pragma unroll
-                for (int c0 = 0; c0 < DH; c0 += 16) {
+                for (int c0 = 0; c0 < HD; c0 += 16) {
                     float vb[16], vsm[16];
-                    tmem_ld_16x2(t_o + lane_off + c0, t_o + lane_off + DH + c0, vb, vsm);
+                    tmem_ld_16x2(t_o + lane_off + hf * HD + c0, t_o + lane_off + DH + hf * HD + c0, vb, vsm);
 #pragma unroll
                     for (int i = 0; i < 16; ++i) o[c0 + i] = o[c0 + i] * corr_prev + (vb[i] + vsm[i]);
                 }
@@ -276,15 +286,14 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attention_tc_kernel(cons
                 if (lane == 0) mbar_arrive(o_empty);
             }
             corr_prev = corr;
-#pragma unroll
-            for (int a = 0; a < kPBN / 32; ++a) {
-                const uint32_t hi_atom = ps + a * kAtomRows128 + p_row;
-                const uint32_t lo_atom = ps + (kPBN / 32 + a) * kAtomRows128 + p_row;
+            {
+                const uint32_t hi_atom = ps + hf * kAtomRows128 + p_row;
+                const uint32_t lo_atom = ps + (kPBN / 32 + hf) * kAtomRows128 + p_row;
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
                     float h4[4], l4[4];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) split_tf32(sc[a * 32 + c * 4 + e], h4[e], l4[e]);
+                    for (int e = 0; e < 4; ++e) split_tf32(sc[c * 4 + e], h4[e], l4[e]);
                     const uint32_t off = static_cast<uint32_t>((c ^ sw) * 16);
                     st_shared_f4(hi_atom + off, h4[0], h4[1], h4[2], h4[3]);
                     st_shared_f4(lo_atom + off, l4[0], l4[1], l4[2], l4[3]);
@@ -301,25 +310,33 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attention_tc_kernel(cons
             if (got) {
                 tc_fence_after();
 #pragma unroll
-                for (int c0 = 0; c0 < DH; c0 += 16) {
+                for (int c0 = 0; c0 < HD; c0 += 16) {
                     float vb[16], vsm[16];
-                    tmem_ld_16x2(t_o + lane_off + c0, t_o + lane_off + DH + c0, vb, vsm);
+                    tmem_ld_16x2(t_o + lane_off + hf * HD + c0, t_o + lane_off + DH + hf * HD + c0, vb, vsm);
 #pragma unroll
                     for (int i = 0; i < 16; ++i) o[c0 + i] = o[c0 + i] * corr_prev + (vb[i] + vsm[i]);
                 }
-                const int q = qb * kPBM + row;
-                if (q < S) {
-                    const float inv = 1.0f / l;
-                    const size_t base = static_cast<size_t>(row0 + q) * p.D + h * DH;
+                // The last P V has completed, so the P buffer is free: the two halves of each row
+                // leave their partial sums there and take the other's.
+                float* lx = reinterpret_cast<float*>(p_s);
+                lx[hf * kPBM + row] = l;
+                mbar_arrive(pair_end + qq);
+                if (mbar_wait(pair_end + qq, 0, p.err, kDevTimeoutAccum)) {
+                    const float l_all = l + lx[(1 - hf) * kPBM + row];
+                    const int q = qb * kPBM + row;
+                    if (q < S) {
+                        const float inv = 1.0f / l_all;
+                        const size_t base = static_cast<size_t>(row0 + q) * p.D + h * DH + hf * HD;
 #pragma unroll
-                    for (int d = 0; d < DH; d += 4) {
-                        float4 hi, lo;
-                        split_tf32(o[d] * inv, hi.x, lo.x);
-                        split_tf32(o[d + 1] * inv, hi.y, lo.y);
-                        split_tf32(o[d + 2] * inv, hi.z, lo.z);
-                        split_tf32(o[d + 3] * inv, hi.w, lo.w);
-                        *reinterpret_cast<float4*>(p.out_hi + base + d) = hi;
-                        *reinterpret_cast<float4*>(p.out_lo + base + d) = lo;
+                        for (int d = 0; d < HD; d += 4) {
+                            float4 hi, lo;
+                            split_tf32(o[d] * inv, hi.x, lo.x);
+                            split_tf32(o[d + 1] * inv, hi.y, lo.y);
+                            split_tf32(o[d + 2] * inv, hi.z, lo.z);
+                            split_tf32(o[d + 3] * inv, hi.w, lo.w);
+                            *reinterpret_cast<float4*>(p.out_hi + base + d) = hi;
+                            *reinterpret_cast<float4*>(p.out_lo + base + d) = lo;
+                        }
                     }
                 }
             }
