@@ -145,6 +145,7 @@ struct adai_b200_kv {
     int *d_self_len = nullptr, *d_cross_len = nullptr;
     int* d_hist = nullptr;  // [max_slots][self_cap]: the argmax produced at each position
     std::vector<int> self_len, cross_len;
+    std::vector<char> encoded;  // the slot holds an encoder output (possibly of no rows)
     // sampling state per slot (allocated on first use): configuration, std::mt19937, the set of
     // token ids already in the sequence (one bit each), steps sampled since configured
     SampleSlot* d_samp = nullptr;
@@ -846,7 +847,7 @@ void stage_batch(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slots, co
             fail(ADAI_B200_ERR_OUT_OF_RANGE, "slot " + std::to_string(s) + " out of range");
         if (seen[s]) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "slot " + std::to_string(s) + " repeated in one batch");
         seen[s] = 1;
-        if (kv->cross_len[s] <= 0)
+        if (!kv->encoded[s])
             fail(ADAI_B200_ERR_STATE, "slot " + std::to_string(s) + " has no encoder output (call adai_b200_encode first)");
         if (kv->self_len[s] + steps > kv->self_cap)
             fail(ADAI_B200_ERR_OUT_OF_RANGE, "self-attention cache of slot " + std::to_string(s) +
@@ -1152,6 +1153,7 @@ int adai_b200_kv_create(adai_b200_ctx* c, int max_slots, int self_cap, int cross
         }
         kv->self_len.assign(max_slots, 0);
         kv->cross_len.assign(max_slots, 0);
+        kv->encoded.assign(max_slots, 0);
         cuda_ok(cudaStreamSynchronize(c->stream), "sync");
         c->kvs.insert(kv.get());
         *out = kv.release();
@@ -1182,6 +1184,7 @@ int adai_b200_kv_reset(adai_b200_ctx* c, adai_b200_kv* kv, int slot) {
         if (slot < 0 || slot >= kv->max_slots) fail(ADAI_B200_ERR_OUT_OF_RANGE, "slot out of range");
         kv->self_len[slot] = 0;
         kv->cross_len[slot] = 0;
+        kv->encoded[slot] = 0;
         cuda_ok(cudaMemsetAsync(kv->d_self_len + slot, 0, sizeof(int), c->stream), "memset");
         cuda_ok(cudaMemsetAsync(kv->d_cross_len + slot, 0, sizeof(int), c->stream), "memset");
         if (kv->d_samp) {  // back to the fused argmax
@@ -1228,7 +1231,9 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
             if (slots[i] < 0 || slots[i] >= kv->max_slots) fail(ADAI_B200_ERR_OUT_OF_RANGE, "slot out of range");
             if (seen[slots[i]]) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "slot repeated in one encode call");
             seen[slots[i]] = 1;
-            if (src_lens[i] <= 0) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "empty source sequence");
+            // No lower bound, as in the reference: an empty source has no encoder rows, and
+            // cross-attention over no rows contributes zeros.
+            if (src_lens[i] < 0) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "negative source length");
             // LLMEncoder::encode_with_mask refuses more than max_seq_length ids (src/LLMEncoder.cpp:106-116)
             if (src_lens[i] > m.d.max_seq)
                 fail(ADAI_B200_ERR_INVALID_ARGUMENT, std::to_string(src_lens[i]) + " tokens exceed max_seq_length " + std::to_string(m.d.max_seq));
@@ -1248,7 +1253,19 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
         while (i0 < n) {
             int i1 = i0, rows = 0;
             while (i1 < n && rows + src_lens[i1] <= e.rows) rows += src_lens[i1++];
+            if (i1 == i0)
+                fail(ADAI_B200_ERR_INVALID_ARGUMENT, "a source of " + std::to_string(src_lens[i0]) +
+                                                         " ids exceeds the encoder's row buffer");
             const int nseq = i1 - i0;
+            if (rows == 0) {  // only empty sources in this chunk: nothing to compute
+                for (int i = i0; i < i1; ++i) {
+                    kv->cross_len[slots[i]] = 0;
+                    kv->self_len[slots[i]] = 0;
+                    kv->encoded[slots[i]] = 1;
+                }
+                i0 = i1;
+                continue;
+            }
             int max_len = 0;
             int* pin = c->pinned(static_cast<size_t>(rows) * 4 + 3 * static_cast<size_t>(nseq));
             int* p_ids = pin;
@@ -1374,6 +1391,7 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
             for (int i = i0; i < i1; ++i) {
                 kv->cross_len[slots[i]] = src_lens[i];
                 kv->self_len[slots[i]] = 0;
+                kv->encoded[slots[i]] = 1;
             }
             c->sync(wait_timeout_seconds());
             row_base += rows;

@@ -161,7 +161,9 @@ ADAI_B200_API int adai_b200_kv_length(adai_b200_ctx* ctx, adai_b200_kv* kv, int 
  * with CrossAttention's first-call K/V projection, src/CrossAttention.cpp:388-413) ----
  * n requests; request i has src_lens[i] source ids (concatenated in ids) and is placed in slot
  * slots[i], whose self cache is cleared. Host arrays. Optionally returns the encoder output
- * [sum(src_lens), d_model] (enc_out may be NULL). */
+ * [sum(src_lens), d_model] (enc_out may be NULL). A source may be empty, as in the reference
+ * (only max_seq bounds it, src/LLMEncoder.cpp:106-122): it has no encoder rows, and the slot's
+ * cross-attention contributes zeros. */
 ADAI_B200_API int adai_b200_encode(adai_b200_ctx* ctx, adai_b200_kv* kv, int n, const int* slots,
                      const int* ids, const int* src_lens, float* enc_out);
 

@@ -214,7 +214,10 @@ static void ffn(const float* x, int rows, int D, int F, const float* w1, const f
 
 int orc_encode(orc_model* m, const int* ids, int S, float* out) {
     const int D = m->D, F = m->F, H = m->H;
-    if (S <= 0 || S > m->max_seq) return -1;
+    /* no lower bound: an empty source encodes to no rows, and cross-attention over no rows gives
+     * zeros (src/LLMEncoder.cpp:106-122 checks only the upper bound) */
+    if (S < 0 || S > m->max_seq) return -1;
+    if (S == 0) return 0;
     for (int i = 0; i < S; ++i)
         if (ids[i] < 0 || ids[i] >= m->V) return -1;
     size_t n = (size_t)S * D;

@@ -250,3 +250,26 @@ def test_wide_batch_one_attention_cta_per_head(ctx, port, tiny):
     kv.close()
     assert worst <= 1.0, worst
     assert all(tie for _, _, tie in mismatch), mismatch
+
+
+def test_empty_sources_decode_like_the_oracle(ctx, port, tiny):
+    # An empty source (no encoder rows, cross-attention contributes zeros) mixed into a batch,
+    # and a batch whose sources are all empty (nothing to encode).
+    srcs = make_sources(TINY, 4, (5, 30), 17)
+    srcs[1] = np.zeros(0, np.int32)
+    kv = ctx.kv_arena(4, 10, 32)
+    worst, mismatch = lockstep(kv, TINY, port.model(TINY, tiny), [0, 1, 2, 3], srcs, 8)
+    assert kv.length(1) == (8, 0)
+    kv.close()
+    assert worst <= 1.0, worst
+    assert all(tie for _, _, tie in mismatch), mismatch
+    kv = ctx.kv_arena(2, 10, 32)
+    empties = [np.zeros(0, np.int32)] * 2
+    worst, mismatch = lockstep(kv, TINY, port.model(TINY, tiny), [0, 1], empties, 8)
+    kv.close()
+    assert worst <= 1.0, worst
+    assert not mismatch, mismatch
+    kv = ctx.kv_arena(1, 4, 8)
+    with pytest.raises(StateError):  # never encoded: refused, as before
+        kv.decode_step([0], [BOS])
+    kv.close()
