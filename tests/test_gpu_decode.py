@@ -273,3 +273,21 @@ def test_empty_sources_decode_like_the_oracle(ctx, port, tiny):
     with pytest.raises(StateError):  # never encoded: refused, as before
         kv.decode_step([0], [BOS])
     kv.close()
+
+
+def test_maximum_source_length_and_last_vocabulary_id(ctx, port, tiny):
+    # A source of exactly max_seq_length ids (the largest LLMEncoder accepts) decodes in lockstep
+    # with the oracle; the last id of the vocabulary is a valid decoder input.
+    m = port.model(TINY, tiny)
+    src = [(np.arange(TINY.max_seq, dtype=np.int32) * 37 + 4) % TINY.vocab]
+    kv = ctx.kv_arena(1, 8, TINY.max_seq)
+    worst, mismatch = lockstep(kv, TINY, m, [0], src, 6)
+    assert worst <= 1.0, worst
+    assert all(tie for _, _, tie in mismatch), mismatch
+    kv.reset(0)
+    kv.encode([0], src)
+    nxt, lg = kv.decode_step([0], [TINY.vocab - 1], want_logits=True)
+    want_ids, want_lg = m.generate(src[0], 1, bos=TINY.vocab - 1, want_logits=True)
+    assert tol_ratio(lg[0], want_lg[0]) <= 1.0
+    assert nxt[0] == want_ids[0] or near_tie(want_lg[0], np.abs(lg[0] - want_lg[0]).max())
+    kv.close()
