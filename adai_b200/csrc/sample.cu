@@ -22,6 +22,7 @@
 // (std::partial_sort and std::sort leave their order unspecified).
 #include <cfloat>
 #include <cmath>
+#include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -616,17 +617,26 @@ int sample_max_vocab() {
     return max_v;
 }
 
+// The kernel's shared-memory limit, raised once per device (a process may drive several GPUs)
+// to what the largest accepted vocabulary needs.
+cudaError_t prepare_sample_attr() {
+    static std::mutex mu;
+    static unsigned long long done_mask = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 64 && (done_mask & (1ull << dev))) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(sample_rows_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(sample_smem_bytes(sample_max_vocab())));
+    if (e == cudaSuccess && dev < 64) done_mask |= 1ull << dev;
+    return e;
+}
+
 cudaError_t launch_sample_rows(const SampleArgs& a, cudaStream_t st) {
-    const size_t smem = sample_smem_bytes(a.V);
-    static size_t configured = 0;
-    if (smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(sample_rows_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
-        if (e != cudaSuccess) return e;
-        configured = smem;
-    }
-    return launch_kernel(sample_rows_kernel, dim3(a.B), dim3(kThreads), smem, st, a);
+    const cudaError_t e = prepare_sample_attr();
+    if (e != cudaSuccess) return e;
+    return launch_kernel(sample_rows_kernel, dim3(a.B), dim3(kThreads), sample_smem_bytes(a.V), st, a);
 }
 
 }  // namespace adai_b200
