@@ -69,6 +69,10 @@ WORKLOADS = {
     "large-encdec-b128-s128to1024-t256": Workload(
         "large-encdec-b128-s128to1024-t256", LARGE, 128, (128, 1024), 256,
         notes="128 sequences per GPU; batch 1024 over 8 GPUs"),
+    # the same 1024 sequences (same seed) on one GPU: the strong-scaling reference point
+    "large-encdec-b1024-s128to1024-t256": Workload(
+        "large-encdec-b1024-s128to1024-t256", LARGE, 1024, (128, 1024), 256,
+        notes="1024 sequences per GPU (about 130 GB of KV caches)"),
 }
 
 # Stacked-GEMM sweep shapes (M rows x K -> N) and the KV-attention op workload.

@@ -103,6 +103,10 @@ struct EncLayerW {
 struct DecLayerW {
     const float *ln1g, *ln1b, *ln2g, *ln2b, *ln3g, *ln3b, *b1, *b2;
     TcWeight qkv, o, cq, ckv, co, w1, w2;
+    // qkv, cq and w1 hold diag(gamma) W of the LayerNorm before them (kEpiLnFold): the column
+    // sums of that product and the bias beta W (+ b1 for w1)
+    float *qkv_c1 = nullptr, *qkv_bias = nullptr, *cq_c1 = nullptr, *cq_bias = nullptr,
+          *w1_c1 = nullptr, *w1_bias = nullptr;
 };
 
 struct Model {
@@ -114,7 +118,8 @@ struct Model {
                 *dec_lnf_b = nullptr, *head_b = nullptr;
     std::vector<EncLayerW> enc;
     std::vector<DecLayerW> dec;
-    TcWeight head;
+    TcWeight head;  // diag(final gamma) W_out; head_c1 / head_bias as for the layers' folded W
+    float *head_c1 = nullptr, *head_bias = nullptr;
     std::vector<void*> owned;
 };
 
@@ -123,6 +128,7 @@ struct StepBufs {
     float *x = nullptr, *nrm_hi = nullptr, *nrm_lo = nullptr, *qkv = nullptr, *attn_hi = nullptr,
           *attn_lo = nullptr, *qc = nullptr, *h_hi = nullptr, *h_lo = nullptr,
           *logits = nullptr;
+    float2* ln_stats = nullptr;  // [rows][d_model / 32] residual-stream group statistics
     int *ids = nullptr, *next = nullptr, *slots = nullptr, *nonfinite = nullptr,
         *nonfinite_any = nullptr;
 };
@@ -426,11 +432,54 @@ void fill_tc_weight(adai_b200_ctx* c, float* staging, const TcWeight& w, int row
     cuda_ok(cudaStreamSynchronize(c->stream), "upload sync");  // staging is reused
 }
 
+// Folds the LayerNorm (gamma g, beta b, both [K]) that precedes W [K, N] into it, in place:
+// W <- diag(g) W, c1[n] = sum_k (diag(g) W)[k][n], bias[n] = sum_k b[k] W[k][n] (+ extra[n]),
+// the sums in double over the fp32 products the GEMM multiplies.
+__global__ void fold_layernorm_kernel(float* __restrict__ w, int K, int N, const float* __restrict__ g,
+                                      const float* __restrict__ b, const float* __restrict__ extra,
+                                      float* __restrict__ c1, float* __restrict__ bias) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    double s1 = 0.0, s0 = extra ? static_cast<double>(extra[n]) : 0.0;
+    for (int k = 0; k < K; ++k) {
+        float* p = w + static_cast<size_t>(k) * N + n;
+        const float wk = *p;
+        const float ws = g[k] * wk;
+        *p = ws;
+        s1 += static_cast<double>(ws);
+        s0 += static_cast<double>(b[k]) * static_cast<double>(wk);
+    }
+    c1[n] = static_cast<float>(s1);
+    bias[n] = static_cast<float>(s0);
+}
+
+// fill_tc_weight for a W that a LayerNorm (g, b on the device) precedes: see
+// fold_layernorm_kernel; c1 / bias receive columns [row0, row0 + Nsub).
+void fill_tc_weight_folded(adai_b200_ctx* c, float* staging, const TcWeight& w, int row0,
+                           const float* host, int K, int Nsub, const float* g, const float* b,
+                           const float* extra, float* c1, float* bias) {
+    const size_t bytes = static_cast<size_t>(K) * Nsub * sizeof(float);
+    cuda_ok(cudaMemcpyAsync(staging, host, bytes, cudaMemcpyHostToDevice, c->stream), "upload");
+    fold_layernorm_kernel<<<(Nsub + 127) / 128, 128, 0, c->stream>>>(staging, K, Nsub, g, b, extra,
+                                                                     c1 + row0, bias + row0);
+    cuda_ok(cudaGetLastError(), "fold-layernorm");
+    launch_transpose_split(staging, K, Nsub, w.hi + static_cast<size_t>(row0) * K,
+                           w.lo + static_cast<size_t>(row0) * K, c->stream);
+    cuda_ok(cudaGetLastError(), "transpose-split");
+    cuda_ok(cudaStreamSynchronize(c->stream), "upload sync");  // staging is reused
+}
+
 float* upload_vec(adai_b200_ctx* c, std::vector<void*>& owned, const float* host, size_t n) {
     float* d = c->dalloc_t<float>(n);
     owned.push_back(d);
     cuda_ok(cudaMemcpyAsync(d, host, n * sizeof(float), cudaMemcpyHostToDevice, c->stream),
             "upload");
+    return d;
+}
+
+float* alloc_vec(adai_b200_ctx* c, std::vector<void*>& owned, size_t n) {
+    float* d = c->dzalloc_t<float>(n);
+    owned.push_back(d);
     return d;
 }
 
@@ -482,7 +531,7 @@ void ensure_step_bufs(adai_b200_ctx* c, int rows_needed) {
     for (void* p : {(void*)s.x, (void*)s.nrm_hi, (void*)s.nrm_lo, (void*)s.qkv, (void*)s.attn_hi,
                     (void*)s.attn_lo, (void*)s.qc, (void*)s.h_hi, (void*)s.h_lo, (void*)s.logits,
                     (void*)s.ids, (void*)s.next, (void*)s.slots, (void*)s.nonfinite,
-                    (void*)s.nonfinite_any})
+                    (void*)s.nonfinite_any, (void*)s.ln_stats})
         c->dfree(p);
     const size_t D = m.d.d_model, F = m.d.d_ff, V = m.d.vocab;
     s.rows = R;
@@ -501,6 +550,7 @@ void ensure_step_bufs(adai_b200_ctx* c, int rows_needed) {
     s.slots = c->dzalloc_t<int>(R);
     s.nonfinite = c->dzalloc_t<int>(R);
     s.nonfinite_any = c->dzalloc_t<int>(1);
+    s.ln_stats = c->dzalloc_t<float2>(R * (D / 32));
 }
 
 void ensure_enc_bufs(adai_b200_ctx* c) {
@@ -551,7 +601,7 @@ void free_step_bufs(adai_b200_ctx* c) {
     for (void* p : {(void*)s.x, (void*)s.nrm_hi, (void*)s.nrm_lo, (void*)s.qkv, (void*)s.attn_hi,
                     (void*)s.attn_lo, (void*)s.qc, (void*)s.h_hi, (void*)s.h_lo, (void*)s.logits,
                     (void*)s.ids, (void*)s.next, (void*)s.slots, (void*)s.nonfinite,
-                    (void*)s.nonfinite_any})
+                    (void*)s.nonfinite_any, (void*)s.ln_stats})
         c->dfree(p);
     s = StepBufs{};
 }
@@ -595,12 +645,29 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
     const float scale = 1.0f / std::sqrt(static_cast<float>(D / H));
     cudaStream_t st = c->stream;
     const double Bd = B, Dd = D, Fd = F;
-    const double ln_bytes = 2.0 * Bd * Dd * 4.0;
+    // Every LayerNorm is folded into the GEMM that consumes it (kEpiLnFold): the kernels that
+    // write the residual stream x also write its tf32 split (into nrm_hi / nrm_lo) and its
+    // per-32-column group statistics (kEpiRowStats), from which that GEMM takes mean and rstd.
+    const double ln_bytes = 3.0 * Bd * Dd * 4.0;
     timed(c, ADAI_B200_KC_NORM, ln_bytes, 0, [&] {
-        launch_embed_ln(m.dec_embed, s.ids, m.pe, m.d.max_seq, s.slots, kv->d_self_len, nullptr,
-                        s.x, m.dec[0].ln1g, m.dec[0].ln1b, s.nrm_hi, s.nrm_lo, B, D, m.d.vocab,
-                        c->d_err, st);
+        launch_embed_stats(m.dec_embed, s.ids, m.pe, m.d.max_seq, s.slots, kv->d_self_len, s.x,
+                           s.nrm_hi, s.nrm_lo, s.ln_stats, B, D, m.d.vocab, c->d_err, st);
     });
+    auto ln_fold = [&](GemmEpilogue& e, const float* c1, const float* bias) {
+        e.flags |= kEpiLnFold | kEpiBias;
+        e.ln_c1 = c1;
+        e.bias = bias;
+        e.row_stats = s.ln_stats;
+        e.stats_ld = R;
+    };
+    auto x_stats = [&](GemmEpilogue& e) {  // x written: also its split and group statistics
+        e.flags |= kEpiSplit | kEpiRowStats;
+        e.out_hi = s.nrm_hi;
+        e.out_lo = s.nrm_lo;
+        e.lds = D;
+        e.row_stats = s.ln_stats;
+        e.stats_ld = R;
+    };
     const double self_bytes = c->prof ? (2.0 * c->prof->sum_self_rows * Dd * 4.0 + 4.0 * Bd * Dd * 4.0) : 0;
     const double cross_bytes = c->prof ? (2.0 * c->prof->sum_cross_rows * Dd * 4.0 + 2.0 * Bd * Dd * 4.0) : 0;
     const TcActs a_nrm = acts(s.nrm_hi, s.nrm_lo, D, R);
@@ -613,6 +680,7 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             e.flags = kEpiStore;
             e.out = s.qkv;
             e.ldo = 3 * D;
+            ln_fold(e, w.qkv_c1, w.qkv_bias);
             timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, 3 * Dd, Dd), gemm_flops(Bd, 3 * Dd, Dd),
                   [&] { c->gemm(a_nrm, B, w.qkv, e); });
         }
@@ -650,17 +718,16 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             e.ldr = D;
             e.out = s.x;
             e.ldo = D;
+            x_stats(e);
             timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Dd, Dd), gemm_flops(Bd, Dd, Dd),
                   [&] { c->gemm(a_attn, B, w.o, e); });
         }
-        timed(c, ADAI_B200_KC_NORM, ln_bytes, 0, [&] {
-            launch_layernorm(s.x, D, w.ln2g, w.ln2b, nullptr, s.nrm_hi, s.nrm_lo, B, D, st);
-        });
-        {  // cross-attention query
+        {  // cross-attention query of LN2(x)
             GemmEpilogue e;
             e.flags = kEpiStore;
             e.out = s.qc;
             e.ldo = D;
+            ln_fold(e, w.cq_c1, w.cq_bias);
             timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Dd, Dd), gemm_flops(Bd, Dd, Dd),
                   [&] { c->gemm(a_nrm, B, w.cq, e); });
         }
@@ -695,19 +762,17 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             e.ldr = D;
             e.out = s.x;
             e.ldo = D;
+            x_stats(e);
             timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Dd, Dd), gemm_flops(Bd, Dd, Dd),
                   [&] { c->gemm(a_attn, B, w.co, e); });
         }
-        timed(c, ADAI_B200_KC_NORM, ln_bytes, 0, [&] {
-            launch_layernorm(s.x, D, w.ln3g, w.ln3b, nullptr, s.nrm_hi, s.nrm_lo, B, D, st);
-        });
-        {  // h = GELU(x W1 + b1), written as its tf32 split for the next GEMM
+        {  // h = GELU(LN3(x) W1 + b1), written as its tf32 split for the next GEMM
             GemmEpilogue e;
-            e.flags = kEpiBias | kEpiGelu | kEpiSplit;
-            e.bias = w.b1;
+            e.flags = kEpiGelu | kEpiSplit;
             e.out_hi = s.h_hi;
             e.out_lo = s.h_lo;
             e.lds = F;
+            ln_fold(e, w.w1_c1, w.w1_bias);
             timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Fd, Dd), gemm_flops(Bd, Fd, Dd),
                   [&] { c->gemm(a_nrm, B, w.w1, e); });
         }
@@ -719,20 +784,15 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             e.ldr = D;
             e.out = s.x;
             e.ldo = D;
+            x_stats(e);
             timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Dd, Fd), gemm_flops(Bd, Dd, Fd),
                   [&] { c->gemm(a_h, B, w.w2, e); });
         }
-        const bool last = (l + 1 == L);
-        timed(c, ADAI_B200_KC_NORM, ln_bytes, 0, [&] {
-            launch_layernorm(s.x, D, last ? m.dec_lnf_g : m.dec[l + 1].ln1g,
-                             last ? m.dec_lnf_b : m.dec[l + 1].ln1b, nullptr, s.nrm_hi, s.nrm_lo,
-                             B, D, st);
-        });
     }
     {  // logits = x W_out + b, first maximum per row
         GemmEpilogue e;
-        e.flags = kEpiBias | kEpiArgmax | ((flags & (kStepLogits | kStepSample)) ? kEpiStore : 0);
-        e.bias = m.head_b;
+        e.flags = kEpiArgmax | ((flags & (kStepLogits | kStepSample)) ? kEpiStore : 0);
+        ln_fold(e, m.head_c1, m.head_bias);  // the decoder's final LayerNorm
         e.out = s.logits;
         e.ldo = m.d.vocab;
         e.next_ids = s.next;
@@ -1011,15 +1071,20 @@ int adai_b200_model_upload(adai_b200_ctx* c, const adai_b200_model_desc* d,
                 w.ln1g = upload_vec(c, own, t[k++], D);
                 w.ln1b = upload_vec(c, own, t[k++], D);
                 w.qkv = make_tc_weight(c, own, D, 3 * D);
-                fill_tc_weight(c, staging, w.qkv, 0, t[k++], D, D);
-                fill_tc_weight(c, staging, w.qkv, D, t[k++], D, D);
-                fill_tc_weight(c, staging, w.qkv, 2 * D, t[k++], D, D);
+                w.qkv_c1 = alloc_vec(c, own, 3 * D);
+                w.qkv_bias = alloc_vec(c, own, 3 * D);
+                for (int j = 0; j < 3; ++j)
+                    fill_tc_weight_folded(c, staging, w.qkv, j * D, t[k++], D, D, w.ln1g, w.ln1b,
+                                          nullptr, w.qkv_c1, w.qkv_bias);
                 w.o = make_tc_weight(c, own, D, D);
                 fill_tc_weight(c, staging, w.o, 0, t[k++], D, D);
                 w.ln2g = upload_vec(c, own, t[k++], D);
                 w.ln2b = upload_vec(c, own, t[k++], D);
                 w.cq = make_tc_weight(c, own, D, D);
-                fill_tc_weight(c, staging, w.cq, 0, t[k++], D, D);
+                w.cq_c1 = alloc_vec(c, own, D);
+                w.cq_bias = alloc_vec(c, own, D);
+                fill_tc_weight_folded(c, staging, w.cq, 0, t[k++], D, D, w.ln2g, w.ln2b, nullptr,
+                                      w.cq_c1, w.cq_bias);
                 w.ckv = make_tc_weight(c, own, D, 2 * D);
                 fill_tc_weight(c, staging, w.ckv, 0, t[k++], D, D);
                 fill_tc_weight(c, staging, w.ckv, D, t[k++], D, D);
@@ -1028,8 +1093,12 @@ int adai_b200_model_upload(adai_b200_ctx* c, const adai_b200_model_desc* d,
                 w.ln3g = upload_vec(c, own, t[k++], D);
                 w.ln3b = upload_vec(c, own, t[k++], D);
                 w.w1 = make_tc_weight(c, own, D, F);
-                fill_tc_weight(c, staging, w.w1, 0, t[k++], D, F);
+                const float* w1_host = t[k++];
                 w.b1 = upload_vec(c, own, t[k++], F);
+                w.w1_c1 = alloc_vec(c, own, F);
+                w.w1_bias = alloc_vec(c, own, F);
+                fill_tc_weight_folded(c, staging, w.w1, 0, w1_host, D, F, w.ln3g, w.ln3b, w.b1,
+                                      w.w1_c1, w.w1_bias);
                 w.w2 = make_tc_weight(c, own, F, D);
                 fill_tc_weight(c, staging, w.w2, 0, t[k++], F, D);
                 w.b2 = upload_vec(c, own, t[k++], D);
@@ -1037,8 +1106,12 @@ int adai_b200_model_upload(adai_b200_ctx* c, const adai_b200_model_desc* d,
             m->dec_lnf_g = upload_vec(c, own, t[k++], D);
             m->dec_lnf_b = upload_vec(c, own, t[k++], D);
             m->head = make_tc_weight(c, own, D, V);
-            fill_tc_weight(c, staging, m->head, 0, t[k++], D, V);
+            const float* head_host = t[k++];
             m->head_b = upload_vec(c, own, t[k++], V);
+            m->head_c1 = alloc_vec(c, own, V);
+            m->head_bias = alloc_vec(c, own, V);
+            fill_tc_weight_folded(c, staging, m->head, 0, head_host, D, V, m->dec_lnf_g,
+                                  m->dec_lnf_b, m->head_b, m->head_c1, m->head_bias);
             std::vector<float> pe;
             if (!pe_table) {
                 pe = pe_table_host(d->max_seq, D);

@@ -47,7 +47,7 @@ constexpr int kThreads = 192;
 constexpr int kWarps = kThreads / 32;
 constexpr int kATileBytes = kBM * kBK * 4;  // 16 KB
 constexpr size_t kSmemLimit = 227 * 1024;
-constexpr size_t kSmemReserve = 1024 /*alignment slack*/ + 256 /*barriers*/;
+constexpr size_t kSmemReserve = 1024 /*alignment slack*/ + 256 /*barriers*/ + 1024 /*row mean, rstd*/;
 constexpr int kMaxCluster = 16;  // 8 is portable; 16 is used only where the device can place it
 
 // The epilogue flag sets the decode step and the op-level entry points use.
@@ -58,6 +58,14 @@ constexpr int kEpiSetFfnDown = kEpiBias | kEpiResid | kEpiStore;
 constexpr int kEpiSetHead = kEpiBias | kEpiArgmax;
 constexpr int kEpiSetHeadLogits = kEpiBias | kEpiArgmax | kEpiStore;
 constexpr int kEpiSetScatter = kEpiKvScatter;
+// The decode step's variants with the LayerNorm folded into the consuming GEMM: the GEMMs that
+// update the residual stream also write its tf32 split and row statistics.
+constexpr int kEpiSetStoreLn = kEpiBias | kEpiStore | kEpiLnFold;
+constexpr int kEpiSetResidStats = kEpiStore | kEpiResid | kEpiSplit | kEpiRowStats;
+constexpr int kEpiSetFfnUpLn = kEpiBias | kEpiGelu | kEpiSplit | kEpiLnFold;
+constexpr int kEpiSetFfnDownStats = kEpiBias | kEpiResid | kEpiStore | kEpiSplit | kEpiRowStats;
+constexpr int kEpiSetHeadLn = kEpiBias | kEpiArgmax | kEpiLnFold;
+constexpr int kEpiSetHeadLogitsLn = kEpiBias | kEpiArgmax | kEpiStore | kEpiLnFold;
 
 struct __align__(64) GemmKParams {
     CUtensorMap a_hi, a_lo, b_hi, b_lo;
@@ -95,13 +103,32 @@ struct ArgState {
 
 __device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
 
-// Epilogue on 4 consecutive output columns [col, col+4) of one row (col % 4 == 0, col < N).
+// Epilogue on 4 consecutive output columns [col, col+4) of one row (col % 4 == 0, col < N);
+// returns the final values (after the residual add). mean / rstd: the row's LayerNorm
+// statistics (kEpiLnFold only).
 template <int EPI>
-__device__ __forceinline__ void epilogue4(const GemmKParams& p, int row, int col, float4 acc,
-                                          ArgState& as) {
+__device__ __forceinline__ float4 epilogue4(const GemmKParams& p, int row, int col, float4 acc,
+                                            ArgState& as, float mean = 0.f, float rstd = 0.f) {
     const GemmEpilogue& e = p.epi;
     const int nv = min(4, p.N - col);
     float v[4] = {acc.x, acc.y, acc.z, acc.w};
+    if constexpr ((EPI & kEpiLnFold) != 0) {
+        // sum_k LN(x)_k W_kn = rstd * (sum_k x_k gamma_k W_kn - mean * ln_c1[n]) + (beta W)_n
+        float c1[4] = {0.f, 0.f, 0.f, 0.f};
+        if (nv == 4) {
+            const float4 c4 = __ldg(reinterpret_cast<const float4*>(e.ln_c1 + col));
+            c1[0] = c4.x;
+            c1[1] = c4.y;
+            c1[2] = c4.z;
+            c1[3] = c4.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (j < nv) c1[j] = __ldg(e.ln_c1 + col + j);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = rstd * fmaf(-mean, c1[j], v[j]);
+    }
     if constexpr ((EPI & kEpiBias) != 0) {
         if (nv == 4) {
             const float4 b4 = __ldg(reinterpret_cast<const float4*>(e.bias + col));
@@ -184,6 +211,51 @@ __device__ __forceinline__ void epilogue4(const GemmKParams& p, int row, int col
                      (static_cast<long long>(h) * e.cap + t) * e.head_dim + j0;
         st4(dst, make_float4(v[0], v[1], v[2], v[3]));
     }
+    return make_float4(v[0], v[1], v[2], v[3]);
+}
+
+// Combines the K / 32 group statistics (sum, squared deviations from the group mean) of one row,
+// contiguous at st, in group order (the parallel-variance combination of Chan et al.):
+// LayerNorm's mean and 1 / sqrt(biased variance + 1e-5), as LayerNorm::forward computes them
+// from the whole row. K is a multiple of 64 (two groups per 16-byte load).
+__device__ __forceinline__ void ln_row_stats(const float2* __restrict__ st, int K, float& mean,
+                                             float& rstd) {
+    const float4* s4 = reinterpret_cast<const float4*>(st);
+    const int pairs = K >> 6;
+    float sum = 0.f;
+#pragma unroll 8
+    for (int t = 0; t < pairs; ++t) {
+        const float4 g = __ldg(s4 + t);
+        sum += g.x;
+        sum += g.z;
+    }
+    mean = sum / static_cast<float>(K);
+    float m2 = 0.f;
+#pragma unroll 8
+    for (int t = 0; t < pairs; ++t) {
+        const float4 g = __ldg(s4 + t);
+        const float d0 = g.x * (1.0f / 32.0f) - mean, d1 = g.z * (1.0f / 32.0f) - mean;
+        m2 += g.y + 32.0f * d0 * d0;
+        m2 += g.w + 32.0f * d1 * d1;
+    }
+    rstd = 1.0f / sqrtf(m2 / static_cast<float>(K) + 1e-5f);
+}
+
+// Group statistics of 32 consecutive values of one row, held as one float4 by each of 8
+// consecutive lanes (lane % 8 == 0 holds the first four): written by that lane.
+__device__ __forceinline__ void row_group_stats(float4 v, float2* dst, int lane) {
+    const unsigned seg = 0xFFu << (lane & 24);
+    float s = (v.x + v.y) + (v.z + v.w);
+    s += __shfl_xor_sync(seg, s, 1);
+    s += __shfl_xor_sync(seg, s, 2);
+    s += __shfl_xor_sync(seg, s, 4);
+    const float mg = s * (1.0f / 32.0f);
+    const float a = v.x - mg, b = v.y - mg, c = v.z - mg, d = v.w - mg;
+    float q = (a * a + b * b) + (c * c + d * d);
+    q += __shfl_xor_sync(seg, q, 1);
+    q += __shfl_xor_sync(seg, q, 2);
+    q += __shfl_xor_sync(seg, q, 4);
+    if ((lane & 7) == 0) *dst = make_float2(s, q);
 }
 
 template <int BN, int EPI>
@@ -217,6 +289,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
     uint64_t* done_bar = recv_bar + 1;         // every MMA this CTA issued has completed
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
     int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+    // LayerNorm mean / rstd of the tile's rows (kEpiLnFold), after the 256 bytes of barriers
+    float* ln_mean = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full_bar) + 256);
+    float* ln_rstd = ln_mean + kBM;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -350,6 +425,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
         pdl_wait();  // the epilogue reads and writes data of earlier kernels
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int row_local = q * 32 + lane;
+        if constexpr ((EPI & kEpiLnFold) != 0) {
+            float mean = 0.f, rstd = 0.f;
+            if (m0 + row_local < p.M)
+                ln_row_stats(p.epi.row_stats + static_cast<size_t>(m0 + row_local) * (p.K >> 5),
+                             p.K, mean, rstd);
+            ln_mean[row_local] = mean;
+            ln_rstd[row_local] = rstd;
+        }
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
         float acc[BN];
 #pragma unroll
@@ -427,6 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
             const int r = it / kChunks, ch = it - r * kChunks;
             const int row = m0 + r_lo + r;
             const int col = n0 + ch * 4;
+            // a row's 32-column group is 8 consecutive items (threads): all skip or none do
             if (row >= p.M || col >= p.N) continue;
             float4 a4 = ld_shared_f4(slot_addr(0, r, ch));
             for (int s = 1; s < S; ++s) {
@@ -437,7 +521,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
                 a4.w += t.w;
             }
             ArgState unused{0.f, 0, 0};
-            epilogue4<EPI>(p, row, col, a4, unused);
+            float mean = 0.f, rstd = 0.f;
+            if constexpr ((EPI & kEpiLnFold) != 0) {
+                mean = ln_mean[r_lo + r];
+                rstd = ln_rstd[r_lo + r];
+            }
+            const float4 v = epilogue4<EPI>(p, row, col, a4, unused, mean, rstd);
+            if constexpr ((EPI & kEpiRowStats) != 0)
+                row_group_stats(v, p.epi.row_stats + static_cast<size_t>(row) * (p.N >> 5) + (col >> 5),
+                                lane);
         }
     } else {
         // one row per warp, so the row's first maximum over this tile is a warp reduction
@@ -445,6 +537,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
             const int row = m0 + r_lo + r;
             if (row >= p.M) break;
             ArgState as{-INFINITY, kArgNone, 0};
+            float mean = 0.f, rstd = 0.f;
+            if constexpr ((EPI & kEpiLnFold) != 0) {
+                mean = ln_mean[r_lo + r];
+                rstd = ln_rstd[r_lo + r];
+            }
             for (int ch = lane; ch < kChunks; ch += 32) {
                 const int col = n0 + ch * 4;
                 if (col >= p.N) break;
@@ -456,7 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
                     a4.z += t.z;
                     a4.w += t.w;
                 }
-                epilogue4<EPI>(p, row, col, a4, as);
+                epilogue4<EPI>(p, row, col, a4, as, mean, rstd);
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
@@ -567,6 +664,12 @@ GemmKernelFn kernel_for_epi(int flags) {
         case kEpiSetHead: return gemm_3xtf32_kernel<BN, kEpiSetHead>;
         case kEpiSetHeadLogits: return gemm_3xtf32_kernel<BN, kEpiSetHeadLogits>;
         case kEpiSetScatter: return gemm_3xtf32_kernel<BN, kEpiSetScatter>;
+        case kEpiSetStoreLn: return gemm_3xtf32_kernel<BN, kEpiSetStoreLn>;
+        case kEpiSetResidStats: return gemm_3xtf32_kernel<BN, kEpiSetResidStats>;
+        case kEpiSetFfnUpLn: return gemm_3xtf32_kernel<BN, kEpiSetFfnUpLn>;
+        case kEpiSetFfnDownStats: return gemm_3xtf32_kernel<BN, kEpiSetFfnDownStats>;
+        case kEpiSetHeadLn: return gemm_3xtf32_kernel<BN, kEpiSetHeadLn>;
+        case kEpiSetHeadLogitsLn: return gemm_3xtf32_kernel<BN, kEpiSetHeadLogitsLn>;
         default: return nullptr;
     }
 }
@@ -590,8 +693,10 @@ cudaError_t prepare_device_attrs() {
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(mu);
     if (dev >= 64 || (done_mask & (1ull << dev))) return cudaSuccess;
-    const int sets[] = {kEpiSetStore, kEpiSetResid, kEpiSetFfnUp, kEpiSetFfnDown, kEpiSetHead,
-                        kEpiSetHeadLogits, kEpiSetScatter};
+    const int sets[] = {kEpiSetStore,       kEpiSetResid,   kEpiSetFfnUp,        kEpiSetFfnDown,
+                        kEpiSetHead,        kEpiSetHeadLogits, kEpiSetScatter,   kEpiSetStoreLn,
+                        kEpiSetResidStats,  kEpiSetFfnUpLn, kEpiSetFfnDownStats, kEpiSetHeadLn,
+                        kEpiSetHeadLogitsLn};
     for (int bn : kTileWidths)
         for (int f : sets) {
             GemmKernelFn k = kernel_for(bn, f);
@@ -840,6 +945,16 @@ int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e
     if ((epi.flags & kEpiKvScatter) &&
         (epi.head_dim % 4 != 0 || epi.d_model % epi.head_dim != 0 || w.N != 2 * epi.d_model))
         return cudaErrorInvalidValue;
+    if ((epi.flags & kEpiRowStats) &&
+        (epi.row_stats == nullptr || epi.stats_ld < M || w.N % 64 != 0))
+        return cudaErrorInvalidValue;
+    if ((epi.flags & kEpiLnFold) &&
+        (epi.row_stats == nullptr || epi.ln_c1 == nullptr || epi.stats_ld < M || w.K % 64 != 0 ||
+         (reinterpret_cast<uintptr_t>(epi.row_stats) & 15) != 0 ||
+         (reinterpret_cast<uintptr_t>(epi.ln_c1) & 15) != 0))
+        return cudaErrorInvalidValue;
+    // barriers (2 per stage + 6), the TMEM slot and the ticket flag share 256 bytes
+    if ((2 * plan.stages + 6) * 8 + 8 > 256) return cudaErrorInvalidValue;
     const int n_rows_alloc = (w.N + 255) / 256 * 256;
 
     GemmKParams p{};

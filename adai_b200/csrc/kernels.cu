@@ -157,6 +157,67 @@ __global__ void embed_ln_kernel(const float* __restrict__ table, const int* __re
     ln_row_regs<NV>(xv, g, b, D, lane, nullptr, out_hi + o, out_lo + o);
 }
 
+// The decode step's embedding when the first LayerNorm is folded into the Q|K|V GEMM:
+// x[r] = table[ids[r]] + pe[pos(r)], its tf32 split, and per 32-column group the statistics
+// (sum, squared deviations from the group mean) that the GEMM combines into mean and rstd.
+template <int NV>
+__global__ void embed_stats_kernel(const float* __restrict__ table, const int* __restrict__ ids,
+                                   const float* __restrict__ pe, int pe_rows,
+                                   const int* __restrict__ slots, const int* __restrict__ pos_by_slot,
+                                   float* __restrict__ x, float* x_hi, float* x_lo,
+                                   float2* __restrict__ stats, int rows, int D, int vocab,
+                                   int* err) {
+    pdl_trigger();
+    pdl_wait();
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    int id = ids[row];
+    if (id < 0 || id >= vocab) {  // TokenEmbedding::forward throws std::out_of_range here
+        if (lane == 0) record_error(err, kDevBadShape);
+        id = 0;
+    }
+    const int pos = pos_by_slot[slots ? slots[row] : row];
+    const float* er = table + static_cast<size_t>(id) * D;
+    const bool has_pe = pos >= 0 && pos < pe_rows;
+    const float* pr = pe + static_cast<size_t>(has_pe ? pos : 0) * D;
+    const unsigned seg = 0xFFu << (lane & 24);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int c0 = (i * 32 + lane) * 4;
+        float4 e = *reinterpret_cast<const float4*>(er + c0);
+        if (has_pe) {
+            const float4 p = *reinterpret_cast<const float4*>(pr + c0);
+            e.x += p.x;
+            e.y += p.y;
+            e.z += p.z;
+            e.w += p.w;
+        }
+        const size_t o = static_cast<size_t>(row) * D + c0;
+        *reinterpret_cast<float4*>(x + o) = e;
+        float4 h, l;
+        split_tf32(e.x, h.x, l.x);
+        split_tf32(e.y, h.y, l.y);
+        split_tf32(e.z, h.z, l.z);
+        split_tf32(e.w, h.w, l.w);
+        *reinterpret_cast<float4*>(x_hi + o) = h;
+        *reinterpret_cast<float4*>(x_lo + o) = l;
+        // lanes 8j..8j+7 hold columns [32(4i+j), 32(4i+j) + 32): one group
+        float sg = (e.x + e.y) + (e.z + e.w);
+        sg += __shfl_xor_sync(seg, sg, 1);
+        sg += __shfl_xor_sync(seg, sg, 2);
+        sg += __shfl_xor_sync(seg, sg, 4);
+        const float mg = sg * (1.0f / 32.0f);
+        const float a = e.x - mg, b = e.y - mg, c = e.z - mg, d = e.w - mg;
+        float q = (a * a + b * b) + (c * c + d * d);
+        q += __shfl_xor_sync(seg, q, 1);
+        q += __shfl_xor_sync(seg, q, 2);
+        q += __shfl_xor_sync(seg, q, 4);
+        if ((lane & 7) == 0)
+            stats[static_cast<size_t>(row) * (D >> 5) + (c0 >> 5)] = make_float2(sg, q);
+    }
+}
+
 // ---------------------------------------------------------------------------------------------
 // Decode attention, templated on the head width DH (32 or 64). One CTA per (chunk of kAttnChunk
 // cached rows, head, batch row), 4 warps. A row of one head is DH floats = LPR lanes x float4, so
@@ -518,6 +579,16 @@ void launch_embed_ln(const float* table, const int* ids, const float* pe, int pe
     const dim3 block(128), grid((rows + 3) / 4);
     ADAI_LN_DISPATCH(D / 128, embed_ln_kernel, table, ids, pe, pe_rows, slots, pos_by_slot,
                      pos_direct, x, g, b, out_hi, out_lo, rows, D, vocab, err);
+}
+
+void launch_embed_stats(const float* table, const int* ids, const float* pe, int pe_rows,
+                        const int* slots, const int* pos_by_slot, float* x, float* x_hi,
+                        float* x_lo, float2* stats, int rows, int D, int vocab, int* err,
+                        cudaStream_t st) {
+    if (rows <= 0) return;
+    const dim3 block(128), grid((rows + 3) / 4);
+    ADAI_LN_DISPATCH(D / 128, embed_stats_kernel, table, ids, pe, pe_rows, slots, pos_by_slot, x,
+                     x_hi, x_lo, stats, rows, D, vocab, err);
 }
 
 bool attention_head_dim_supported(int dh) { return dh == 32 || dh == 64; }

@@ -53,6 +53,15 @@ enum GemmFlags : int {
     kEpiSplit = 16,     // write the tf32 split of the result to out_hi / out_lo
     kEpiArgmax = 32,    // per-row first maximum -> next_ids (and the non-finite flag)
     kEpiKvScatter = 64, // columns [0,D) -> K cache, [D,2D) -> V cache at (row_slot, row_pos)
+    // Per output row and 32-column group: (sum, sum of squared deviations from the group mean)
+    // -> row_stats[row * (N / 32) + col / 32] (N a multiple of 64). Written by the GEMMs that
+    // produce the residual stream, for the LayerNorm the next GEMM folds in.
+    kEpiRowStats = 128,
+    // LayerNorm folded into this GEMM: A holds the split of the un-normalised rows x, W holds
+    // diag(gamma) W, and the result is rstd * (acc - mean * ln_c1[n]) before the bias, where
+    // ln_c1 = column sums of diag(gamma) W and the bias holds beta W (+ the layer's own bias).
+    // mean / rstd per row come from the K / 32 group statistics in row_stats.
+    kEpiLnFold = 256,
 };
 
 struct GemmEpilogue {
@@ -77,6 +86,10 @@ struct GemmEpilogue {
     int d_model = 0;
     const int* row_slot = nullptr;
     const int* row_pos = nullptr;
+    // row statistics (kEpiRowStats writes, kEpiLnFold reads): float2 [stats_ld rows][width / 32]
+    float2* row_stats = nullptr;
+    int stats_ld = 0;  // rows allocated
+    const float* ln_c1 = nullptr;  // kEpiLnFold: [N]
 };
 
 // A prepared right-hand operand: W^T split into hi/lo, [N, K] row-major, device memory.
@@ -146,6 +159,13 @@ void launch_embed_ln(const float* table, const int* ids, const float* pe, int pe
                      const int* slots, const int* pos_by_slot, const int* pos_direct, float* x,
                      const float* g, const float* b, float* out_hi, float* out_lo, int rows,
                      int D, int vocab, int* err, cudaStream_t st);
+// x[r] = table[ids[r]] + pe[pos_by_slot[slots[r]]] (no positional row when pos >= pe_rows),
+// its tf32 split, and the row statistics of kEpiRowStats (the decode step's first LayerNorm is
+// folded into the Q|K|V GEMM).
+void launch_embed_stats(const float* table, const int* ids, const float* pe, int pe_rows,
+                        const int* slots, const int* pos_by_slot, float* x, float* x_hi,
+                        float* x_lo, float2* stats, int rows, int D, int vocab, int* err,
+                        cudaStream_t st);
 
 // ------------------------------------------------------------------------------------------
 // Attention
