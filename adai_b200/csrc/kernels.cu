@@ -256,27 +256,50 @@ __device__ __forceinline__ void write_out(const DecodeAttnArgs& a, int b, int h,
 }
 
 template <int DH>
-__global__ void __launch_bounds__(kAttnWarps * 32) decode_attention_kernel(const __grid_constant__ DecodeAttnArgs a) {
+__global__ void __launch_bounds__(kAttnWarps * 32, 8) decode_attention_kernel(const __grid_constant__ DecodeAttnArgs a) {
     constexpr int LPR = DH / 4;        // lanes per cached row
     constexpr int RPW = 32 / LPR;      // rows per warp per load
     constexpr int G = kAttnWarps * RPW;  // consecutive rows per CTA per load
     constexpr unsigned kRowMask = (LPR == 32) ? 0xffffffffu : ((1u << LPR) - 1u);
     pdl_trigger();
-    pdl_wait();
+    // Before the wait for the preceding kernel: the slot table, the cached lengths and the rows
+    // cached before this step were all written before this step's first kernel (the lengths
+    // advance only after the step's last GEMM), so the first batch of rows is requested now.
+    // The appended row, q and the output are touched only after the wait.
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int slot = a.slots ? a.slots[b] : b;
     const int len = a.len_by_slot[slot] + a.len_add;
     const int nch = (len + kAttnChunk - 1) / kAttnChunk;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int rsub = lane / LPR, l = lane % LPR;
+    const int r0 = c * kAttnChunk;
+    const int r1 = min(len, r0 + kAttnChunk);
+    const int pre_end = min(r1, len - a.len_add);  // rows cached before this step
+    float* Kh = a.kc + static_cast<long long>(slot) * a.slot_stride + static_cast<long long>(h) * a.cap * DH;
+    float* Vh = a.vc + static_cast<long long>(slot) * a.slot_stride + static_cast<long long>(h) * a.cap * DH;
+    float4 kk0[kAttnUnroll], vv0[kAttnUnroll];
+    {
+        const int base = r0 + warp * RPW + rsub;
+#pragma unroll
+        for (int u = 0; u < kAttnUnroll; ++u) {
+            const int r = base + G * u;
+            if (len > 0 && c < nch && r < pre_end) {
+                kk0[u] = __ldcs(reinterpret_cast<const float4*>(Kh + static_cast<size_t>(r) * DH + l * 4));
+                vv0[u] = __ldcs(reinterpret_cast<const float4*>(Vh + static_cast<size_t>(r) * DH + l * 4));
+            } else {
+                kk0[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                vv0[u] = kk0[u];
+            }
+        }
+    }
+    pdl_wait();
     if (len <= 0) {
         // No cached rows: the reference's softmax over an empty row leaves nothing; output 0.
         if (c == 0 && warp == 0 && rsub == 0) write_out<DH>(a, b, h, l, make_float4(0.f, 0.f, 0.f, 0.f));
         return;
     }
     if (c >= nch) return;
-    float* Kh = a.kc + static_cast<long long>(slot) * a.slot_stride + static_cast<long long>(h) * a.cap * DH;
-    float* Vh = a.vc + static_cast<long long>(slot) * a.slot_stride + static_cast<long long>(h) * a.cap * DH;
+    const float4 q = *reinterpret_cast<const float4*>(a.q + static_cast<size_t>(b) * a.ldq + h * DH + l * 4);
 
     // Fused KV append: the CTA whose chunk holds the new row writes it (KVCache::append).
     if (a.k_new && (len - 1) / kAttnChunk == c) {
@@ -292,27 +315,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32) decode_attention_kernel(const
         __syncthreads();
     }
 
-    const float4 q = *reinterpret_cast<const float4*>(a.q + static_cast<size_t>(b) * a.ldq + h * DH + l * 4);
-    const int r0 = c * kAttnChunk;
-    const int r1 = min(len, r0 + kAttnChunk);
     float m = -INFINITY, lsum = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 
-    // The loop bound (gb) is warp-uniform, so every shuffle has all 32 lanes present.
-    for (int gb = r0 + warp * RPW; gb < r1; gb += G * kAttnUnroll) {
-        const int base = gb + rsub;
-        float4 kk[kAttnUnroll], vv[kAttnUnroll];
-#pragma unroll
-        for (int u = 0; u < kAttnUnroll; ++u) {
-            const int r = base + G * u;
-            if (r < r1) {
-                kk[u] = __ldcs(reinterpret_cast<const float4*>(Kh + static_cast<size_t>(r) * DH + l * 4));
-                vv[u] = __ldcs(reinterpret_cast<const float4*>(Vh + static_cast<size_t>(r) * DH + l * 4));
-            } else {
-                kk[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                vv[u] = kk[u];
-            }
-        }
+    // One batch of kAttnUnroll row groups: scores, online softmax, weighted V.
+    auto batch = [&](const float4 (&kk)[kAttnUnroll], const float4 (&vv)[kAttnUnroll], int base) {
         float s[kAttnUnroll];
 #pragma unroll
         for (int u = 0; u < kAttnUnroll; ++u) {
@@ -343,6 +350,37 @@ __global__ void __launch_bounds__(kAttnWarps * 32) decode_attention_kernel(const
             acc.w = fmaf(pu, vv[u].w, acc.w);
         }
         m = mu;
+    };
+    // The loop bound (gb) is warp-uniform, so every shuffle has all 32 lanes present. The first
+    // batch was requested before the wait, except rows appended by this step.
+    const int gb0 = r0 + warp * RPW;
+    if (gb0 < r1) {
+        const int base = gb0 + rsub;
+#pragma unroll
+        for (int u = 0; u < kAttnUnroll; ++u) {
+            const int r = base + G * u;
+            if (r >= pre_end && r < r1) {
+                kk0[u] = __ldcs(reinterpret_cast<const float4*>(Kh + static_cast<size_t>(r) * DH + l * 4));
+                vv0[u] = __ldcs(reinterpret_cast<const float4*>(Vh + static_cast<size_t>(r) * DH + l * 4));
+            }
+        }
+        batch(kk0, vv0, base);
+    }
+    for (int gb = gb0 + G * kAttnUnroll; gb < r1; gb += G * kAttnUnroll) {
+        const int base = gb + rsub;
+        float4 kk[kAttnUnroll], vv[kAttnUnroll];
+#pragma unroll
+        for (int u = 0; u < kAttnUnroll; ++u) {
+            const int r = base + G * u;
+            if (r < r1) {
+                kk[u] = __ldcs(reinterpret_cast<const float4*>(Kh + static_cast<size_t>(r) * DH + l * 4));
+                vv[u] = __ldcs(reinterpret_cast<const float4*>(Vh + static_cast<size_t>(r) * DH + l * 4));
+            } else {
+                kk[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                vv[u] = kk[u];
+            }
+        }
+        batch(kk, vv, base);
     }
     // merge the warp's row groups (lanes l, l+LPR, l+2LPR, ... hold the same output dims)
 #pragma unroll

@@ -113,6 +113,27 @@ def test_ragged_batch_lockstep_with_random_affine(ctx, port, tiny):
     kv.close()
 
 
+@pytest.mark.parametrize("offset", [4.0, 16.0])
+def test_folded_layernorm_on_rows_with_a_large_mean(port, offset):
+    # The decode step folds each LayerNorm into the GEMM after it, which subtracts
+    # mean * colsum(diag(gamma) W) from the product of the raw rows: the cancellation grows with
+    # |mean| / std of a row. A decoder embedding shifted by `offset` gives every residual row a
+    # mean of about offset against a spread below 1.
+    from adai_b200.synth import tensor_specs
+    w = make_weights(TINY, 13, affine=True)
+    names = [n for n, _ in tensor_specs(TINY)]
+    w[names.index("dec.embed")] = w[names.index("dec.embed")] + np.float32(offset)
+    with Context(0) as c:
+        c.upload(TINY, w)
+        srcs = make_sources(TINY, 4, (8, 48), 13)
+        kv = c.kv_arena(4, 16, 64)
+        worst, mism = lockstep(kv, TINY, port.model(TINY, w), [0, 1, 2, 3], srcs, 12)
+        print(f"row mean offset {offset}: worst tolerance ratio {worst:.4f}")
+        assert worst <= 1.0, worst
+        assert all(tie for _, _, tie in mism), mism
+        kv.close()
+
+
 def test_mid_model_lockstep(port):
     # Mid encoder-decoder (d_model 512, 8 heads, 6+6 layers, d_ff 2048, vocab 16000); 4 of the
     # workload's 64 sequences (source length 256), 12 steps.
