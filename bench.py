@@ -306,6 +306,7 @@ def main():
     ap.add_argument("--cpu-baseline-steps", type=int, default=12)
     ap.add_argument("--reference-max-steps", type=int, default=48)
     ap.add_argument("--profile-steps", type=int, default=3)
+    ap.add_argument("--src-len", default="", help="LO,HI: override the workload's source lengths")
     ap.add_argument("--op", choices=["gemm", "attention", "sample", "prefill"], default=None)
     ap.add_argument("--prefill-batch", type=int, default=16)
     ap.add_argument("--prefill-len", type=int, default=512)
@@ -325,6 +326,10 @@ def main():
         run_op(args)
         return
     wl = WORKLOADS[args.workload]
+    if args.src_len:  # a smaller case of the workload (profiling captures); named as such
+        import dataclasses
+        lo, hi = (int(v) for v in args.src_len.split(","))
+        wl = dataclasses.replace(wl, name=f"{wl.name}-src{lo}to{hi}", src_len=(lo, hi))
     rank, world, local = dist_env()
 
     if args.impl == "reference":
