@@ -255,11 +255,11 @@ __device__ __forceinline__ void write_out(const DecodeAttnArgs& a, int b, int h,
     }
 }
 
-template <int DH, int NW>
-__global__ void __launch_bounds__(NW * 32, 32 / NW) decode_attention_kernel(const __grid_constant__ DecodeAttnArgs a) {
+template <int DH>
+__global__ void __launch_bounds__(kAttnWarps * 32, 8) decode_attention_kernel(const __grid_constant__ DecodeAttnArgs a) {
     constexpr int LPR = DH / 4;        // lanes per cached row
     constexpr int RPW = 32 / LPR;      // rows per warp per load
-    constexpr int G = NW * RPW;  // consecutive rows per CTA per load
+    constexpr int G = kAttnWarps * RPW;  // consecutive rows per CTA per load
     constexpr unsigned kRowMask = (LPR == 32) ? 0xffffffffu : ((1u << LPR) - 1u);
     pdl_trigger();
     // Before the wait for the preceding kernel: the slot table, the cached lengths and the rows
@@ -394,8 +394,8 @@ __global__ void __launch_bounds__(NW * 32, 32 / NW) decode_attention_kernel(cons
         a2.w = __shfl_xor_sync(0xffffffffu, acc.w, o);
         merge_into(m, lsum, acc, m2, l2, a2);
     }
-    __shared__ float sm_m[NW], sm_l[NW];
-    __shared__ float4 sm_acc[NW][LPR];
+    __shared__ float sm_m[kAttnWarps], sm_l[kAttnWarps];
+    __shared__ float4 sm_acc[kAttnWarps][LPR];
     if (rsub == 0) {
         sm_acc[warp][l] = acc;
         if (l == 0) {
@@ -408,7 +408,7 @@ __global__ void __launch_bounds__(NW * 32, 32 / NW) decode_attention_kernel(cons
     float M = sm_m[0], L = sm_l[0];
     float4 A = sm_acc[0][l];
 #pragma unroll
-    for (int w = 1; w < NW; ++w) merge_into(M, L, A, sm_m[w], sm_l[w], sm_acc[w][l]);
+    for (int w = 1; w < kAttnWarps; ++w) merge_into(M, L, A, sm_m[w], sm_l[w], sm_acc[w][l]);
 
     if (nch == 1) {
         const float inv = 1.0f / L;
@@ -641,22 +641,10 @@ void launch_decode_attention(const DecodeAttnArgs& a, int* err, cudaStream_t st)
     if (a.B <= 0) return;
     const int max_ch = (std::max(a.max_len, 1) + kAttnChunk - 1) / kAttnChunk;
     dim3 grid(max_ch, a.H, a.B);
-    // Up to 512 cached rows per (sequence, head): two-warp CTAs, so that the whole grid is
-    // resident at once (16 per SM at 64 registers) and no second wave waits behind the first.
-    // Longer rows keep four warps per CTA (more loads in flight per CTA, the bandwidth-bound
-    // case). Measured on the large decode step: 2.418 -> 2.408 ms per step with two-warp
-    // self-attention; two-warp cross-attention (up to 1024 rows) 2.477 ms.
-    if (max_ch <= 2) {
-        if (a.head_dim == 32)
-            launch_kernel(decode_attention_kernel<32, 2>, grid, dim3(2 * 32), 0, st, a);
-        else
-            launch_kernel(decode_attention_kernel<64, 2>, grid, dim3(2 * 32), 0, st, a);
-    } else {
-        if (a.head_dim == 32)
-            launch_kernel(decode_attention_kernel<32, kAttnWarps>, grid, dim3(kAttnWarps * 32), 0, st, a);
-        else
-            launch_kernel(decode_attention_kernel<64, kAttnWarps>, grid, dim3(kAttnWarps * 32), 0, st, a);
-    }
+    if (a.head_dim == 32)
+        launch_kernel(decode_attention_kernel<32>, grid, dim3(kAttnWarps * 32), 0, st, a);
+    else
+        launch_kernel(decode_attention_kernel<64>, grid, dim3(kAttnWarps * 32), 0, st, a);
 }
 
 void launch_prefill_attention(const float* qkv, int D, int H, const int* offsets, const int* lens,
