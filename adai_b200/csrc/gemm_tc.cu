@@ -23,8 +23,9 @@
 // with one bulk copy per owner (cp.async.bulk shared::cta -> shared::cluster, completing on the
 // owner's mbarrier); every CTA then sums its 128/S rows over the S slots in rank order 0..S-1
 // (deterministic) and runs the fused epilogue with coalesced float4 stores:
-// bias / GELU / residual / fp32 store / tf32 split of the output / KV-cache scatter /
-// first-maximum argmax partials (the LM head). The epilogue is a template parameter so each
+// folded LayerNorm / bias / GELU / residual / fp32 store / tf32 split of the output / row
+// statistics for the next folded LayerNorm / KV-cache scatter / first-maximum argmax partials
+// (the LM head). The epilogue is a template parameter so each
 // instantiation carries only its own code. No TMA multicast anywhere.
 #include <algorithm>
 #include <cstdio>
