@@ -222,6 +222,8 @@ struct adai_b200_ctx {
     float* samp_park = nullptr;  // [rows, V]: top-p parks the filtered logits here
     size_t samp_park_floats = 0;
     int* h_pin = nullptr;  // pinned staging for ids / slots / lengths
+    int* h_err = nullptr;  // pinned copy of the device error word, read back by sync()
+    cudaEvent_t sync_ev = nullptr;
     size_t h_pin_ints = 0;
     std::map<GraphKey, cudaGraphExec_t> graphs;
     std::map<GraphKey, int> graph_kernels;
@@ -283,31 +285,29 @@ struct adai_b200_ctx {
     }
     // Bounded host wait (GPU_WAIT_TIMEOUT_SECONDS semantics), then the device error word.
     void sync(double timeout_s) {
-        cudaEvent_t ev;
-        cuda_ok(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "cudaEventCreate");
+        // the error word comes back with the work (no second round trip after the wait)
+        cuda_ok(cudaMemcpyAsync(h_err, d_err, sizeof(int), cudaMemcpyDeviceToHost, stream),
+                "read error word");
+        cudaEvent_t ev = sync_ev;
         cuda_ok(cudaEventRecord(ev, stream), "cudaEventRecord");
         const auto t0 = std::chrono::steady_clock::now();
         while (true) {
             const cudaError_t q = cudaEventQuery(ev);
             if (q == cudaSuccess) break;
             if (q != cudaErrorNotReady) {
-                cudaEventDestroy(ev);
                 unusable = true;
                 fail(ADAI_B200_ERR_CUDA, std::string("device error: ") + cudaGetErrorString(q));
             }
             const double el =
                 std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
             if (el > timeout_s) {
-                cudaEventDestroy(ev);
                 unusable = true;
                 fail(ADAI_B200_ERR_TIMEOUT,
                      "device wait exceeded " + std::to_string(timeout_s) + " s");
             }
             std::this_thread::yield();
         }
-        cudaEventDestroy(ev);
-        int herr = 0;
-        cuda_ok(cudaMemcpy(&herr, d_err, sizeof(int), cudaMemcpyDeviceToHost), "read error word");
+        const int herr = *h_err;
         if (herr != 0) {
             cuda_ok(cudaMemset(d_err, 0, sizeof(int)), "clear error word");
             if (herr >= 101 && herr <= 103) {
@@ -956,6 +956,10 @@ int adai_b200_ctx_create(int device, float mem_fraction, adai_b200_ctx** out) {
         if (mem_fraction > 0.f) c->mem_cap = static_cast<size_t>(static_cast<double>(prop.totalGlobalMem) * mem_fraction);
         cuda_ok(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate");
         c->d_err = c->dzalloc_t<int>(1);
+        cuda_ok(cudaHostAlloc(reinterpret_cast<void**>(&c->h_err), sizeof(int), cudaHostAllocDefault),
+                "cudaHostAlloc");
+        *c->h_err = 0;
+        cuda_ok(cudaEventCreateWithFlags(&c->sync_ev, cudaEventDisableTiming), "cudaEventCreate");
         cuda_ok(cudaStreamSynchronize(c->stream), "sync");
         *out = c.release();
     });
@@ -972,6 +976,8 @@ int adai_b200_ctx_destroy(adai_b200_ctx* c) {
         for (adai_b200_kv* kv : c->kvs) delete kv;
         c->kvs.clear();
         if (c->h_pin) cudaFreeHost(c->h_pin);
+        if (c->h_err) cudaFreeHost(c->h_err);
+        if (c->sync_ev) cudaEventDestroy(c->sync_ev);
         cudaStreamDestroy(c->stream);
         delete c;
     });
