@@ -348,7 +348,8 @@ struct adai_b200_ctx {
         }
     }
     void ensure_attn_scratch(int B, int H, int max_len, int dh) {
-        const size_t f = decode_attn_ws_floats(B, H, max_len, dh);
+        // the decode step's cross-attention uses the shorter chunk: the most partials per row
+        const size_t f = decode_attn_ws_floats(B, H, max_len, dh, kAttnChunkShort);
         const int tk = B * H;
         if (f > attn_ws_floats || tk > attn_n_tickets) {
             cuda_ok(cudaStreamSynchronize(stream), "sync before scratch growth");
@@ -742,6 +743,7 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             a.slots = s.slots;
             a.len_by_slot = kv->d_cross_len;
             a.len_add = 0;
+            a.chunk = kAttnChunkShort;  // 128-row chunks: more CTAs over the longer source rows
             a.out_hi = s.attn_hi;
             a.out_lo = s.attn_lo;
             a.ldo = D;

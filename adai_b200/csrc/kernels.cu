@@ -219,7 +219,7 @@ __global__ void embed_stats_kernel(const float* __restrict__ table, const int* _
 }
 
 // ---------------------------------------------------------------------------------------------
-// Decode attention, templated on the head width DH (32 or 64). One CTA per (chunk of kAttnChunk
+// Decode attention, templated on the head width DH (32 or 64). One CTA per (chunk of a.chunk
 // cached rows, head, batch row), 4 warps. A row of one head is DH floats = LPR lanes x float4, so
 // a warp covers RPW = 32 / LPR rows per load and the CTA 4 * RPW consecutive rows (contiguous
 // bytes in the [slot][head][row][DH] cache). Online softmax per row group of lanes, merged across
@@ -269,11 +269,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 8) decode_attention_kernel(co
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int slot = a.slots ? a.slots[b] : b;
     const int len = a.len_by_slot[slot] + a.len_add;
-    const int nch = (len + kAttnChunk - 1) / kAttnChunk;
+    const int chunk = a.chunk;
+    const int nch = (len + chunk - 1) / chunk;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int rsub = lane / LPR, l = lane % LPR;
-    const int r0 = c * kAttnChunk;
-    const int r1 = min(len, r0 + kAttnChunk);
+    const int r0 = c * chunk;
+    const int r1 = min(len, r0 + chunk);
     const int pre_end = min(r1, len - a.len_add);  // rows cached before this step
     float* Kh = a.kc + static_cast<long long>(slot) * a.slot_stride + static_cast<long long>(h) * a.cap * DH;
     float* Vh = a.vc + static_cast<long long>(slot) * a.slot_stride + static_cast<long long>(h) * a.cap * DH;
@@ -302,7 +303,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 8) decode_attention_kernel(co
     const float4 q = *reinterpret_cast<const float4*>(a.q + static_cast<size_t>(b) * a.ldq + h * DH + l * 4);
 
     // Fused KV append: the CTA whose chunk holds the new row writes it (KVCache::append).
-    if (a.k_new && (len - 1) / kAttnChunk == c) {
+    if (a.k_new && (len - 1) / chunk == c) {
         const int t = len - 1;
         if (threadIdx.x < LPR) {
             const float4 kv = *reinterpret_cast<const float4*>(a.k_new + static_cast<size_t>(b) * a.ldkv + h * DH + threadIdx.x * 4);
@@ -418,7 +419,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 8) decode_attention_kernel(co
     // Split-KV: publish this chunk's partial; the last chunk to finish merges them in order.
     constexpr int kPart = DH + 4;  // m, l, 2 pad, DH accumulators
     const int pair = b * a.H + h;
-    const int max_ch = (a.max_len + kAttnChunk - 1) / kAttnChunk;
+    const int max_ch = (a.max_len + chunk - 1) / chunk;
     float* part = a.ws + (static_cast<size_t>(pair) * max_ch + c) * kPart;
     *reinterpret_cast<float4*>(part + 4 + l * 4) = A;
     if (l == 0) {
@@ -631,20 +632,22 @@ void launch_embed_stats(const float* table, const int* ids, const float* pe, int
 
 bool attention_head_dim_supported(int dh) { return dh == 32 || dh == 64; }
 
-size_t decode_attn_ws_floats(int B, int H, int max_len, int head_dim) {
-    const int max_ch = (std::max(max_len, 1) + kAttnChunk - 1) / kAttnChunk;
+size_t decode_attn_ws_floats(int B, int H, int max_len, int head_dim, int chunk) {
+    const int max_ch = (std::max(max_len, 1) + chunk - 1) / chunk;
     return static_cast<size_t>(B) * H * max_ch * (head_dim + 4);
 }
 
 void launch_decode_attention(const DecodeAttnArgs& a, int* err, cudaStream_t st) {
     (void)err;
     if (a.B <= 0) return;
-    const int max_ch = (std::max(a.max_len, 1) + kAttnChunk - 1) / kAttnChunk;
-    dim3 grid(max_ch, a.H, a.B);
+    DecodeAttnArgs args = a;  // chunk: one of the two sizes the scratch is sized for
+    args.chunk = (a.chunk == kAttnChunkShort) ? kAttnChunkShort : kAttnChunk;
+    const int max_ch = (std::max(args.max_len, 1) + args.chunk - 1) / args.chunk;
+    dim3 grid(max_ch, args.H, args.B);
     if (a.head_dim == 32)
-        launch_kernel(decode_attention_kernel<32>, grid, dim3(kAttnWarps * 32), 0, st, a);
+        launch_kernel(decode_attention_kernel<32>, grid, dim3(kAttnWarps * 32), 0, st, args);
     else
-        launch_kernel(decode_attention_kernel<64>, grid, dim3(kAttnWarps * 32), 0, st, a);
+        launch_kernel(decode_attention_kernel<64>, grid, dim3(kAttnWarps * 32), 0, st, args);
 }
 
 void launch_prefill_attention(const float* qkv, int D, int H, const int* offsets, const int* lens,

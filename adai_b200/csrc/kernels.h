@@ -192,11 +192,13 @@ struct DecodeAttnArgs {
     float scale = 0.f;
     float* ws = nullptr;  // split-KV partials
     int* tickets = nullptr;
+    int chunk = 256;  // cached rows per CTA: kAttnChunk or kAttnChunkShort
 };
-constexpr int kAttnChunk = 256;  // cached rows per CTA
+constexpr int kAttnChunk = 256;       // cached rows per CTA (default)
+constexpr int kAttnChunkShort = 128;  // the decode step's cross-attention
 bool attention_head_dim_supported(int head_dim);
 // split-KV partials: per (b, h, chunk) m, l, 2 pad, head_dim accumulators
-size_t decode_attn_ws_floats(int B, int H, int max_len, int head_dim);
+size_t decode_attn_ws_floats(int B, int H, int max_len, int head_dim, int chunk = kAttnChunk);
 void launch_decode_attention(const DecodeAttnArgs& a, int* err, cudaStream_t st);
 
 // Encoder self-attention on the tensor cores (prefill_tc.cu). qkv [rows, 3D] fp32 is split into
