@@ -271,6 +271,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 8) decode_attention_kernel(co
     const int len = a.len_by_slot[slot] + a.len_add;
     const int chunk = a.chunk;
     const int nch = (len + chunk - 1) / chunk;
+    // A CTA past the last chunk of its row (the grid is sized for the capacity) touches nothing:
+    // it leaves at once instead of holding a slot until the preceding kernel completes.
+    if (c >= max(nch, 1)) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int rsub = lane / LPR, l = lane % LPR;
     const int r0 = c * chunk;
