@@ -37,7 +37,8 @@ def test_reference_arm_json_line():
               "cpu_baseline", "e2e"):
         assert k in line, k
     assert line["value"] > 0 and line["unit"] == "tokens/s" and line["higher_is_better"] is True
-    assert line["metric"] == bench.METRIC
+    assert line["metric"] == "batched greedy decode tokens/s (tiny-encdec-b8-s64-t32, fp32)"
+    assert bench.metric_for(bench.WORKLOADS[bench.DEFAULT_WORKLOAD]) == bench.METRIC
     cb = line["cpu_baseline"]
     assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["value"] == line["value"]
     e2e = line["e2e"]
