@@ -529,10 +529,10 @@ void ensure_step_bufs(adai_b200_ctx* c, int rows_needed) {
     cuda_ok(cudaStreamSynchronize(c->stream), "sync");
     c->clear_graphs();
     StepBufs& s = c->sb;
+    // slots / ids and next / nonfinite_any are two allocations each (see below)
     for (void* p : {(void*)s.x, (void*)s.nrm_hi, (void*)s.nrm_lo, (void*)s.qkv, (void*)s.attn_hi,
                     (void*)s.attn_lo, (void*)s.qc, (void*)s.h_hi, (void*)s.h_lo, (void*)s.logits,
-                    (void*)s.ids, (void*)s.next, (void*)s.slots, (void*)s.nonfinite,
-                    (void*)s.nonfinite_any, (void*)s.ln_stats})
+                    (void*)s.slots, (void*)s.next, (void*)s.nonfinite, (void*)s.ln_stats})
         c->dfree(p);
     const size_t D = m.d.d_model, F = m.d.d_ff, V = m.d.vocab;
     s.rows = R;
@@ -546,11 +546,12 @@ void ensure_step_bufs(adai_b200_ctx* c, int rows_needed) {
     s.h_hi = c->dzalloc_t<float>(R * F);
     s.h_lo = c->dzalloc_t<float>(R * F);
     s.logits = c->dzalloc_t<float>(R * V);
-    s.ids = c->dzalloc_t<int>(R);
-    s.next = c->dzalloc_t<int>(R);
-    s.slots = c->dzalloc_t<int>(R);
+    // [slots R | ids R] and [next R | nonfinite_any]: one copy each way per decode step
+    s.slots = c->dzalloc_t<int>(2 * static_cast<size_t>(R));
+    s.ids = s.slots + R;
+    s.next = c->dzalloc_t<int>(R + 1);
+    s.nonfinite_any = s.next + R;
     s.nonfinite = c->dzalloc_t<int>(R);
-    s.nonfinite_any = c->dzalloc_t<int>(1);
     s.ln_stats = c->dzalloc_t<float2>(R * (D / 32));
 }
 
@@ -599,10 +600,10 @@ void free_enc_bufs(adai_b200_ctx* c) {
 
 void free_step_bufs(adai_b200_ctx* c) {
     StepBufs& s = c->sb;
+    // slots / ids and next / nonfinite_any are two allocations each (see below)
     for (void* p : {(void*)s.x, (void*)s.nrm_hi, (void*)s.nrm_lo, (void*)s.qkv, (void*)s.attn_hi,
                     (void*)s.attn_lo, (void*)s.qc, (void*)s.h_hi, (void*)s.h_lo, (void*)s.logits,
-                    (void*)s.ids, (void*)s.next, (void*)s.slots, (void*)s.nonfinite,
-                    (void*)s.nonfinite_any, (void*)s.ln_stats})
+                    (void*)s.slots, (void*)s.next, (void*)s.nonfinite, (void*)s.ln_stats})
         c->dfree(p);
     s = StepBufs{};
 }
@@ -919,11 +920,13 @@ void stage_batch(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slots, co
                                                  std::to_string(c->model->d.vocab) + ")");
     }
     ensure_step_bufs(c, B);
-    int* pin = c->pinned(2 * static_cast<size_t>(B));
+    // slots into [0, B), ids into [R, R + B) of the [slots R | ids R] block, in one copy
+    const size_t R = static_cast<size_t>(c->sb.rows);
+    int* pin = c->pinned(R + B);
     std::memcpy(pin, slots, B * sizeof(int));
-    std::memcpy(pin + B, ids, B * sizeof(int));
-    cuda_ok(cudaMemcpyAsync(c->sb.slots, pin, B * sizeof(int), cudaMemcpyHostToDevice, c->stream), "H2D slots");
-    cuda_ok(cudaMemcpyAsync(c->sb.ids, pin + B, B * sizeof(int), cudaMemcpyHostToDevice, c->stream), "H2D ids");
+    std::memcpy(pin + R, ids, B * sizeof(int));
+    cuda_ok(cudaMemcpyAsync(c->sb.slots, pin, (R + B) * sizeof(int), cudaMemcpyHostToDevice, c->stream),
+            "H2D slots and ids");
 }
 
 }  // namespace
@@ -1500,16 +1503,18 @@ int adai_b200_decode_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* 
         cudaGraphExec_t g = get_graph(c, kv, B, flags);
         cuda_ok(cudaMemsetAsync(c->sb.nonfinite_any, 0, sizeof(int), c->stream), "memset");
         cuda_ok(cudaGraphLaunch(g, c->stream), "graph launch");
-        int* pin = c->pinned(static_cast<size_t>(B) + 1);
-        cuda_ok(cudaMemcpyAsync(pin, c->sb.next, B * sizeof(int), cudaMemcpyDeviceToHost, c->stream), "D2H ids");
-        cuda_ok(cudaMemcpyAsync(pin + B, c->sb.nonfinite_any, sizeof(int), cudaMemcpyDeviceToHost, c->stream), "D2H flag");
+        // next ids and the non-finite flag: [next R | flag], one copy
+        const size_t R = static_cast<size_t>(c->sb.rows);
+        int* pin = c->pinned(R + 1);
+        cuda_ok(cudaMemcpyAsync(pin, c->sb.next, (R + 1) * sizeof(int), cudaMemcpyDeviceToHost, c->stream),
+                "D2H ids and flag");
         if (logits)
             cuda_ok(cudaMemcpyAsync(logits, c->sb.logits, static_cast<size_t>(B) * c->model->d.vocab * sizeof(float),
                                     cudaMemcpyDeviceToHost, c->stream), "D2H logits");
         c->sync(wait_timeout_seconds());
         for (int b = 0; b < B; ++b) kv->self_len[slots[b]] += 1;
         std::memcpy(next_ids, pin, B * sizeof(int));
-        if (pin[B]) fail(ADAI_B200_ERR_NONFINITE, "the model returned non-finite logits");
+        if (pin[R]) fail(ADAI_B200_ERR_NONFINITE, "the model returned non-finite logits");
     });
 }
 
