@@ -18,6 +18,7 @@ enum DeviceError : int {
     kDevTimeoutSmemEmpty = 102, // producer gave up waiting for a free stage
     kDevTimeoutAccum = 103,     // epilogue gave up waiting for the accumulator
     kDevBadShape = 110,
+    kDevAttnLength = 111,       // a cached length outside [0, max_len] or past the capacity
 };
 
 // Wait deadline for any device-side spin (nanoseconds of %globaltimer).

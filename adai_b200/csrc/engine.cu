@@ -2106,7 +2106,11 @@ int adai_b200_embedding_gather_add_pe(adai_b200_ctx* c, const float* table, cons
 // stall the device while its streams are busy), or that forbids allocation on its serving path.
 // The price is a hard size limit and one shared buffer per device: calls that overlap in time
 // on the same device (two streams, two contexts, two threads) race on it and corrupt each
-// other's results. Serialize them.
+// other's results. Serializing the host calls is not enough, because each call only queues its
+// kernel: calls on different streams must also be ordered on the device (one stream, events, or
+// a device synchronize between them). A cached length outside [0, max_len] is refused by the
+// kernel itself (the call then fails at the next synchronize with ADAI_B200_ERR_OUT_OF_RANGE) and
+// leaves the merge counters at zero.
 static constexpr size_t kStaticAttnScratchBytes = size_t(16) << 20;  // per device
 static constexpr size_t kStaticAttnTicketBytes = size_t(64) << 10;   // first part: tickets
 static constexpr int kStaticAttnMaxPairs = static_cast<int>(kStaticAttnTicketBytes / sizeof(int));
@@ -2117,22 +2121,27 @@ namespace {
 
 constexpr int kStaticMaxDevices = 64;
 std::mutex g_static_attn_mu;
-unsigned char* g_static_attn_base[kStaticMaxDevices] = {};
+// Per device, the array address whose merge counters this process has zeroed. A device reset
+// reloads the module; its array then shows up at a fresh lookup and is zeroed again if its address
+// differs (a reloaded module's array starts zeroed in any case).
+void* g_static_attn_zeroed[kStaticMaxDevices] = {};
 
-// The scratch array's address on the current device. The first call on a device looks the
-// address up and zeroes the tickets (the merge counts on them starting at zero; every launch
-// hands them back at zero). `device` must be the current device.
+// The scratch array's address on the current device, looked up on every call (the lookup is a
+// host-side table read). The first call on a device zeroes the merge counters (every launch hands
+// them back at zero) and waits for that before it returns, so a later call on any stream of the
+// device is ordered after it. `device` must be the current device.
 unsigned char* static_attn_scratch(int device, cudaStream_t st) {
     if (device < 0 || device >= kStaticMaxDevices)
         fail(ADAI_B200_ERR_INVALID_ARGUMENT, "device index out of range for the static scratch table");
+    void* p = nullptr;
+    cuda_ok(cudaGetSymbolAddress(&p, g_static_attn_scratch), "cudaGetSymbolAddress(static attention scratch)");
     std::lock_guard<std::mutex> lock(g_static_attn_mu);
-    if (g_static_attn_base[device] == nullptr) {
-        void* p = nullptr;
-        cuda_ok(cudaGetSymbolAddress(&p, g_static_attn_scratch), "cudaGetSymbolAddress(static attention scratch)");
+    if (g_static_attn_zeroed[device] != p) {
         cuda_ok(cudaMemsetAsync(p, 0, kStaticAttnTicketBytes, st), "zero static attention tickets");
-        g_static_attn_base[device] = static_cast<unsigned char*>(p);
+        cuda_ok(cudaStreamSynchronize(st), "wait for the static attention tickets to be zeroed");
+        g_static_attn_zeroed[device] = p;
     }
-    return g_static_attn_base[device];
+    return static_cast<unsigned char*>(p);
 }
 
 }  // namespace

@@ -269,6 +269,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 8) decode_attention_kernel(co
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int slot = a.slots ? a.slots[b] : b;
     const int len = a.len_by_slot[slot] + a.len_add;
+    // A length the grid and the scratch were not sized for (or past the cache) is refused before
+    // any load, append or merge ticket: every CTA of the pair sees the same length and leaves, so
+    // the tickets stay at zero and nothing outside the cache is written.
+    if (len < a.len_add || len > a.max_len || len > a.cap) {
+        if (c == 0 && threadIdx.x == 0) record_error(a.err, kDevAttnLength);
+        return;
+    }
     const int chunk = a.chunk;
     const int nch = (len + chunk - 1) / chunk;
     // A CTA past the last chunk of its row (the grid is sized for the capacity) touches nothing:
@@ -641,10 +648,10 @@ size_t decode_attn_ws_floats(int B, int H, int max_len, int head_dim, int chunk)
 }
 
 void launch_decode_attention(const DecodeAttnArgs& a, int* err, cudaStream_t st) {
-    (void)err;
     if (a.B <= 0) return;
     DecodeAttnArgs args = a;  // chunk: one of the two sizes the scratch is sized for
     args.chunk = (a.chunk == kAttnChunkShort) ? kAttnChunkShort : kAttnChunk;
+    args.err = err;
     const int max_ch = (std::max(args.max_len, 1) + args.chunk - 1) / args.chunk;
     dim3 grid(max_ch, args.H, args.B);
     if (a.head_dim == 32)

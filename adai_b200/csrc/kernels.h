@@ -193,6 +193,7 @@ struct DecodeAttnArgs {
     float* ws = nullptr;  // split-KV partials
     int* tickets = nullptr;
     int chunk = 256;  // cached rows per CTA: kAttnChunk or kAttnChunkShort
+    int* err = nullptr;  // device error word: a length outside [0, max_len] records kDevAttnLength
 };
 constexpr int kAttnChunk = 256;       // cached rows per CTA (default)
 constexpr int kAttnChunkShort = 128;  // the decode step's cross-attention

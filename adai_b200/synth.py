@@ -4,9 +4,20 @@ The tensor order and shapes are the model-upload order of the C-ABI (adai_b200_m
 include/adai_b200.h), which is also the order the reference's public setters are called in
 (MultiHeadAttention::set_W*, CrossAttention::set_W*, FeedForward::set_W1/b1/W2/b2,
 LayerNorm::set_gamma/set_beta, TokenEmbedding::set_embeddings, LanguageModelHead::set_W_output /
-set_bias). Matrices are Xavier-uniform U(+-sqrt(6/(fan_in+fan_out))) drawn from one numpy PCG64
-stream in that order; LayerNorm gamma = 1, beta = 0 and biases = 0 unless `affine` asks for random
-ones (parity tests use random ones so every bias and affine path is exercised).
+set_bias). Two weight schemes, each drawn from one numpy PCG64 stream in that order:
+
+* "xavier": every matrix Xavier-uniform U(+-sqrt(6/(fan_in+fan_out))), the embedding tables
+  included (the benchmark workloads' weights).
+* "reference": the distributions of the reference's own constructors, which make a sequence's
+  greedy tokens depend on its source: token embeddings N(0, 1) (TokenEmbedding::kInitStd,
+  src/TokenEmbedding.cpp:15-24), attention projections N(0, 2/d_model)
+  (src/MultiHeadAttention.cpp:66-72, src/CrossAttention.cpp:84-90), W1 N(0, 2/d_model) and
+  W2 N(0, 2/d_ff) (src/FeedForward.cpp:28-50), the head N(0, 2/(d_model + vocab))
+  (src/LanguageModelHead.cpp:30-32). Under "xavier" the embedding rows are far smaller than the
+  positional rows, so every source gives nearly the same greedy stream.
+
+LayerNorm gamma = 1, beta = 0 and biases = 0 unless `affine` asks for random ones (parity tests
+use random ones so every bias and affine path is exercised).
 """
 from __future__ import annotations
 
@@ -43,12 +54,29 @@ def tensor_specs(cfg: ModelConfig) -> list[tuple[str, tuple[int, ...]]]:
     return out
 
 
-def make_weights(cfg: ModelConfig, seed: int = 0, affine: bool = False) -> list[np.ndarray]:
-    """Weights in upload order, C-contiguous float32."""
+def _reference_std(cfg: ModelConfig, name: str) -> float:
+    D, F, V = cfg.d_model, cfg.d_ff, cfg.vocab
+    if name.endswith("embed"):
+        return 1.0
+    if name == "head.w":
+        return float(np.sqrt(2.0 / (D + V)))
+    if name.endswith("ffn.w2"):
+        return float(np.sqrt(2.0 / F))
+    return float(np.sqrt(2.0 / D))
+
+
+def make_weights(cfg: ModelConfig, seed: int = 0, affine: bool = False,
+                 scheme: str = "xavier") -> list[np.ndarray]:
+    """Weights in upload order, C-contiguous float32 (scheme "xavier" or "reference")."""
+    if scheme not in ("xavier", "reference"):
+        raise ValueError(f"unknown weight scheme {scheme!r}")
     rng = np.random.default_rng(seed)
     out = []
     for name, shape in tensor_specs(cfg):
-        if len(shape) == 2:
+        if len(shape) == 2 and scheme == "reference":
+            w = rng.standard_normal(shape, dtype=np.float32)
+            w *= np.float32(_reference_std(cfg, name))
+        elif len(shape) == 2:
             bound = np.float32(np.sqrt(6.0 / (shape[0] + shape[1])))
             w = rng.random(shape, dtype=np.float32)
             w *= np.float32(2.0) * bound

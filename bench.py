@@ -130,23 +130,45 @@ def dist_env():
             int(os.environ.get("LOCAL_RANK", 0)))
 
 
-def cpu_reference_tokens_per_s(wl, weights, src, steps, warmup=1):
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_reference_tokens_per_s(wl, weights, src, steps, warmup=1, single_steps=0):
     """The reference CPU path (oracle/_ref) on the host cores, or the oracle port if the
-    reference build is absent: greedy decode of one sequence, seconds per token."""
+    reference build is absent: greedy decode of one sequence after one encoder pass. Returns
+    (tokens/s on every host thread, tokens/s on one thread or None, kind, cores, details): the
+    first `warmup` steps are untimed, the next `steps` run on all threads, the last
+    `single_steps` on one thread (continuing the same sequence)."""
     from oracle.pyoracle import Port, Ref
     cores = os.cpu_count() or 1
+    details = {"cpu_model": cpu_model()}
     if Ref.available():
-        m = Ref().model(wl.model, weights)
-        ids, st, enc_s = m.generate_timed(src, warmup + steps)
+        ref = Ref()
+        m = ref.model(wl.model, weights)
+        threads = [0] * (warmup + steps) + [1] * single_steps
+        ids, st, enc_s = m.generate_timed_threads(src, threads)
         kind = "reference"
-        t = float(np.sum(st[warmup:]))
+        t = float(np.sum(st[warmup:warmup + steps]))
+        t1 = float(np.sum(st[warmup + steps:])) if single_steps else 0.0
+        details.update(matmul_kernel=ref.matmul_kernel(), encoder_s=enc_s,
+                       omp_threads=int(os.environ.get("OMP_NUM_THREADS", cores)))
     else:
         m = Port().model(wl.model, weights)
         t0 = time.perf_counter()
         m.generate(src, warmup + steps)
         t = (time.perf_counter() - t0) * steps / (warmup + steps)
+        t1 = 0.0
         kind = "port"
-    return steps / t, kind, cores
+    one = single_steps / t1 if t1 > 0 else None
+    return steps / t, one, kind, cores, details
 
 
 def run_reference_arm(args, wl, rank):
@@ -155,7 +177,8 @@ def run_reference_arm(args, wl, rank):
     weights = make_weights(wl.model, seed=0)
     src = make_sources(wl.model, wl.batch, wl.src_len, seed=0)[0]
     steps = min(args.steps, args.reference_max_steps)
-    tps, kind, cores = cpu_reference_tokens_per_s(wl, weights, src, steps, warmup=args.warmup)
+    tps, _, kind, cores, details = cpu_reference_tokens_per_s(wl, weights, src, steps,
+                                                              warmup=args.warmup)
     sample = (f"1 sequence (source length {len(src)}) of the {wl.name} workload, sequences "
               f"processed one after another as the reference's BatchedInferenceEngine does; "
               f"{args.warmup} untimed + {steps} timed greedy tokens, encoder excluded; OpenMP "
@@ -167,7 +190,7 @@ def run_reference_arm(args, wl, rank):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": wl.name, "sequences_timed": 1, "src_len": int(len(src))},
         "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": kind,
-                         "sample": sample},
+                         "sample": sample, **details},
         "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -310,7 +333,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-baseline-steps", type=int, default=12)
+    ap.add_argument("--cpu-baseline-steps", type=int, default=48)
+    ap.add_argument("--cpu-baseline-single-steps", type=int, default=6)
     ap.add_argument("--reference-max-steps", type=int, default=48)
     ap.add_argument("--profile-steps", type=int, default=3)
     ap.add_argument("--src-len", default="", help="LO,HI: override the workload's source lengths")
@@ -358,18 +382,31 @@ def main():
             dist.barrier()
 
     from adai_b200 import Context
-    from adai_b200.parallel import max_over_ranks, shard_ranges
+    from adai_b200.parallel import balanced_shards, max_over_ranks
     reduce_max = max_over_ranks
+
+    def gather(obj):
+        if dist is None:
+            return [obj]
+        out = [None] * world
+        dist.all_gather_object(out, obj)
+        return out
 
     cfg = wl.model
     B, K, W = wl.batch, args.steps, args.warmup
     weights = make_weights(cfg, seed=0)
-    # the global batch (B sequences per GPU) and this rank's contiguous shard of it
-    lo, hi = shard_ranges(B * world, world)[rank]
-    srcs = make_sources(cfg, B * world, wl.src_len, seed=0)[lo:hi]
+    # The global batch (B sequences per GPU) split so that every rank gets B sequences with
+    # nearly the same total source length (the cross-attention bytes per step).
+    all_srcs = make_sources(cfg, B * world, wl.src_len, seed=0)
+    mine = balanced_shards([len(s) for s in all_srcs], world)[rank]
+    srcs = [all_srcs[i] for i in mine]
+    # The timed window sits in the middle of the workload's generation: self-attention costs
+    # grow linearly with the position, so K steps centred on the workload's mean position cost
+    # what the workload's steps cost on average (K = the workload's length times all of them).
+    start = max(0, (wl.steps - K) // 2)
     ctx = Context(local)
     ctx.upload(cfg, weights)
-    self_cap = max(W, K) + args.profile_steps + 8
+    self_cap = max(W, start + K) + args.profile_steps + 8
     kv = ctx.kv_arena(B, self_cap, max(len(s) for s in srcs) if wl.src_len[0] == wl.src_len[1]
                       else wl.src_len[1])
     slots = np.arange(B, dtype=np.int32)
@@ -382,29 +419,35 @@ def main():
         for s in slots:
             kv.clear_self(int(s))
             if sampling:
-                kv.set_sampling(int(s), Sampling.make(**sampling, seed=1000 + lo + int(s)))
+                kv.set_sampling(int(s), Sampling.make(**sampling, seed=1000 + mine[int(s)]))
 
     barrier()
     t0 = time.perf_counter()
     kv.encode(slots, srcs)
     prefill_s = reduce_max(time.perf_counter() - t0)
 
+    def advance_to(pos):
+        """Untimed greedy steps from position 0 to `pos`; returns the ids to feed next."""
+        restart()
+        return kv.generate(slots, bos, pos)[:, -1].copy() if pos > 0 else bos.copy()
+
     # ---- device-resident decode: W warm-up steps, restart, K timed steps ----
     restart()
     kv.generate(slots, bos, W)
-    restart()
+    first = advance_to(start)
     barrier()
     with ClockSampler(local) as clk:
-        ids_dev = kv.generate(slots, bos, K)
+        ids_dev = kv.generate(slots, first, K)
         ms, kernels_per_step = ctx.last_timing()
     ms_max = reduce_max(ms)
     value = world * B * K / (ms_max / 1000.0)
+    ranks = gather({"rank": rank, "src_tokens": int(sum(len(s) for s in srcs)),
+                    "ms_per_step": ms / K})
 
     # ---- end to end through the per-step C-ABI call with host buffers ----
     restart()
     kv.decode_step(slots, bos)          # captures the per-step graph outside the timed region
-    restart()
-    feed = bos.copy()
+    feed = advance_to(start)
     barrier()
     t0 = time.perf_counter()
     for t in range(K):
@@ -413,12 +456,9 @@ def main():
     e2e_match = bool(np.array_equal(feed, ids_dev[:, K - 1]))
     e2e_value = world * B * K / e2e_s
 
-    # ---- per-kernel device times of a profiled step at mid-generation (roofline) ----
-    restart()
-    if K >= 2:
-        kv.generate(slots, bos, K // 2)
+    # ---- per-kernel device times of a profiled step in the middle of the window (roofline) ----
+    feed = advance_to(start + K // 2)
     prof = None
-    feed = ids_dev[:, K // 2 - 1] if K >= 2 else bos
     for _ in range(args.profile_steps):
         p = kv.profile_step(slots, feed)
         prof = p if prof is None else {k: {f: prof[k][f] + p[k][f] for f in p[k]} for k in p}
@@ -460,8 +500,11 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded Xavier-uniform weights, uniform source ids)",
             "config": {"workload": wl.name, "batch_per_gpu": B, "global_batch": B * world,
-                       "src_len": list(wl.src_len), "decode_positions": [0, K - 1],
-                       "parallelism": f"batch-sharded x{world}, no collectives",
+                       "src_len": list(wl.src_len), "decode_positions": [start, start + K - 1],
+                       "parallelism": f"batch-sharded x{world} (shards balanced by source "
+                                      f"length), no collectives",
+                       "ranks": ranks,
+                       "slowest_rank": max(ranks, key=lambda r: r["ms_per_step"]),
                        "l2": "per-step working set ~9 GB >> 126 MB L2 (no flush needed)",
                        "prefill_s": prefill_s,
                        "token_selection": ({"sampling": sampling} if sampling
@@ -474,13 +517,22 @@ def main():
             "clocks": clk.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
-            tps, kind, cores = cpu_reference_tokens_per_s(wl, weights, srcs[0],
-                                                          args.cpu_baseline_steps)
+            # the sequence whose source length is nearest the workload's mean
+            mean_len = float(np.mean([len(x) for x in srcs]))
+            src = min(srcs, key=lambda x: abs(len(x) - mean_len))
+            n1 = args.cpu_baseline_single_steps
+            tps, tps1, kind, cores, details = cpu_reference_tokens_per_s(
+                wl, weights, src, args.cpu_baseline_steps, single_steps=n1)
             line["cpu_baseline"] = {
                 "value": tps, "unit": "tokens/s", "cores": cores, "kind": kind,
-                "sample": (f"1 sequence (source length {len(srcs[0])}), {args.cpu_baseline_steps}"
-                           f" greedy tokens after 1 warm-up, encoder excluded; reference CPU "
-                           f"path (OpenMP, {cores} threads), sequences one after another")}
+                "value_1_thread": tps1,
+                "sample": (f"1 sequence of the workload (source length {len(src)}, the nearest "
+                           f"to the mean {mean_len:.0f}), sequences processed one after another "
+                           f"as the reference's BatchedInferenceEngine does: encoder once, 1 "
+                           f"untimed + {args.cpu_baseline_steps} timed greedy tokens on {cores} "
+                           f"OpenMP threads (positions 1-{args.cpu_baseline_steps}), then "
+                           f"{n1} more on one thread (value_1_thread); encoder excluded"),
+                **details}
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

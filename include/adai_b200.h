@@ -269,10 +269,15 @@ ADAI_B200_API int adai_b200_decode_attention(adai_b200_ctx* ctx, int B, int H, i
  * Limits: B * H <= 16384, and the split partials, B * H * ceil((max_len + appended) / 256) *
  * (head_dim + 4) floats, must fit in 16 MiB - 64 KiB (B = 256, H = 16, head_dim = 64 fits while
  * max_len + appended <= 3840); larger calls return ADAI_B200_ERR_OUT_OF_RANGE and launch nothing.
- * The first call on each device does a one-time setup (looks up the array's address and zeroes
- * its merge counters on ctx's stream); make that first call before any stream capture.
+ * The first call on each device does a one-time setup (zeroes the array's merge counters on
+ * ctx's stream and waits for that); make that first call before any stream capture.
  * The array is shared by every caller on a device: calls that overlap in time on one device race
- * and corrupt each other's results, so serialize them. */
+ * and corrupt each other's results. Serializing the host calls is not enough (each call only
+ * queues a kernel): calls on different streams or contexts of one device must also be ordered on
+ * the device (one stream, events, or a synchronize between them).
+ * A lens[b] outside [0, max_len] is refused by the kernel: that pair computes nothing, and the
+ * next adai_b200_ctx_synchronize returns ADAI_B200_ERR_OUT_OF_RANGE (also for
+ * adai_b200_decode_attention). */
 ADAI_B200_API int adai_b200_decode_attention_static(adai_b200_ctx* ctx, int B, int H, int head_dim,
                                                     int capacity, const float* q,
                                                     const float* k_new, const float* v_new,

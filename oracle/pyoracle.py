@@ -240,10 +240,16 @@ class Ref(_Base):
                                            np.ctypeslib.ndpointer(np.float64,
                                                                   flags="C_CONTIGUOUS"),
                                            C.POINTER(C.c_double)]
+        lib.ref_generate_timed_threads.argtypes = [
+            C.c_void_p, _i32p, C.c_int, C.c_int, C.c_int, _i32p, _i32p,
+            np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS"), C.POINTER(C.c_double)]
         lib.ref_encode.argtypes = [C.c_void_p, _i32p, C.c_int, _f32p]
         lib.ref_generate.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                      _i32p, C.c_void_p, C.POINTER(C.c_double),
                                      C.POINTER(C.c_double)]
+        _f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
+        lib.ref_generate_hidden.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, C.c_int,
+                                            C.c_void_p, _i32p, _f32p, _f64p, _f32p]
         lib.ref_sample_generate.argtypes = [_f32p, C.c_int, C.c_int, _f32p, _i32p, C.c_uint,
                                             C.c_void_p, C.c_int, _i32p, C.POINTER(C.c_int)]
         lib.ref_model_save.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_int, C.c_int]
@@ -328,6 +334,20 @@ class _RefModel:
         """The reference's own checkpoint files (EncoderDecoderModel::save_model layout)."""
         self.ref._check(self.ref.lib.ref_model_save(self.h, os.fsencode(prefix), bos, eos, pad))
 
+    def generate_hidden(self, src, steps, bos=2, forced=None):
+        """Greedy decode returning (ids, hidden [steps, D], float64 logit-row sums, top-2 logits
+        [steps, 2]); hidden is the decoder output row the head multiplies."""
+        src = np.ascontiguousarray(src, np.int32)
+        ids = np.empty(steps, np.int32)
+        hid = np.empty((steps, self.cfg.d_model), np.float32)
+        sums = np.empty(steps, np.float64)
+        top2 = np.empty((steps, 2), np.float32)
+        fz = np.ascontiguousarray(forced, np.int32) if forced is not None else None
+        self.ref._check(self.ref.lib.ref_generate_hidden(
+            self.h, src, src.size, bos, steps, fz.ctypes.data if fz is not None else None, ids,
+            hid, sums, top2))
+        return ids, hid, sums, top2
+
     def generate_timed(self, src, steps, bos=2):
         """Greedy decode; returns (ids, per-step wall seconds, encoder seconds)."""
         src = np.ascontiguousarray(src, np.int32)
@@ -336,6 +356,18 @@ class _RefModel:
         te = C.c_double()
         self.ref._check(self.ref.lib.ref_generate_timed(self.h, src, src.size, bos, steps, ids,
                                                         st, C.byref(te)))
+        return ids, st, te.value
+
+    def generate_timed_threads(self, src, threads, bos=2):
+        """Greedy decode of len(threads) steps, step s on threads[s] OpenMP threads (0: the
+        default team); returns (ids, per-step wall seconds, encoder seconds)."""
+        src = np.ascontiguousarray(src, np.int32)
+        th = np.ascontiguousarray(threads, np.int32)
+        ids = np.empty(th.size, np.int32)
+        st = np.empty(th.size, np.float64)
+        te = C.c_double()
+        self.ref._check(self.ref.lib.ref_generate_timed_threads(
+            self.h, src, src.size, bos, th.size, th, ids, st, C.byref(te)))
         return ids, st, te.value
 
     def generate(self, src, steps, bos=2, forced=None, want_logits=False, timings=None):

@@ -21,10 +21,13 @@
 #include <algorithm>
 #include <chrono>
 #include <cstring>
+#include <functional>
 #include <memory>
 #include <stdexcept>
 #include <string>
 #include <vector>
+
+#include <omp.h>
 
 #include "Activation.hpp"
 #include "BinaryIO.hpp"
@@ -199,6 +202,44 @@ int ref_generate(void* h, const int* src, int S, int bos, int steps, const int* 
     });
 }
 
+// ref_generate that also returns, per step, the decoder's output row (after its final LayerNorm,
+// src/Decoder.cpp:284), which LanguageModelHead::forward turns into the logits as hidden * W_output
+// + bias (src/LanguageModelHead.cpp:49-69). hidden: [steps, D]. logit_sum / top2: per step, the
+// float64 sum of the logits row and its two largest values (either may be null). These are what the
+// long-run fixtures keep: the logits follow from the hidden rows with the same in-order product.
+int ref_generate_hidden(void* h, const int* src, int S, int bos, int steps, const int* forced,
+                        int* out_ids, float* hidden, double* logit_sum, float* top2) {
+    return guarded([&] {
+        auto* m = static_cast<RefModel*>(h);
+        std::vector<int> v(src, src + S);
+        Matrix mask(S, S);
+        for (auto& row : mask.data) std::fill(row.begin(), row.end(), 1.0f);
+        Matrix enc = m->enc->encode_with_mask(v, mask);
+        DecoderKVCache cache(m->L);
+        int tok = bos;
+        for (int s = 0; s < steps; ++s) {
+            Matrix x = m->dec->forward_with_cache({tok}, cache, &enc, true);
+            Matrix lg = m->head->forward(x);
+            const std::vector<float>& row = lg.data[lg.rows - 1];
+            out_ids[s] = first_max(row);
+            if (hidden) std::memcpy(hidden + static_cast<size_t>(s) * m->D, x.data[x.rows - 1].data(),
+                                    sizeof(float) * m->D);
+            if (logit_sum) {
+                double acc = 0.0;
+                for (float f : row) acc += static_cast<double>(f);
+                logit_sum[s] = acc;
+            }
+            if (top2) {
+                std::vector<float> c(row);
+                std::partial_sort(c.begin(), c.begin() + 2, c.end(), std::greater<float>());
+                top2[2 * s] = c[0];
+                top2[2 * s + 1] = c[1];
+            }
+            tok = forced ? forced[s] : out_ids[s];
+        }
+    });
+}
+
 // The same greedy loop with the wall time of every decode step (decoder + head + argmax) in
 // step_s[s]; the encoder time in *enc_s. Used to time the reference CPU path per token.
 int ref_generate_timed(void* h, const int* src, int S, int bos, int steps, int* out_ids,
@@ -223,6 +264,38 @@ int ref_generate_timed(void* h, const int* src, int S, int bos, int steps, int* 
             tok = out_ids[s];
         }
     });
+}
+
+// ref_generate_timed with a host thread count per step: before step s the OpenMP team size is set
+// to threads[s] (0: unchanged), so one run gives both the all-core and the one-thread rate of the
+// reference's decode after a single encoder pass (run with the default team). The team size is
+// restored afterwards.
+int ref_generate_timed_threads(void* h, const int* src, int S, int bos, int steps,
+                               const int* threads, int* out_ids, double* step_s, double* enc_s) {
+    const int saved = omp_get_max_threads();
+    const int rc = guarded([&] {
+        auto* m = static_cast<RefModel*>(h);
+        using clk = std::chrono::steady_clock;
+        auto t0 = clk::now();
+        std::vector<int> v(src, src + S);
+        Matrix mask(S, S);
+        for (auto& row : mask.data) std::fill(row.begin(), row.end(), 1.0f);
+        Matrix enc = m->enc->encode_with_mask(v, mask);
+        if (enc_s) *enc_s = std::chrono::duration<double>(clk::now() - t0).count();
+        DecoderKVCache cache(m->L);
+        int tok = bos;
+        for (int s = 0; s < steps; ++s) {
+            if (threads && threads[s] > 0) omp_set_num_threads(threads[s]);
+            auto a = clk::now();
+            Matrix x = m->dec->forward_with_cache({tok}, cache, &enc, true);
+            Matrix lg = m->head->forward(x);
+            out_ids[s] = first_max(lg.data[lg.rows - 1]);
+            step_s[s] = std::chrono::duration<double>(clk::now() - a).count();
+            tok = out_ids[s];
+        }
+    });
+    omp_set_num_threads(saved);
+    return rc;
 }
 
 // One decoder step over a caller-supplied encoder output, returning the final-LN hidden row and

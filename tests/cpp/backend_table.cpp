@@ -1,5 +1,6 @@
 // Calls the decode-path functions of the reference backend table through their reference C++
-// signatures (adai::gpu::matrix_*_gpu, include/adai_b200_backend.hpp) on a bound context, and
+// signatures (adai::gpu::matrix_*_gpu: the reference's src/gpu/MatrixGPU.hpp when built with
+// ADAI_REFERENCE_HEADERS, else include/adai_b200_backend.hpp) on a bound context, and
 // checks each against a host computation. Prints "all ok" and exits 0 when every check passes.
 #include <cuda_runtime.h>
 
@@ -10,7 +11,13 @@
 #include <vector>
 
 #include "adai_b200.h"
+#ifdef ADAI_REFERENCE_HEADERS
+// The reference's own declarations (src/gpu/MatrixGPU.hpp, built with ADAI_ENABLE_GPU): the
+// program then proves that untouched callers compile against them and link to libadai_b200.so.
+#include "gpu/MatrixGPU.hpp"
+#else
 #include "adai_b200_backend.hpp"
+#endif
 
 static int failures = 0;
 static void expect(bool ok, const char* what) {

@@ -153,3 +153,38 @@ def test_batch_generator_sampled_requests(driver, tmp_path, port):
     assert checked >= 0.8 * total, (checked, total)
     kv.close()
     ctx.close()
+
+
+@pytest.mark.gpu
+def test_batched_inference_engine_submit_matches_oracle(driver, tmp_path, port):
+    """adai_b200::BatchedInferenceEngine (include/adai_b200_engine.hpp), the reference's
+    BatchedInferenceEngine::submit -> std::future<std::string> contract
+    (src/BatchedInferenceEngine.hpp:242-272): ten greedy requests submitted from three threads at
+    once, collected into batches of at most four and decoded on 3 slots; each future's text is the
+    request's greedy ids without special tokens (TextGenerator::generate_text's decode with
+    skip_special_tokens), checked against the oracle. A request with decoder seed text fails alone,
+    and a submit after shutdown() is refused."""
+    w = make_weights(TINY, 17, affine=True, scheme="reference")
+    srcs = make_sources(TINY, 9, (4, 48), 17)
+    lens = [12, 3, 20, 7, 1, 16, 9, 5, 11]
+    reqs = list(zip(lens, srcs))
+    reqs.insert(4, (6, [-1]))   # submitted with decoder seed text: refused by the engine
+    path = str(tmp_path / "req.bin")
+    _write_requests(path, TINY, w, 3, reqs)
+    out = subprocess.run([driver, path, "engine"], check=True, capture_output=True, text=True,
+                         timeout=300).stdout.splitlines()
+    assert len(out) == len(reqs) + 1, out
+    model = port.model(TINY, w)
+    texts = []
+    for i, (max_len, src) in enumerate(reqs):
+        head, rest = out[i].split(":", 1)
+        assert int(head) == i
+        if i == 4:
+            assert rest.startswith(" error:") and "decoder seed text" in rest, out[i]
+            continue
+        want = " ".join(str(t) for t in _greedy(model, src, max_len) if t >= 4)
+        assert rest[1:] == want, (i, rest, want)
+        texts.append(want)
+    assert len(set(texts)) > len(texts) // 2     # the requests do not all decode alike
+    assert out[-1].endswith("refused_after_shutdown 1"), out[-1]
+    assert "requests 10 " in out[-1], out[-1]

@@ -168,6 +168,18 @@ def test_reference_signatures_link_and_run(tmp_path):
     assert "all ok" in r.stdout, r.stdout
 
 
+def test_program_built_against_the_reference_header_runs():
+    # oracle/_ref/backend_table_refhdr: the same program compiled against the reference's own
+    # src/gpu/MatrixGPU.hpp (oracle/Makefile, target `boundary`, built where the reference sources
+    # are; it travels with the built library). Its calls resolve to libadai_b200.so.
+    exe = os.path.join(ROOT, "oracle", "_ref", "backend_table_refhdr")
+    if not os.path.exists(exe):
+        pytest.skip("built only where the reference sources are (make -C oracle boundary)")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "all ok" in r.stdout, r.stdout
+
+
 def test_softmax_known_answers(ctx, torch_cuda):
     # tests/matrixgpu_td003_test.cpp:234-249: [0, 0] -> [0.5, 0.5]; [0, ln 3] -> [0.25, 0.75]
     torch = torch_cuda

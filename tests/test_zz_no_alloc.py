@@ -1,7 +1,9 @@
 """adai_b200_decode_attention_static, the decode-attention entry point that allocates nothing (its
 split-KV scratch is a fixed per-device array in the library's device image), against the
 allocating adai_b200_decode_attention on the same inputs, several calls in a row (each call
-reuses the merge counters the previous one handed back), and its size limit.
+reuses the merge counters the previous one handed back), against the oracle's per-head attention
+directly, its size limit, and a call whose cached length exceeds max_len (refused by the kernel,
+after which the next call still matches).
 
 Tolerance: |static - allocating| <= 1e-5 + 1e-4 |allocating| elementwise, the decode-path bound;
 the appended cache rows must be identical.
@@ -53,6 +55,48 @@ def test_static_scratch_matches_allocating_entry_point(ctx, torch_cuda, calls):
         torch.cuda.synchronize()
         assert tol_ok(got.cpu().numpy(), want.cpu().numpy()), (dh, append, seed)
         assert torch.equal(kc_a, kc_b) and torch.equal(vc_a, vc_b)
+
+
+def test_static_scratch_matches_oracle(ctx, torch_cuda, port):
+    # The reference's per-head cached attention (src/MultiHeadAttention.cpp:336-367), restated by
+    # the oracle, on each sequence's appended cache.
+    torch = torch_cuda
+    B, H, dh, cap = 4, 4, 64, 700
+    lens = [0, 255, 256, 600]
+    kc, vc, q, kn, vn, dl = _inputs(torch, 31, B, H, dh, cap, lens, True)
+    torch.cuda.synchronize()
+    got, kc_b, vc_b = _run(ctx.decode_attention_static, torch, B, H, dh, cap, kc, vc, q, kn, vn,
+                           dl, max(lens))
+    ctx.synchronize()
+    got = got.cpu().numpy()
+    kc_h, vc_h, q_h = kc_b.cpu().numpy(), vc_b.cpu().numpy(), q.cpu().numpy()
+    for b in range(B):
+        t = lens[b] + 1
+        K = kc_h[b, :, :t, :].transpose(1, 0, 2).reshape(t, H * dh)
+        V = vc_h[b, :, :t, :].transpose(1, 0, 2).reshape(t, H * dh)
+        assert tol_ok(got[b], port.attention_single(q_h[b], K, V, H)), b
+
+
+def test_static_scratch_refuses_a_length_past_max_len(ctx, torch_cuda):
+    # lens[2] = 900 > max_len = 600: the kernel refuses that pair before any load, append or merge
+    # counter and the synchronize reports it; the counters stay at zero, so the next call on the
+    # shared array matches the allocating entry point.
+    torch = torch_cuda
+    B, H, dh, cap = 4, 4, 64, 1024
+    bad = [10, 300, 900, 600]
+    kc, vc, q, kn, vn, dl = _inputs(torch, 41, B, H, dh, cap, bad, True)
+    torch.cuda.synchronize()
+    with pytest.raises(IndexError, match="code 111"):
+        _run(ctx.decode_attention_static, torch, B, H, dh, cap, kc, vc, q, kn, vn, dl, 600)
+        ctx.synchronize()
+    good = [10, 300, 599, 600]
+    kc, vc, q, kn, vn, dl = _inputs(torch, 42, B, H, dh, cap, good, True)
+    torch.cuda.synchronize()
+    want, _, _ = _run(ctx.decode_attention, torch, B, H, dh, cap, kc, vc, q, kn, vn, dl, 600)
+    got, _, _ = _run(ctx.decode_attention_static, torch, B, H, dh, cap, kc, vc, q, kn, vn, dl, 600)
+    ctx.synchronize()
+    torch.cuda.synchronize()
+    assert tol_ok(got.cpu().numpy(), want.cpu().numpy())
 
 
 def test_static_scratch_rejects_oversized_calls(ctx, torch_cuda):
