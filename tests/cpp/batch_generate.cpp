@@ -82,7 +82,8 @@ static int run_engine(adai_b200::KVArena& kv, const std::vector<adai_b200::Reque
     for (auto& x : th) x.join();
     for (size_t i = 0; i < futs.size(); ++i) {
         try {
-            std::cout << i << ": " << futs[i].get() << "\n";
+            const std::string text = futs[i].get();
+            std::cout << i << ": " << text << "\n";
         } catch (const std::exception& e) {
             std::cout << i << ": error: " << e.what() << "\n";
         }
