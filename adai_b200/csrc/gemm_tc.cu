@@ -16,7 +16,9 @@
 //
 // One CTA computes one 128 x BN output tile over one K-slice:
 //   warp 0    TMA producer: 4 boxes per stage (A_hi, A_lo 128x32; W_hi, W_lo BNx32), 128B swizzle
-//   warp 1    TMEM allocator + single-thread tcgen05.mma issuer (3 MMAs per K=8 step)
+//   warp 1    TMEM allocator + tcgen05.mma issuer of A_hi*W_hi
+//   warps 6-7 tcgen05.mma issuers of the correction terms (one warp for both at BN = 128), each
+//             into its own TMEM accumulator
 //   warps 2-5 promote finished TMEM chunks into fp32 registers (one output row per thread)
 // Split-K: the S K-slices of a tile are the S CTAs of one thread-block cluster. Each CTA stages
 // its partial tile in its own shared memory and ships the rows it does not own to their owners
@@ -44,8 +46,29 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 32;  // fp32 elements per 128-byte swizzled row
-constexpr int kThreads = 192;
-constexpr int kWarps = kThreads / 32;
+
+// The three MMAs of a 3xTF32 k-step are issued by up to three threads of different warps, each
+// into its own TMEM accumulator: a single thread issuing tcgen05.mma back to back, with the
+// barrier wait, fence and commit of every K block, is limited by its own issue rate (measured on
+// B200: about 35 ns per MMA and 0.3 us per K block of synchronisation), while a second issuing
+// warp nearly doubles the tensor core's rate for N <= 64.
+// Accumulators: 0 = A_hi*B_hi, 1 = A_lo*B_hi (and A_hi*B_lo when there are two), 2 = A_hi*B_lo.
+// Two TMEM buffers of kNAcc x BN columns must fit the 512 columns of an SM.
+template <int BN>
+struct GemmShape {
+    static constexpr int kNAcc = (6 * BN <= 512) ? 3 : 2;
+    // warp 0 TMA producer, warp 1 issuer 0, warps 2-5 epilogue, warps 6.. further issuers
+    static constexpr int kWarps = 6 + kNAcc - 1;
+    static constexpr int kThreads = 32 * kWarps;
+};
+int threads_for(int bn) {
+    switch (bn) {
+        case 32: return GemmShape<32>::kThreads;
+        case 64: return GemmShape<64>::kThreads;
+        default: return GemmShape<128>::kThreads;
+    }
+}
+int nacc_for(int bn) { return (6 * bn <= 512) ? 3 : 2; }
 constexpr int kATileBytes = kBM * kBK * 4;  // 16 KB
 constexpr size_t kSmemLimit = 227 * 1024;
 constexpr size_t kSmemReserve = 1024 /*alignment slack*/ + 256 /*barriers*/ + 1024 /*row mean, rstd*/;
@@ -260,7 +283,10 @@ __device__ __forceinline__ void row_group_stats(float4 v, float2* dst, int lane)
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_constant__ GemmKParams p) {
+__global__ void __launch_bounds__(GemmShape<BN>::kThreads, 1) gemm_3xtf32_kernel(const __grid_constant__ GemmKParams p) {
+    constexpr int kThreads = GemmShape<BN>::kThreads;
+    constexpr int kWarps = GemmShape<BN>::kWarps;
+    constexpr int kNAcc = GemmShape<BN>::kNAcc;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -287,8 +313,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
     uint64_t* tfull_bar = empty_bar + stages;  // [2] chunk accumulated in TMEM buffer b
     uint64_t* tempty_bar = tfull_bar + 2;      // [2] TMEM buffer b drained by the epilogue
     uint64_t* recv_bar = tempty_bar + 2;       // peers' partials have landed in `recv`
-    uint64_t* done_bar = recv_bar + 1;         // every MMA this CTA issued has completed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+    uint64_t* done_bar = recv_bar + 1;         // [3] every MMA issuer i issued has completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 3);
     int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
     // LayerNorm mean / rstd of the tile's rows (kEpiLnFold), after the 256 bytes of barriers
     float* ln_mean = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full_bar) + 256);
@@ -312,14 +338,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
         tma_prefetch_desc(&p.b_lo);
         for (int s = 0; s < stages; ++s) {
             mbar_init(&full_bar[s], 1);
-            mbar_init(&empty_bar[s], 1);
+            mbar_init(&empty_bar[s], kNAcc);  // one commit per MMA issuer
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&tfull_bar[b], 1);
-            mbar_init(&tempty_bar[b], 4);  // one arrival per epilogue warp
+            mbar_init(&tfull_bar[b], kNAcc);  // one commit per MMA issuer
+            mbar_init(&tempty_bar[b], 4);     // one arrival per epilogue warp
         }
         mbar_init(recv_bar, 1);
-        mbar_init(done_bar, 1);
+        for (int r = 0; r < 3; ++r) mbar_init(&done_bar[r], 1);
         if (S > 1)  // the phase completes once every peer's rows have arrived
             mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>((S - 1) * rows_per * BN * 4));
         fence_barrier_init();
@@ -375,10 +401,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
                 mbar_wait_drain(&full_bar[i % stages], static_cast<uint32_t>(i / stages) & 1u,
                                 p.err, kDevTimeoutTmaFull);
         }
-    } else if (warp == 1) {
+    } else if (warp == 1 || warp >= 6) {
+        // ---- MMA issuers: role 0 (warp 1), 1 (warp 6), 2 (warp 7) ----
+        const int role = (warp == 1) ? 0 : warp - 5;
         if (lane == 0 && nkb > 0) {
             bool ok = true;
-            int i = 0;
+            int i = 0, s = 0;
+            uint32_t phase = 0;  // parity of stage s's current fill
+            const uint32_t smem0 = smem_u32(smem);
             for (int c = 0; c < nchunks && ok; ++c) {
                 const int b = c & 1;
                 const uint32_t use = static_cast<uint32_t>(c >> 1);
@@ -387,39 +417,47 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
                     break;
                 }
                 tc_fence_after();
-                const uint32_t t_big = tmem_base + static_cast<uint32_t>(b * 2 * BN);
-                const uint32_t t_small = t_big + BN;
+                const uint32_t t_acc = tmem_base + static_cast<uint32_t>((b * kNAcc + role) * BN);
                 const int kend = min(nkb, (c + 1) * CK);
                 for (; i < kend; ++i) {
-                    const int s = i % stages;
-                    const uint32_t round = static_cast<uint32_t>(i / stages);
-                    if (!mbar_wait(&full_bar[s], round & 1u, p.err, kDevTimeoutTmaFull)) {
+                    if (!mbar_wait(&full_bar[s], phase, p.err, kDevTimeoutTmaFull)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t st = smem_u32(smem + static_cast<size_t>(s) * stage_bytes);
-                    const uint32_t a_hi = st, a_lo = st + kATileBytes;
-                    const uint32_t b_hi = st + 2 * kATileBytes, b_lo = b_hi + b_tile_bytes;
+                    // Descriptors of the stage's planes; a k-step moves the start address by 32
+                    // bytes, i.e. +2 in the descriptor's address field.
+                    const uint32_t st = smem0 + static_cast<uint32_t>(s * stage_bytes);
+                    const uint64_t d_ahi = smem_desc_k_sw128(st);
+                    const uint64_t d_alo = smem_desc_k_sw128(st + kATileBytes);
+                    const uint64_t d_bhi = smem_desc_k_sw128(st + 2 * kATileBytes);
+                    const uint64_t d_blo = smem_desc_k_sw128(st + 2 * kATileBytes + b_tile_bytes);
+                    const uint32_t first = (i == c * CK) ? 0u : 1u;  // 0: overwrite the accumulator
 #pragma unroll
                     for (int kk = 0; kk < kBK / 8; ++kk) {
-                        const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
-                        const uint32_t acc = (i == c * CK && kk == 0) ? 0u : 1u;
-                        mma_tf32(t_small, smem_desc_k_sw128(a_lo + off), smem_desc_k_sw128(b_hi + off),
-                                 p.idesc, acc);
-                        mma_tf32(t_small, smem_desc_k_sw128(a_hi + off), smem_desc_k_sw128(b_lo + off),
-                                 p.idesc, 1u);
-                        mma_tf32(t_big, smem_desc_k_sw128(a_hi + off), smem_desc_k_sw128(b_hi + off),
-                                 p.idesc, acc);
+                        const uint64_t o = static_cast<uint64_t>(kk * 2);
+                        const uint32_t acc = (kk == 0) ? first : 1u;
+                        if (role == 0) {
+                            mma_tf32(t_acc, d_ahi + o, d_bhi + o, p.idesc, acc);
+                        } else if (role == 1) {
+                            mma_tf32(t_acc, d_alo + o, d_bhi + o, p.idesc, acc);
+                            if constexpr (kNAcc == 2) mma_tf32(t_acc, d_ahi + o, d_blo + o, p.idesc, 1u);
+                        } else {
+                            mma_tf32(t_acc, d_ahi + o, d_blo + o, p.idesc, acc);
+                        }
                     }
                     mma_commit(&empty_bar[s]);
+                    if (++s == stages) {
+                        s = 0;
+                        phase ^= 1u;
+                    }
                 }
                 if (ok) mma_commit(&tfull_bar[b]);
             }
             // Tensor memory is released after the CTA barrier below: every MMA issued here must
             // have completed by then, also when the loop was aborted.
-            mma_commit(done_bar);
-            mbar_wait_drain(done_bar, 0, p.err, kDevTimeoutAccum);
+            mma_commit(&done_bar[role]);
+            mbar_wait_drain(&done_bar[role], 0, p.err, kDevTimeoutAccum);
         }
     } else {
         // ---- warps 2..5: promote each finished chunk into fp32 registers, one row per thread ----
@@ -446,13 +484,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_3xtf32_kernel(const __grid_c
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t t_big = taddr + static_cast<uint32_t>(b * 2 * BN);
+            const uint32_t t_big = taddr + static_cast<uint32_t>(b * kNAcc * BN);
 #pragma unroll
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 float vb[16], vs[16];
                 tmem_ld_16x2(t_big + c0, t_big + BN + c0, vb, vs);
+                if constexpr (kNAcc == 3) {
+                    float v2[16];
+                    tmem_ld_16(t_big + 2 * BN + c0, v2);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) acc[c0 + j] += vb[j] + vs[j];
+                    for (int j = 0; j < 16; ++j) acc[c0 + j] += vb[j] + (vs[j] + v2[j]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) acc[c0 + j] += vb[j] + vs[j];
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -646,10 +691,10 @@ size_t recv_bytes_for(int bn, int s) {
     return s > 1 ? static_cast<size_t>(s) * rows_per_for(s) * bn * 4 : 0;
 }
 
-// Two TMEM buffers, each with a hi*hi and a correction accumulator of BN columns.
+// Two TMEM buffers, each with one accumulator of BN columns per MMA issuer.
 uint32_t tmem_cols_for(int bn) {
     uint32_t cols = 32;
-    while (cols < static_cast<uint32_t>(4 * bn)) cols <<= 1;
+    while (cols < static_cast<uint32_t>(2 * nacc_for(bn) * bn)) cols <<= 1;
     return cols;
 }
 
@@ -725,7 +770,7 @@ int max_active_clusters(int bn, int s, size_t smem) {
     if (prepare_device_attrs() == cudaSuccess) {
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(1, 1, s);
-        cfg.blockDim = dim3(kThreads);
+        cfg.blockDim = dim3(threads_for(bn));
         cfg.dynamicSmemBytes = smem;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -954,8 +999,8 @@ int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e
          (reinterpret_cast<uintptr_t>(epi.row_stats) & 15) != 0 ||
          (reinterpret_cast<uintptr_t>(epi.ln_c1) & 15) != 0))
         return cudaErrorInvalidValue;
-    // barriers (2 per stage + 6), the TMEM slot and the ticket flag share 256 bytes
-    if ((2 * plan.stages + 6) * 8 + 8 > 256) return cudaErrorInvalidValue;
+    // barriers (2 per stage + 8), the TMEM slot and the ticket flag share 256 bytes
+    if ((2 * plan.stages + 8) * 8 + 8 > 256) return cudaErrorInvalidValue;
     const int n_rows_alloc = (w.N + 255) / 256 * 256;
 
     GemmKParams p{};
@@ -985,7 +1030,7 @@ int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e
 
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(plan.n_tiles, plan.m_tiles, plan.splits);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads_for(plan.bn));
     cfg.dynamicSmemBytes = plan.smem_bytes;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
