@@ -1720,6 +1720,29 @@ namespace {
 __global__ void pack_split_a_kernel(const float* __restrict__ a, int lda, int trans, int m, int k,
                                     float alpha, float* __restrict__ hi, float* __restrict__ lo,
                                     int kpad, int rows_alloc) {
+    // The GEMM that follows (programmatic dependent launch) may start its prologue and weight
+    // loads now; it reads hi / lo only after this grid has completed.
+    pdl_trigger();
+    if (!trans && k == kpad && (kpad & 3) == 0 && (lda & 3) == 0 &&
+        (reinterpret_cast<uintptr_t>(a) & 15) == 0) {
+        // row-major A with whole 16-byte rows: four elements per thread
+        const int q = kpad >> 2;
+        const size_t n4 = static_cast<size_t>(rows_alloc) * q;
+        for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+             i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+            const int r = static_cast<int>(i / q), c4 = static_cast<int>(i - static_cast<size_t>(r) * q);
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (r < m) v = *reinterpret_cast<const float4*>(a + static_cast<size_t>(r) * lda + c4 * 4);
+            float4 h, l;
+            split_tf32(alpha * v.x, h.x, l.x);
+            split_tf32(alpha * v.y, h.y, l.y);
+            split_tf32(alpha * v.z, h.z, l.z);
+            split_tf32(alpha * v.w, h.w, l.w);
+            reinterpret_cast<float4*>(hi)[i] = h;
+            reinterpret_cast<float4*>(lo)[i] = l;
+        }
+        return;
+    }
     const size_t n = static_cast<size_t>(rows_alloc) * kpad;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {

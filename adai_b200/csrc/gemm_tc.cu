@@ -824,6 +824,7 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
     {32000, 1024, 128, 1, 3, 8},
     // d_model 512, d_ff 2048, vocab 16000
     {1536, 512, 64, 4, 2, 4},
+    {2048, 512, 64, 4, 2, 4},
     {16000, 512, 128, 1, 3, 8},
     // d_model 128, d_ff 512
     {384, 128, 32, 2, 2, 2},

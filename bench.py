@@ -248,10 +248,28 @@ def run_op(args):
             ms = timed(lambda: w.matmul(M, A.data_ptr(), C.data_ptr()), args.steps)
             w.close()
             flops = 2.0 * M * N * K
-            print(json.dumps({"op": "gemm", "M": M, "N": N, "K": K, "us": ms * 1e3,
-                              "TFLOP/s": flops / ms / 1e9,
-                              "algorithmic_GB/s": 4.0 * (M * K + K * N + M * N) / ms / 1e6,
-                              "note": "per call: A split into tf32 hi/lo + the GEMM"}), flush=True)
+            line = {"op": "gemm", "M": M, "N": N, "K": K, "us": ms * 1e3,
+                    "TFLOP/s": flops / ms / 1e9,
+                    "algorithmic_GB/s": 4.0 * (M * K + K * N + M * N) / ms / 1e6,
+                    "note": "per call: A split into tf32 hi/lo + the GEMM"}
+            if args.cublas:
+                # Comparison column only (off the product path): cuBLAS SGEMM, what the reference's
+                # matrix_multiply_gpu calls (src/gpu/MatrixGPU.cu:351-370), timed the same way on
+                # the same inputs with TF32 disabled; and both results against a float64 product
+                # within the bound of the reference's tests/matrix_simd_test.cpp:290-319.
+                prev = torch.backends.cuda.matmul.allow_tf32
+                torch.backends.cuda.matmul.allow_tf32 = False
+                C2 = torch.empty(M, N, device="cuda")
+                with torch.cuda.stream(st):
+                    ms2 = timed(lambda: torch.mm(A, B, out=C2), args.steps)
+                torch.backends.cuda.matmul.allow_tf32 = prev
+                ref = A.double() @ B.double()
+                bound = 1e-5 + 1e-5 * (A.double().abs() @ B.double().abs())
+                line.update({"cublas_sgemm_us": ms2 * 1e3,
+                             "speedup_vs_cublas_sgemm": ms2 / ms,
+                             "tol_ratio": float(((C.double() - ref).abs() / bound).max()),
+                             "cublas_tol_ratio": float(((C2.double() - ref).abs() / bound).max())})
+            print(json.dumps(line), flush=True)
     elif args.op == "sample":
         # token selection alone: --sample-batch rows of --sample-vocab random logits, every slot
         # configured with --sampling; one adai_b200_sample_logits call per iteration (the host
@@ -344,6 +362,8 @@ def main():
     ap.add_argument("--sample-batch", type=int, default=128)
     ap.add_argument("--sample-vocab", type=int, default=32000)
     ap.add_argument("--shapes", default="", help="--op gemm: 'M,N,K;M,N,K;...'")
+    ap.add_argument("--cublas", action="store_true",
+                    help="--op gemm: also time cuBLAS SGEMM (comparison column) on the same inputs")
     ap.add_argument("--attn-batch", type=int, default=256)
     ap.add_argument("--attn-lens", default="256,2047")
     ap.add_argument("--attn-append", type=int, default=1)
