@@ -57,7 +57,12 @@ EXPORTS = [
     "adai_b200_activation", "adai_b200_embedding_gather_add_pe", "adai_b200_backend_bind",
     "adai_b200_kv_set_sampling", "adai_b200_kv_sampling_state", "adai_b200_sample_logits",
     "adai_b200_checkpoint_special_tokens", "adai_b200_ctx_check_wait_timeout",
+    "adai_b200_ctx_last_work", "adai_b200_debug_sync_parse", "adai_b200_debug_configure",
+    "adai_b200_debug_settings",
 ]
+
+# Debug-sync modes (adai_b200_debug_configure).
+SYNC_OFF, SYNC_STEP, SYNC_KERNEL = 0, 1, 2
 
 # Kernel classes of adai_b200_profile_step (adai_b200_kernel_class).
 KERNEL_CLASSES = ("gemm", "self_attention", "cross_attention", "norm", "lm_head", "other")
@@ -106,6 +111,10 @@ def load() -> C.CDLL:
     lib.adai_b200_ctx_synchronize.argtypes = [_vp, C.c_double]
     lib.adai_b200_ctx_memory.argtypes = [_vp, C.POINTER(C.c_ulonglong)]
     lib.adai_b200_ctx_check_wait_timeout.argtypes = [_vp, C.POINTER(C.c_double)]
+    lib.adai_b200_ctx_last_work.argtypes = [_vp, C.c_char_p, C.c_int, C.POINTER(C.c_ulonglong)]
+    lib.adai_b200_debug_sync_parse.argtypes = [C.c_char_p, _ip, C.POINTER(C.c_uint)]
+    lib.adai_b200_debug_configure.argtypes = [C.c_int, C.c_uint, C.c_char_p]
+    lib.adai_b200_debug_settings.argtypes = [_ip, C.POINTER(C.c_uint)]
     lib.adai_b200_ctx_stream.argtypes = [_vp]
     lib.adai_b200_ctx_stream.restype = _vp
     lib.adai_b200_model_tensor_count.argtypes = [C.POINTER(ModelDesc)]
@@ -169,6 +178,26 @@ def check(rc: int) -> None:
     if rc == IO:
         raise OSError(msg)
     raise AdaiError(msg)
+
+
+def debug_sync_parse(value: str | None) -> tuple[int, int]:
+    """(mode, every) of an ADAI_B200_SYNC value; ValueError for one the library cannot read."""
+    m, e = C.c_int(), C.c_uint()
+    check(load().adai_b200_debug_sync_parse(None if value is None else value.encode(), C.byref(m),
+                                            C.byref(e)))
+    return m.value, e.value
+
+
+def debug_configure(mode: int = SYNC_OFF, every: int = 1, trace_file: str | None = None) -> None:
+    """Replaces the process's debug-sync settings (ADAI_B200_SYNC / ADAI_B200_TRACE_FILE)."""
+    check(load().adai_b200_debug_configure(mode, every,
+                                           None if trace_file is None else os.fsencode(trace_file)))
+
+
+def debug_settings() -> tuple[int, int]:
+    m, e = C.c_int(), C.c_uint()
+    check(load().adai_b200_debug_settings(C.byref(m), C.byref(e)))
+    return m.value, e.value
 
 
 def checkpoint_config(directory: str) -> ModelConfig:
@@ -253,6 +282,13 @@ class Context:
             check(rc)
             raise AdaiError("the device wait did not report a timeout")
         return t.value
+
+    def last_work(self) -> tuple[str, int]:
+        """("<seq> <phase> <kernel>", seq) of the last GPU work this context queued."""
+        buf = C.create_string_buffer(256)
+        n = C.c_ulonglong()
+        check(self.lib.adai_b200_ctx_last_work(self.h, buf, len(buf), C.byref(n)))
+        return buf.value.decode(), n.value
 
     def memory_bytes(self) -> int:
         v = C.c_ulonglong()

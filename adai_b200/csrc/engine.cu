@@ -29,6 +29,7 @@
 #include "common.cuh"
 #include "checkpoint.h"
 #include "kernels.h"
+#include "trace.h"
 
 using namespace adai_b200;
 
@@ -230,6 +231,7 @@ struct adai_b200_ctx {
     Profiler* prof = nullptr;
     double last_decode_ms = 0.0;
     int last_kernels_per_step = 0;
+    adai_b200_trace::WorkTrace trace;  // last work queued, for failed waits (trace.h)
 
     void* dalloc(size_t bytes) {
         if (bytes == 0) bytes = 16;
@@ -283,6 +285,23 @@ struct adai_b200_ctx {
         }
         return h_pin;
     }
+    bool capturing() const {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        return cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone;
+    }
+    // Records a launch about to be queued. With ADAI_B200_SYNC=kernel[:N] it first waits for the
+    // work already queued (before every Nth launch), so a failure is reported against the kernel
+    // that ran; never inside a stream capture.
+    void note(const char* kernel) {
+        if (capturing()) return;  // recorded into a graph, not queued: its replay is noted
+        const adai_b200_trace::Settings& st = adai_b200_trace::settings();
+        if (st.mode == adai_b200_trace::kSyncKernel) {
+            const unsigned long long n = trace.seq.load(std::memory_order_relaxed);
+            if (n > 0 && (st.every <= 1 || n % st.every == 0)) sync(wait_timeout_seconds());
+        }
+        trace.note_kernel(kernel);
+    }
+    std::string last_work() const { return "; last GPU work queued: " + trace.describe(); }
     // Bounded host wait (GPU_WAIT_TIMEOUT_SECONDS semantics), then the device error word.
     void sync(double timeout_s) {
         // the error word comes back with the work (no second round trip after the wait)
@@ -296,14 +315,15 @@ struct adai_b200_ctx {
             if (q == cudaSuccess) break;
             if (q != cudaErrorNotReady) {
                 unusable = true;
-                fail(ADAI_B200_ERR_CUDA, std::string("device error: ") + cudaGetErrorString(q));
+                fail(ADAI_B200_ERR_CUDA,
+                     std::string("device error: ") + cudaGetErrorString(q) + last_work());
             }
             const double el =
                 std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
             if (el > timeout_s) {
                 unusable = true;
                 fail(ADAI_B200_ERR_TIMEOUT,
-                     "device wait exceeded " + std::to_string(timeout_s) + " s");
+                     "device wait exceeded " + std::to_string(timeout_s) + " s" + last_work());
             }
             std::this_thread::yield();
         }
@@ -312,11 +332,11 @@ struct adai_b200_ctx {
             cuda_ok(cudaMemset(d_err, 0, sizeof(int)), "clear error word");
             if (herr >= 101 && herr <= 103) {
                 unusable = true;
-                fail(ADAI_B200_ERR_TIMEOUT,
-                     "a kernel gave up waiting (code " + std::to_string(herr) + ")");
+                fail(ADAI_B200_ERR_TIMEOUT, "a kernel gave up waiting (code " +
+                                                std::to_string(herr) + ")" + last_work());
             }
             fail(ADAI_B200_ERR_OUT_OF_RANGE,
-                 "a kernel rejected its input (code " + std::to_string(herr) + ")");
+                 "a kernel rejected its input (code " + std::to_string(herr) + ")" + last_work());
         }
     }
 
@@ -376,9 +396,11 @@ struct adai_b200_ctx {
         samp_park_floats = floats;
     }
 
-    void gemm(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e) {
+    void gemm(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e,
+              const char* what = "gemm_3xtf32_kernel") {
         const GemmPlan p = gemm_plan(M, w.N, w.K, e.flags, num_sms);
         ensure_gemm_scratch(p);
+        note(what);
         launch_ok(gemm_launch(a, M, w, e, p, gs, d_err, stream), "gemm launch");
     }
 };
@@ -405,6 +427,18 @@ void timed(adai_b200_ctx* c, int cls, double bytes, double flops, Fn&& fn) {
     c->prof->spans.push_back(sp);
 }
 
+// guarded() for an entry point that queues GPU work: its phase tag and NVTX range around `fn`,
+// and with ADAI_B200_SYNC=step or kernel a bounded wait for that work before it returns.
+template <class Fn>
+int traced(adai_b200_ctx* c, const char* phase, Fn&& fn) {
+    return guarded([&] {
+        adai_b200_trace::PhaseScope ps(c ? &c->trace : nullptr, phase);
+        fn();
+        if (c && !c->unusable && adai_b200_trace::settings().mode != adai_b200_trace::kSyncOff)
+            c->sync(wait_timeout_seconds());
+    });
+}
+
 double gemm_bytes(double M, double N, double K) { return 4.0 * (M * K + K * N + M * N); }
 double gemm_flops(double M, double N, double K) { return 2.0 * M * N * K; }
 
@@ -427,6 +461,7 @@ void fill_tc_weight(adai_b200_ctx* c, float* staging, const TcWeight& w, int row
                     int K, int Nsub) {
     const size_t bytes = static_cast<size_t>(K) * Nsub * sizeof(float);
     cuda_ok(cudaMemcpyAsync(staging, host, bytes, cudaMemcpyHostToDevice, c->stream), "upload");
+    c->note("transpose_split_kernel");
     launch_transpose_split(staging, K, Nsub, w.hi + static_cast<size_t>(row0) * K,
                            w.lo + static_cast<size_t>(row0) * K, c->stream);
     cuda_ok(cudaGetLastError(), "transpose-split");
@@ -461,9 +496,11 @@ void fill_tc_weight_folded(adai_b200_ctx* c, float* staging, const TcWeight& w, 
                            const float* extra, float* c1, float* bias) {
     const size_t bytes = static_cast<size_t>(K) * Nsub * sizeof(float);
     cuda_ok(cudaMemcpyAsync(staging, host, bytes, cudaMemcpyHostToDevice, c->stream), "upload");
+    c->note("fold_layernorm_kernel");
     fold_layernorm_kernel<<<(Nsub + 127) / 128, 128, 0, c->stream>>>(staging, K, Nsub, g, b, extra,
                                                                      c1 + row0, bias + row0);
     cuda_ok(cudaGetLastError(), "fold-layernorm");
+    c->note("transpose_split_kernel");
     launch_transpose_split(staging, K, Nsub, w.hi + static_cast<size_t>(row0) * K,
                            w.lo + static_cast<size_t>(row0) * K, c->stream);
     cuda_ok(cudaGetLastError(), "transpose-split");
@@ -652,6 +689,7 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
     // per-32-column group statistics (kEpiRowStats), from which that GEMM takes mean and rstd.
     const double ln_bytes = 3.0 * Bd * Dd * 4.0;
     timed(c, ADAI_B200_KC_NORM, ln_bytes, 0, [&] {
+        c->note("embed_stats_kernel");
         launch_embed_stats(m.dec_embed, s.ids, m.pe, m.d.max_seq, s.slots, kv->d_self_len, s.x,
                            s.nrm_hi, s.nrm_lo, s.ln_stats, B, D, m.d.vocab, c->d_err, st);
     });
@@ -684,7 +722,7 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             e.ldo = 3 * D;
             ln_fold(e, w.qkv_c1, w.qkv_bias);
             timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, 3 * Dd, Dd), gemm_flops(Bd, 3 * Dd, Dd),
-                  [&] { c->gemm(a_nrm, B, w.qkv, e); });
+                  [&] { c->gemm(a_nrm, B, w.qkv, e, "gemm_3xtf32_kernel (decoder self Q|K|V)"); });
         }
         {  // masked self-attention over the cache, the new K/V appended first
             DecodeAttnArgs a;
@@ -710,8 +748,10 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             a.scale = scale;
             a.ws = c->attn_ws;
             a.tickets = c->attn_tickets;
-            timed(c, ADAI_B200_KC_SELF_ATTN, self_bytes, 0,
-                  [&] { launch_decode_attention(a, c->d_err, st); });
+            timed(c, ADAI_B200_KC_SELF_ATTN, self_bytes, 0, [&] {
+                c->note("decode_attention_kernel (self, append)");
+                launch_decode_attention(a, c->d_err, st);
+            });
         }
         {  // x = x + attn W_o
             GemmEpilogue e;
@@ -722,7 +762,7 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             e.ldo = D;
             x_stats(e);
             timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Dd, Dd), gemm_flops(Bd, Dd, Dd),
-                  [&] { c->gemm(a_attn, B, w.o, e); });
+                  [&] { c->gemm(a_attn, B, w.o, e, "gemm_3xtf32_kernel (decoder self W_o)"); });
         }
         {  // cross-attention query of LN2(x)
             GemmEpilogue e;
@@ -731,7 +771,7 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             e.ldo = D;
             ln_fold(e, w.cq_c1, w.cq_bias);
             timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Dd, Dd), gemm_flops(Bd, Dd, Dd),
-                  [&] { c->gemm(a_nrm, B, w.cq, e); });
+                  [&] { c->gemm(a_nrm, B, w.cq, e, "gemm_3xtf32_kernel (decoder cross Q)"); });
         }
         {
             DecodeAttnArgs a;
@@ -755,8 +795,10 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             a.scale = scale;
             a.ws = c->attn_ws;
             a.tickets = c->attn_tickets;
-            timed(c, ADAI_B200_KC_CROSS_ATTN, cross_bytes, 0,
-                  [&] { launch_decode_attention(a, c->d_err, st); });
+            timed(c, ADAI_B200_KC_CROSS_ATTN, cross_bytes, 0, [&] {
+                c->note("decode_attention_kernel (cross)");
+                launch_decode_attention(a, c->d_err, st);
+            });
         }
         {
             GemmEpilogue e;
@@ -767,7 +809,7 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             e.ldo = D;
             x_stats(e);
             timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Dd, Dd), gemm_flops(Bd, Dd, Dd),
-                  [&] { c->gemm(a_attn, B, w.co, e); });
+                  [&] { c->gemm(a_attn, B, w.co, e, "gemm_3xtf32_kernel (decoder cross W_o)"); });
         }
         {  // h = GELU(LN3(x) W1 + b1), written as its tf32 split for the next GEMM
             GemmEpilogue e;
@@ -777,7 +819,7 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             e.lds = F;
             ln_fold(e, w.w1_c1, w.w1_bias);
             timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Fd, Dd), gemm_flops(Bd, Fd, Dd),
-                  [&] { c->gemm(a_nrm, B, w.w1, e); });
+                  [&] { c->gemm(a_nrm, B, w.w1, e, "gemm_3xtf32_kernel (decoder FFN W1)"); });
         }
         {  // x = x + (h W2 + b2)
             GemmEpilogue e;
@@ -789,7 +831,7 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
             e.ldo = D;
             x_stats(e);
             timed(c, ADAI_B200_KC_GEMM, gemm_bytes(Bd, Dd, Fd), gemm_flops(Bd, Dd, Fd),
-                  [&] { c->gemm(a_h, B, w.w2, e); });
+                  [&] { c->gemm(a_h, B, w.w2, e, "gemm_3xtf32_kernel (decoder FFN W2)"); });
         }
     }
     {  // logits = x W_out + b, first maximum per row
@@ -802,12 +844,14 @@ void record_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
         e.nonfinite = s.nonfinite;
         const double Vd = m.d.vocab;
         timed(c, ADAI_B200_KC_HEAD, 4.0 * (Bd * Dd + Dd * Vd), gemm_flops(Bd, Vd, Dd),
-              [&] { c->gemm(a_nrm, B, m.head, e); });
+              [&] { c->gemm(a_nrm, B, m.head, e, "gemm_3xtf32_kernel (LM head + argmax)"); });
     }
     if (flags & kStepSample) {  // rows whose slot samples replace the argmax (sample.cu)
         const SampleArgs a = sample_args(c, kv, B, s.logits, m.d.vocab, s.ids, s.next, s.nonfinite);
-        timed(c, ADAI_B200_KC_OTHER, 4.0 * Bd * m.d.vocab, 0,
-              [&] { cuda_ok(launch_sample_rows(a, st), "sample launch"); });
+        timed(c, ADAI_B200_KC_OTHER, 4.0 * Bd * m.d.vocab, 0, [&] {
+            c->note("sample_rows_kernel");
+            cuda_ok(launch_sample_rows(a, st), "sample launch");
+        });
     }
 }
 
@@ -873,6 +917,24 @@ cudaGraphExec_t get_graph(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) 
     cudaGraphDestroy(g);
     c->graphs[key] = ge;
     return ge;
+}
+
+// Queues one decode step: replays the step's CUDA graph, or, with ADAI_B200_SYNC=kernel, queues
+// its kernels one by one without a graph so that each launch is waited for and named.
+void run_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, int flags) {
+    if (adai_b200_trace::settings().mode != adai_b200_trace::kSyncKernel) {
+        cudaGraphExec_t g = get_graph(c, kv, B, flags);
+        c->note("decode step (CUDA graph)");
+        cuda_ok(cudaGraphLaunch(g, c->stream), "graph launch");
+        return;
+    }
+    presize_step_scratch(c, kv, B, flags);
+    record_step(c, kv, B, flags);
+    c->note("record_and_advance_kernel");
+    record_and_advance_kernel<<<(B + 127) / 128, 128, 0, c->stream>>>(
+        c->sb.next, c->sb.ids, c->sb.slots, kv->d_self_len, kv->d_hist, kv->self_cap,
+        c->sb.nonfinite, c->sb.nonfinite_any, B, (flags & kStepAdvanceIds) ? 1 : 0);
+    cuda_ok(cudaGetLastError(), "advance launch");
 }
 
 void check_ctx(adai_b200_ctx* c) {
@@ -996,11 +1058,12 @@ int adai_b200_ctx_synchronize(adai_b200_ctx* c, double timeout_seconds) {
 }
 
 int adai_b200_ctx_check_wait_timeout(adai_b200_ctx* c, double* waited_seconds) {
-    return guarded([&] {
+    return traced(c, "adai_b200_ctx_check_wait_timeout", [&] {
         check_ctx(c);
         int* gave_up = c->dzalloc_t<int>(1);
         const auto t0 = std::chrono::steady_clock::now();
         try {
+            c->note("wait_selftest_kernel");
             launch_wait_selftest(c->d_err, gave_up, c->stream);
             cuda_ok(cudaGetLastError(), "wait self-test launch");
             int h = 0;
@@ -1017,6 +1080,51 @@ int adai_b200_ctx_check_wait_timeout(adai_b200_ctx* c, double* waited_seconds) {
     });
 }
 
+int adai_b200_ctx_last_work(adai_b200_ctx* c, char* buf, int buf_len, unsigned long long* launches) {
+    return guarded([&] {
+        if (!c) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null context");
+        if (launches) *launches = c->trace.seq.load(std::memory_order_relaxed);
+        if (buf && buf_len > 0) {
+            const std::string w = c->trace.describe();
+            const size_t n = std::min(w.size(), static_cast<size_t>(buf_len - 1));
+            std::memcpy(buf, w.data(), n);
+            buf[n] = '\0';
+        }
+    });
+}
+
+int adai_b200_debug_sync_parse(const char* value, int* mode, unsigned* every) {
+    return guarded([&] {
+        if (!mode || !every) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null output");
+        std::string problem;
+        if (!adai_b200_trace::parse_sync(value, mode, every, &problem))
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, problem);
+    });
+}
+
+int adai_b200_debug_configure(int mode, unsigned every, const char* trace_file) {
+    return guarded([&] {
+        if (mode < adai_b200_trace::kSyncOff || mode > adai_b200_trace::kSyncKernel)
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "mode must be 0 (off), 1 (step) or 2 (kernel)");
+        if (every < 1 || every > 1000000)
+            fail(ADAI_B200_ERR_INVALID_ARGUMENT, "every must be in [1, 1000000]");
+        adai_b200_trace::Settings st;
+        st.mode = mode;
+        st.every = every;
+        if (trace_file) st.trace_file = trace_file;
+        adai_b200_trace::set_settings(st);
+    });
+}
+
+int adai_b200_debug_settings(int* mode, unsigned* every) {
+    return guarded([&] {
+        if (!mode || !every) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null output");
+        const adai_b200_trace::Settings& st = adai_b200_trace::settings();
+        *mode = st.mode;
+        *every = st.every;
+    });
+}
+
 int adai_b200_ctx_memory(adai_b200_ctx* c, unsigned long long* bytes) {
     return guarded([&] {
         if (!c || !bytes) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null argument");
@@ -1030,7 +1138,7 @@ int adai_b200_model_tensor_count(const adai_b200_model_desc* d) { return d ? ten
 
 int adai_b200_model_upload(adai_b200_ctx* c, const adai_b200_model_desc* d,
                            const float* const* t, const float* pe_table) {
-    return guarded([&] {
+    return traced(c, "adai_b200_model_upload", [&] {
         check_ctx(c);
         validate_desc(d);
         if (!t) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null tensor list");
@@ -1171,7 +1279,7 @@ int adai_b200_checkpoint_read(const char* dir, const adai_b200_model_desc* d, fl
 }
 
 int adai_b200_model_load(adai_b200_ctx* c, const char* dir, const adai_b200_model_desc* expect) {
-    return guarded([&] {
+    return traced(c, "adai_b200_model_load", [&] {
         check_ctx(c);
         if (!dir) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null checkpoint directory");
         const adai_b200_model_desc d = read_checkpoint_config(dir);
@@ -1199,7 +1307,7 @@ int adai_b200_model_load(adai_b200_ctx* c, const char* dir, const adai_b200_mode
 
 int adai_b200_kv_create(adai_b200_ctx* c, int max_slots, int self_cap, int cross_cap,
                         adai_b200_kv** out) {
-    return guarded([&] {
+    return traced(c, "adai_b200_kv_create", [&] {
         check_ctx(c);
         check_model(c);
         if (!out) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null output handle");
@@ -1262,7 +1370,7 @@ int adai_b200_kv_destroy(adai_b200_ctx* c, adai_b200_kv* kv) {
 }
 
 int adai_b200_kv_reset(adai_b200_ctx* c, adai_b200_kv* kv, int slot) {
-    return guarded([&] {
+    return traced(c, "adai_b200_kv_reset", [&] {
         check_ctx(c);
         check_kv(c, kv);
         if (slot < 0 || slot >= kv->max_slots) fail(ADAI_B200_ERR_OUT_OF_RANGE, "slot out of range");
@@ -1280,7 +1388,7 @@ int adai_b200_kv_reset(adai_b200_ctx* c, adai_b200_kv* kv, int slot) {
 }
 
 int adai_b200_kv_clear_self(adai_b200_ctx* c, adai_b200_kv* kv, int slot) {
-    return guarded([&] {
+    return traced(c, "adai_b200_kv_clear_self", [&] {
         check_ctx(c);
         check_kv(c, kv);
         if (slot < 0 || slot >= kv->max_slots) fail(ADAI_B200_ERR_OUT_OF_RANGE, "slot out of range");
@@ -1303,7 +1411,7 @@ int adai_b200_kv_length(adai_b200_ctx* c, adai_b200_kv* kv, int slot, int* self_
 
 int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots, const int* ids,
                      const int* src_lens, float* enc_out) {
-    return guarded([&] {
+    return traced(c, "adai_b200_encode", [&] {
         check_ctx(c);
         check_model(c);
         check_kv(c, kv);
@@ -1386,11 +1494,14 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
             cuda_ok(cudaMemcpyAsync(e.offsets, p_off, nseq * sizeof(int), cudaMemcpyHostToDevice, st), "H2D");
             cuda_ok(cudaMemcpyAsync(e.lens, p_len, nseq * sizeof(int), cudaMemcpyHostToDevice, st), "H2D");
             const int Le = m.d.enc_layers;
+            c->note("embed_ln_kernel");
             launch_embed_ln(m.enc_embed, e.ids, m.pe, m.d.max_seq, nullptr, nullptr, e.row_pos, e.x,
                             Le ? m.enc[0].ln1g : m.enc_lnf_g, Le ? m.enc[0].ln1b : m.enc_lnf_b,
                             e.nrm_hi, e.nrm_lo, rows, D, m.d.vocab, c->d_err, st);
-            if (Le == 0)  // the embedding row LayerNorm'd by final_norm is the encoder output
+            if (Le == 0) {  // the embedding row LayerNorm'd by final_norm is the encoder output
+                c->note("layernorm_kernel (encoder final)");
                 launch_layernorm(e.x, D, m.enc_lnf_g, m.enc_lnf_b, e.out, e.nrm_hi, e.nrm_lo, rows, D, st);
+            }
             const TcActs a_nrm = acts(e.nrm_hi, e.nrm_lo, D, e.rows);
             const TcActs a_attn = acts(e.attn_hi, e.attn_lo, D, e.rows);
             const TcActs a_h = acts(e.h_hi, e.h_lo, F, e.rows);
@@ -1400,7 +1511,7 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
                 q.flags = kEpiStore;
                 q.out = e.qkv;
                 q.ldo = 3 * D;
-                c->gemm(a_nrm, rows, w.qkv, q);
+                c->gemm(a_nrm, rows, w.qkv, q, "gemm_3xtf32_kernel (encoder Q|K|V)");
                 if (tc_attn) {
                     PrefillTcArgs pa;
                     pa.qkv = e.qkv;
@@ -1422,8 +1533,10 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
                     pa.out_lo = e.attn_lo;
                     pa.scale = scale;
                     pa.err = c->d_err;
+                    c->note("prefill_attention_tc_kernel");
                     launch_ok(launch_prefill_attention_tc(pa, st), "prefill attention launch");
                 } else {
+                    c->note("prefill_attention_kernel");
                     launch_prefill_attention(e.qkv, D, H, e.offsets, e.lens, nseq, max_len, e.attn_hi,
                                              e.attn_lo, scale, st);
                 }
@@ -1433,7 +1546,8 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
                 o.ldr = D;
                 o.out = e.x;
                 o.ldo = D;
-                c->gemm(a_attn, rows, w.o, o);
+                c->gemm(a_attn, rows, w.o, o, "gemm_3xtf32_kernel (encoder W_o)");
+                c->note("layernorm_kernel (encoder LN2)");
                 launch_layernorm(e.x, D, w.ln2g, w.ln2b, nullptr, e.nrm_hi, e.nrm_lo, rows, D, st);
                 GemmEpilogue f1;
                 f1.flags = kEpiBias | kEpiGelu | kEpiSplit;
@@ -1441,7 +1555,7 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
                 f1.out_hi = e.h_hi;
                 f1.out_lo = e.h_lo;
                 f1.lds = F;
-                c->gemm(a_nrm, rows, w.w1, f1);
+                c->gemm(a_nrm, rows, w.w1, f1, "gemm_3xtf32_kernel (encoder FFN W1)");
                 GemmEpilogue f2;
                 f2.flags = kEpiBias | kEpiResid | kEpiStore;
                 f2.bias = w.b2;
@@ -1449,8 +1563,9 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
                 f2.ldr = D;
                 f2.out = e.x;
                 f2.ldo = D;
-                c->gemm(a_h, rows, w.w2, f2);
+                c->gemm(a_h, rows, w.w2, f2, "gemm_3xtf32_kernel (encoder FFN W2)");
                 const bool last = l + 1 == Le;
+                c->note("layernorm_kernel (encoder LN1 / final)");
                 launch_layernorm(e.x, D, last ? m.enc_lnf_g : m.enc[l + 1].ln1g,
                                  last ? m.enc_lnf_b : m.enc[l + 1].ln1b, last ? e.out : nullptr,
                                  e.nrm_hi, e.nrm_lo, rows, D, st);
@@ -1467,7 +1582,7 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
                 s.d_model = D;
                 s.row_slot = e.row_slot;
                 s.row_pos = e.row_pos;
-                c->gemm(a_nrm, rows, m.dec[l].ckv, s);
+                c->gemm(a_nrm, rows, m.dec[l].ckv, s, "gemm_3xtf32_kernel (cross K|V scatter)");
             }
             if (enc_out)
                 cuda_ok(cudaMemcpyAsync(enc_out + row_base * D, e.out, static_cast<size_t>(rows) * D * sizeof(float),
@@ -1493,16 +1608,15 @@ int adai_b200_encode(adai_b200_ctx* c, adai_b200_kv* kv, int n, const int* slots
 
 int adai_b200_decode_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slots,
                           const int* ids, int* next_ids, float* logits) {
-    return guarded([&] {
+    return traced(c, "adai_b200_decode_step", [&] {
         check_ctx(c);
         check_model(c);
         check_kv(c, kv);
         if (!next_ids) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null next_ids");
         stage_batch(c, kv, B, slots, ids, 1);
         const int flags = (logits ? kStepLogits : 0) | sample_flag(kv, B, slots);
-        cudaGraphExec_t g = get_graph(c, kv, B, flags);
         cuda_ok(cudaMemsetAsync(c->sb.nonfinite_any, 0, sizeof(int), c->stream), "memset");
-        cuda_ok(cudaGraphLaunch(g, c->stream), "graph launch");
+        run_step(c, kv, B, flags);
         // next ids and the non-finite flag: [next R | flag], one copy
         const size_t R = static_cast<size_t>(c->sb.rows);
         int* pin = c->pinned(R + 1);
@@ -1520,7 +1634,7 @@ int adai_b200_decode_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* 
 
 int adai_b200_generate(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slots,
                        const int* first_ids, int steps, int* out_ids) {
-    return guarded([&] {
+    return traced(c, "adai_b200_generate", [&] {
         check_ctx(c);
         check_model(c);
         check_kv(c, kv);
@@ -1529,13 +1643,14 @@ int adai_b200_generate(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slo
         std::vector<int> pos0(B);
         for (int b = 0; b < B; ++b) pos0[b] = kv->self_len[slots[b]];
         const int flags = kStepAdvanceIds | sample_flag(kv, B, slots);
-        cudaGraphExec_t g = get_graph(c, kv, B, flags);
+        if (adai_b200_trace::settings().mode != adai_b200_trace::kSyncKernel)
+            get_graph(c, kv, B, flags);  // captured before the timed region
         cuda_ok(cudaMemsetAsync(c->sb.nonfinite_any, 0, sizeof(int), c->stream), "memset");
         cudaEvent_t e0, e1;
         cuda_ok(cudaEventCreate(&e0), "cudaEventCreate");
         cuda_ok(cudaEventCreate(&e1), "cudaEventCreate");
         cuda_ok(cudaEventRecord(e0, c->stream), "cudaEventRecord");
-        for (int s = 0; s < steps; ++s) cuda_ok(cudaGraphLaunch(g, c->stream), "graph launch");
+        for (int s = 0; s < steps; ++s) run_step(c, kv, B, flags);
         cuda_ok(cudaEventRecord(e1, c->stream), "cudaEventRecord");
         c->sync(wait_timeout_seconds() + 1e-3 * steps);
         float ms = 0.f;
@@ -1543,7 +1658,8 @@ int adai_b200_generate(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slo
         cudaEventDestroy(e0);
         cudaEventDestroy(e1);
         c->last_decode_ms = ms;
-        c->last_kernels_per_step = c->graph_kernels[GraphKey{kv, B, flags}];
+        const auto gk = c->graph_kernels.find(GraphKey{kv, B, flags});
+        c->last_kernels_per_step = gk != c->graph_kernels.end() ? gk->second : 0;
         for (int b = 0; b < B; ++b) kv->self_len[slots[b]] += steps;
         int nf = 0;
         cuda_ok(cudaMemcpy(&nf, c->sb.nonfinite_any, sizeof(int), cudaMemcpyDeviceToHost), "D2H flag");
@@ -1599,7 +1715,7 @@ extern "C" {
 
 int adai_b200_kv_set_sampling(adai_b200_ctx* c, adai_b200_kv* kv, int slot,
                               const adai_b200_sampling* cfg, const int* history, int n_history) {
-    return guarded([&] {
+    return traced(c, "adai_b200_kv_set_sampling", [&] {
         check_ctx(c);
         check_model(c);
         check_kv(c, kv);
@@ -1653,7 +1769,7 @@ int adai_b200_kv_set_sampling(adai_b200_ctx* c, adai_b200_kv* kv, int slot,
 
 int adai_b200_kv_sampling_state(adai_b200_ctx* c, adai_b200_kv* kv, int slot, unsigned* mt_state,
                                 int* new_tokens) {
-    return guarded([&] {
+    return traced(c, "adai_b200_kv_sampling_state", [&] {
         check_ctx(c);
         check_kv(c, kv);
         check_slot(kv, slot);
@@ -1670,7 +1786,7 @@ int adai_b200_kv_sampling_state(adai_b200_ctx* c, adai_b200_kv* kv, int slot, un
 
 int adai_b200_sample_logits(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slots,
                             const int* fed_ids, const float* logits, int ld, int* next_ids) {
-    return guarded([&] {
+    return traced(c, "adai_b200_sample_logits", [&] {
         check_ctx(c);
         check_model(c);
         check_kv(c, kv);
@@ -1701,6 +1817,7 @@ int adai_b200_sample_logits(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int
         cuda_ok(cudaMemsetAsync(c->sb.nonfinite, 0, B * sizeof(int), st), "memset");
         const SampleArgs a = sample_args(c, kv, B, logits, ld, fed_ids ? c->sb.ids : nullptr,
                                          c->sb.next, c->sb.nonfinite);
+        c->note("sample_rows_kernel");
         cuda_ok(launch_sample_rows(a, st), "sample launch");
         cuda_ok(cudaMemcpyAsync(pin, c->sb.next, B * sizeof(int), cudaMemcpyDeviceToHost, st), "D2H");
         cuda_ok(cudaMemcpyAsync(pin + 2 * B, c->sb.nonfinite, B * sizeof(int), cudaMemcpyDeviceToHost, st), "D2H");
@@ -1807,6 +1924,7 @@ adai_b200_weight* prepare_weight(adai_b200_ctx* c, const float* B, int k, int n,
     w->w.N = n;
     w->w.hi = c->dzalloc_t<float>(rows * kpad);
     w->w.lo = c->dzalloc_t<float>(rows * kpad);
+    c->note(trans_b ? "copy_split_pad_kernel" : "transpose_split_pad_kernel");
     if (trans_b) {
         copy_split_pad_kernel<<<blocks_for(static_cast<size_t>(n) * kpad), 256, 0, c->stream>>>(
             B, ldb, k, n, kpad, w->w.hi, w->w.lo);
@@ -1856,6 +1974,7 @@ void gemm_run(adai_b200_ctx* c, int m, const float* A, int lda, bool trans_a, fl
             c->op_c_floats = need_c;
         }
     }
+    c->note("pack_split_a_kernel");
     pack_split_a_kernel<<<blocks_for(need), 256, 0, c->stream>>>(A, lda, trans_a ? 1 : 0, m, k, alpha,
                                                                  c->op_a_hi, c->op_a_lo, kpad, rows_alloc);
     cuda_ok(cudaGetLastError(), "split");
@@ -1873,7 +1992,7 @@ void gemm_run(adai_b200_ctx* c, int m, const float* A, int lda, bool trans_a, fl
 }  // namespace
 
 int adai_b200_weight_create(adai_b200_ctx* c, const float* B, int k, int n, adai_b200_weight** out) {
-    return guarded([&] {
+    return traced(c, "adai_b200_weight_create", [&] {
         check_ctx(c);
         if (!out) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null output handle");
         *out = prepare_weight(c, B, k, n);
@@ -1890,7 +2009,7 @@ int adai_b200_weight_destroy(adai_b200_ctx* c, adai_b200_weight* w) {
 }
 
 int adai_b200_sgemm_prepared(adai_b200_ctx* c, int m, const float* A, const adai_b200_weight* w, float* C) {
-    return guarded([&] {
+    return traced(c, "adai_b200_sgemm_prepared", [&] {
         check_ctx(c);
         if (!w) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "null weight");
         gemm_run(c, m, A, w->K, false, 1.0f, w, C, w->w.N);
@@ -1898,7 +2017,7 @@ int adai_b200_sgemm_prepared(adai_b200_ctx* c, int m, const float* A, const adai
 }
 
 int adai_b200_sgemm(adai_b200_ctx* c, int m, int n, int k, const float* A, const float* B, float* C) {
-    return guarded([&] {
+    return traced(c, "adai_b200_sgemm", [&] {
         check_ctx(c);
         adai_b200_weight* w = prepare_weight(c, B, k, n);
         try {
@@ -1917,7 +2036,7 @@ int adai_b200_decode_attention(adai_b200_ctx* c, int B, int H, int head_dim, int
                                const float* q, const float* k_new, const float* v_new,
                                float* k_cache, float* v_cache, const int* lens, int max_len,
                                float* out) {
-    return guarded([&] {
+    return traced(c, "adai_b200_decode_attention", [&] {
         check_ctx(c);
         if (B <= 0 || H <= 0 || capacity <= 0 || !q || !k_cache || !v_cache || !lens || !out)
             fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad attention arguments");
@@ -1956,6 +2075,7 @@ int adai_b200_decode_attention(adai_b200_ctx* c, int B, int H, int head_dim, int
         a.scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
         a.ws = c->attn_ws;
         a.tickets = c->attn_tickets;
+        c->note("decode_attention_kernel");
         launch_decode_attention(a, c->d_err, c->stream);
         cuda_ok(cudaGetLastError(), "attention launch");
     });
@@ -1972,7 +2092,7 @@ int adai_b200_ctx_last_timing(adai_b200_ctx* c, double* decode_ms, int* kernels_
 int adai_b200_profile_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int* slots,
                            const int* ids, int n_classes, double* ms, double* bytes,
                            double* flops, int* launches) {
-    return guarded([&] {
+    return traced(c, "adai_b200_profile_step", [&] {
         check_ctx(c);
         check_model(c);
         check_kv(c, kv);
@@ -1990,6 +2110,7 @@ int adai_b200_profile_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int*
         try {
             record_step(c, kv, B, flags);
             timed(c, ADAI_B200_KC_OTHER, 0, 0, [&] {
+                c->note("record_and_advance_kernel");
                 record_and_advance_kernel<<<(B + 127) / 128, 128, 0, c->stream>>>(
                     c->sb.next, c->sb.ids, c->sb.slots, kv->d_self_len, kv->d_hist, kv->self_cap,
                     c->sb.nonfinite, c->sb.nonfinite_any, B, 0);
@@ -2025,10 +2146,11 @@ int adai_b200_profile_step(adai_b200_ctx* c, adai_b200_kv* kv, int B, const int*
 
 int adai_b200_layernorm(adai_b200_ctx* c, const float* x, const float* gamma, const float* beta,
                         float* out, int rows, int D) {
-    return guarded([&] {
+    return traced(c, "adai_b200_layernorm", [&] {
         check_ctx(c);
         if (!x || !gamma || !beta || !out || rows <= 0) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad LayerNorm arguments");
         if (!layernorm_width_supported(D)) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "D must be 128 * {1,2,3,4,6,8,12,16}");
+        c->note("layernorm_kernel");
         launch_layernorm(x, D, gamma, beta, out, nullptr, nullptr, rows, D, c->stream);
         cuda_ok(cudaGetLastError(), "layernorm launch");
     });
@@ -2038,7 +2160,7 @@ int adai_b200_layernorm(adai_b200_ctx* c, const float* x, const float* gamma, co
 int adai_b200_gemm_strided(adai_b200_ctx* c, int trans_a, int trans_b, int m, int n, int k,
                            float alpha, const float* a, int lda, const float* b, int ldb, float* out,
                            int ldc) {
-    return guarded([&] {
+    return traced(c, "adai_b200_gemm_strided", [&] {
         check_ctx(c);
         if (m <= 0 || n <= 0) return;  // nothing to write, as the reference returns early
         if (!out || ldc < n) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad output of the strided GEMM");
@@ -2064,9 +2186,10 @@ int adai_b200_gemm_strided(adai_b200_ctx* c, int trans_a, int trans_b, int m, in
 }
 
 int adai_b200_softmax_rows(adai_b200_ctx* c, float* data, int rows, int cols) {
-    return guarded([&] {
+    return traced(c, "adai_b200_softmax_rows", [&] {
         check_ctx(c);
         if (rows < 0 || cols < 0 || (rows && cols && !data)) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad softmax arguments");
+        c->note("softmax_rows_kernel");
         launch_softmax_rows(data, rows, cols, c->stream);
         cuda_ok(cudaGetLastError(), "softmax launch");
     });
@@ -2075,10 +2198,11 @@ int adai_b200_softmax_rows(adai_b200_ctx* c, float* data, int rows, int cols) {
 int adai_b200_layernorm_fwd(adai_b200_ctx* c, const float* x, float* y, float* x_normed,
                             const float* gamma, const float* beta, float* mean, float* rstd,
                             int rows, int cols, float eps) {
-    return guarded([&] {
+    return traced(c, "adai_b200_layernorm_fwd", [&] {
         check_ctx(c);
         if (rows < 0 || cols <= 0 || (rows && (!x || !y || !gamma || !beta)))
             fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad LayerNorm arguments");
+        c->note("layernorm_rows_kernel");
         launch_layernorm_rows(x, y, x_normed, gamma, beta, mean, rstd, rows, cols, eps, c->stream);
         cuda_ok(cudaGetLastError(), "layernorm launch");
     });
@@ -2086,20 +2210,22 @@ int adai_b200_layernorm_fwd(adai_b200_ctx* c, const float* x, float* y, float* x
 
 int adai_b200_add_row_bias(adai_b200_ctx* c, const float* m, const float* bias, float* out, int rows,
                            int cols) {
-    return guarded([&] {
+    return traced(c, "adai_b200_add_row_bias", [&] {
         check_ctx(c);
         if (rows < 0 || cols <= 0 || (rows && (!m || !bias || !out)))
             fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad bias arguments");
+        c->note("add_row_bias_kernel");
         launch_add_row_bias(m, bias, out, rows, cols, c->stream);
         cuda_ok(cudaGetLastError(), "bias launch");
     });
 }
 
 int adai_b200_activation(adai_b200_ctx* c, float* data, int size, int type) {
-    return guarded([&] {
+    return traced(c, "adai_b200_activation", [&] {
         check_ctx(c);
         if (size < 0 || (size && !data)) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad activation arguments");
         if (type < 0 || type > 3) fail(ADAI_B200_ERR_INVALID_ARGUMENT, "activation type must be 0..3");
+        c->note("activation_kernel");
         launch_activation(data, static_cast<size_t>(size), type, c->stream);
         cuda_ok(cudaGetLastError(), "activation launch");
     });
@@ -2108,10 +2234,11 @@ int adai_b200_activation(adai_b200_ctx* c, float* data, int size, int type) {
 int adai_b200_embedding_gather_add_pe(adai_b200_ctx* c, const float* table, const int* ids,
                                       const float* pe, int pe_rows, int pos_offset, float* out, int n,
                                       int d, int vocab) {
-    return guarded([&] {
+    return traced(c, "adai_b200_embedding_gather_add_pe", [&] {
         check_ctx(c);
         if (n < 0 || d <= 0 || (n && (!table || !ids || !out)))
             fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad embedding arguments");
+        c->note("embed_pe_kernel");
         launch_embed_pe(table, ids, pe, pe_rows, pos_offset, out, n, d,
                         vocab > 0 ? vocab : std::numeric_limits<int>::max(), c->d_err, c->stream);
         cuda_ok(cudaGetLastError(), "embedding launch");
@@ -2175,7 +2302,7 @@ int adai_b200_decode_attention_static(adai_b200_ctx* c, int B, int H, int head_d
                                       const float* q, const float* k_new, const float* v_new,
                                       float* k_cache, float* v_cache, const int* lens, int max_len,
                                       float* out) {
-    return guarded([&] {
+    return traced(c, "adai_b200_decode_attention_static", [&] {
         check_ctx(c);
         if (B <= 0 || H <= 0 || capacity <= 0 || !q || !k_cache || !v_cache || !lens || !out)
             fail(ADAI_B200_ERR_INVALID_ARGUMENT, "bad attention arguments");
@@ -2225,6 +2352,7 @@ int adai_b200_decode_attention_static(adai_b200_ctx* c, int B, int H, int head_d
         a.scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
         a.tickets = reinterpret_cast<int*>(base);
         a.ws = reinterpret_cast<float*>(base + kStaticAttnTicketBytes);
+        c->note("decode_attention_kernel");
         launch_decode_attention(a, c->d_err, c->stream);
         cuda_ok(cudaGetLastError(), "attention launch");
     });

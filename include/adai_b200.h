@@ -76,6 +76,32 @@ ADAI_B200_API int adai_b200_ctx_synchronize(adai_b200_ctx* ctx, double timeout_s
  * and the context is unusable, as after any device timeout; any other status means the path is
  * broken. waited_seconds (may be NULL) receives the host's wall time for the call. */
 ADAI_B200_API int adai_b200_ctx_check_wait_timeout(adai_b200_ctx* ctx, double* waited_seconds);
+/* The last GPU work this context queued, as "<seq> <phase> <kernel>": seq counts the launches
+ * queued so far, phase is the entry point that queued the last one, kernel its name (a replayed
+ * decode step is one launch, "decode step (CUDA graph)"). Replaces describe_last_gpu_work() over
+ * the tag every reference kernel entry point stores (note_gpu_kernel,
+ * src/gpu/GPUDebugSync.cpp:246-253); a failed or timed-out wait appends the same text to
+ * adai_b200_last_error(). `buf` receives at most buf_len - 1 characters and a NUL; launches (may
+ * be NULL) receives seq. */
+ADAI_B200_API int adai_b200_ctx_last_work(adai_b200_ctx* ctx, char* buf, int buf_len,
+                                          unsigned long long* launches);
+/* Debug-sync settings of the process (ADAI_GPU_SYNC / ADAI_GPU_TRACE_FILE,
+ * src/gpu/GPUDebugSync.hpp:5-22), read from ADAI_B200_SYNC (else ADAI_GPU_SYNC) and
+ * ADAI_B200_TRACE_FILE (else ADAI_GPU_TRACE_FILE) on first use:
+ *   mode 0 (off), 1 (step: every entry point waits for its work before it returns), 2 (kernel:
+ *   also wait before every `every`-th launch, and the decode step runs its kernels one by one
+ *   instead of replaying its graph, so a failure names the kernel that ran);
+ *   trace_file: "<seq> <phase> <kernel>" of the last launch, rewritten in place.
+ * Every wait is the bounded one of adai_b200_ctx_synchronize. */
+/* Parses an ADAI_B200_SYNC value: "off", "step", "kernel" or "kernel:N" (1 <= N <= 1000000);
+ * NULL or "" is off. A value it cannot read returns ADAI_B200_ERR_INVALID_ARGUMENT (mode stays
+ * 0), as parse_gpu_debug_settings records a problem and keeps the default. Host only. */
+ADAI_B200_API int adai_b200_debug_sync_parse(const char* value, int* mode, unsigned* every);
+/* Replaces the process's settings (tools and tests; set_gpu_debug_settings_for_testing).
+ * trace_file may be NULL (no file). */
+ADAI_B200_API int adai_b200_debug_configure(int mode, unsigned every, const char* trace_file);
+/* The process's current settings (mode, every). Host only. */
+ADAI_B200_API int adai_b200_debug_settings(int* mode, unsigned* every);
 /* Device bytes this context holds. */
 ADAI_B200_API int adai_b200_ctx_memory(adai_b200_ctx* ctx, unsigned long long* bytes);
 /* The CUDA stream (as void*) the context launches on. */

@@ -71,6 +71,12 @@ class Context {
         check(adai_b200_checkpoint_config(dir.c_str(), &desc_));
     }
     void synchronize(double timeout_s = 0.0) { check(adai_b200_ctx_synchronize(ctx_, timeout_s)); }
+    // "<seq> <phase> <kernel>" of the last GPU work queued (describe_last_gpu_work).
+    std::string last_work() const {
+        char buf[256];
+        check(adai_b200_ctx_last_work(ctx_, buf, static_cast<int>(sizeof(buf)), nullptr));
+        return buf;
+    }
     const adai_b200_model_desc& desc() const { return desc_; }
     adai_b200_ctx* get() const { return ctx_; }
 
