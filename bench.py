@@ -148,18 +148,22 @@ def cpu_reference_tokens_per_s(wl, weights, src, steps, warmup=1, single_steps=0
     first `warmup` steps are untimed, the next `steps` run on all threads, the last
     `single_steps` on one thread (continuing the same sequence)."""
     from oracle.pyoracle import Port, Ref
-    cores = os.cpu_count() or 1
+    # Every host core this process may run on, requested explicitly: torchrun sets
+    # OMP_NUM_THREADS=1 for its ranks, so the OpenMP default team would be one thread there.
+    try:
+        cores = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        cores = os.cpu_count() or 1
     details = {"cpu_model": cpu_model()}
     if Ref.available():
         ref = Ref()
         m = ref.model(wl.model, weights)
-        threads = [0] * (warmup + steps) + [1] * single_steps
+        threads = [cores] * (warmup + steps) + [1] * single_steps
         ids, st, enc_s = m.generate_timed_threads(src, threads)
         kind = "reference"
         t = float(np.sum(st[warmup:warmup + steps]))
         t1 = float(np.sum(st[warmup + steps:])) if single_steps else 0.0
-        details.update(matmul_kernel=ref.matmul_kernel(), encoder_s=enc_s,
-                       omp_threads=int(os.environ.get("OMP_NUM_THREADS", cores)))
+        details.update(matmul_kernel=ref.matmul_kernel(), encoder_s=enc_s, omp_threads=cores)
     else:
         m = Port().model(wl.model, weights)
         t0 = time.perf_counter()

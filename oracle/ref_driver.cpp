@@ -268,14 +268,15 @@ int ref_generate_timed(void* h, const int* src, int S, int bos, int steps, int* 
 
 // ref_generate_timed with a host thread count per step: before step s the OpenMP team size is set
 // to threads[s] (0: unchanged), so one run gives both the all-core and the one-thread rate of the
-// reference's decode after a single encoder pass (run with the default team). The team size is
-// restored afterwards.
+// reference's decode after a single encoder pass (which runs on the first step's team). The team
+// size is restored afterwards.
 int ref_generate_timed_threads(void* h, const int* src, int S, int bos, int steps,
                                const int* threads, int* out_ids, double* step_s, double* enc_s) {
     const int saved = omp_get_max_threads();
     const int rc = guarded([&] {
         auto* m = static_cast<RefModel*>(h);
         using clk = std::chrono::steady_clock;
+        if (threads && steps > 0 && threads[0] > 0) omp_set_num_threads(threads[0]);
         auto t0 = clk::now();
         std::vector<int> v(src, src + S);
         Matrix mask(S, S);
