@@ -57,6 +57,9 @@ constexpr int kBK = 32;  // fp32 elements per 128-byte swizzled row
 template <int BN>
 struct GemmShape {
     static constexpr int kNAcc = (6 * BN <= 512) ? 3 : 2;
+    // TMEM buffers of the accumulators: two (chunks promoted while the next one accumulates), or
+    // one for tiles too wide for two (224 columns, the LM head): the K slice is then one chunk.
+    static constexpr int kTBufs = (2 * kNAcc * BN <= 512) ? 2 : 1;
     // warp 0 TMA producer, warp 1 issuer 0, warps 2-5 epilogue, warps 6.. further issuers
     static constexpr int kWarps = 6 + kNAcc - 1;
     static constexpr int kThreads = 32 * kWarps;
@@ -65,6 +68,7 @@ int threads_for(int bn) {
     switch (bn) {
         case 32: return GemmShape<32>::kThreads;
         case 64: return GemmShape<64>::kThreads;
+        case 224: return GemmShape<224>::kThreads;
         default: return GemmShape<128>::kThreads;
     }
 }
@@ -409,10 +413,11 @@ __global__ void __launch_bounds__(GemmShape<BN>::kThreads, 1) gemm_3xtf32_kernel
             int i = 0, s = 0;
             uint32_t phase = 0;  // parity of stage s's current fill
             const uint32_t smem0 = smem_u32(smem);
+            constexpr int kTB = GemmShape<BN>::kTBufs;
             for (int c = 0; c < nchunks && ok; ++c) {
-                const int b = c & 1;
-                const uint32_t use = static_cast<uint32_t>(c >> 1);
-                if (c >= 2 && !mbar_wait(&tempty_bar[b], (use - 1u) & 1u, p.err, kDevTimeoutAccum)) {
+                const int b = c % kTB;
+                const uint32_t use = static_cast<uint32_t>(c / kTB);
+                if (c >= kTB && !mbar_wait(&tempty_bar[b], (use - 1u) & 1u, p.err, kDevTimeoutAccum)) {
                     ok = false;
                     break;
                 }
@@ -473,44 +478,72 @@ __global__ void __launch_bounds__(GemmShape<BN>::kThreads, 1) gemm_3xtf32_kernel
             ln_rstd[row_local] = rstd;
         }
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-        float acc[BN];
-#pragma unroll
-        for (int j = 0; j < BN; ++j) acc[j] = 0.f;
-        for (int c = 0; c < nchunks; ++c) {
-            const int b = c & 1;
-            int ok = 1;
-            if (lane == 0)
-                ok = mbar_wait(&tfull_bar[b], static_cast<uint32_t>(c >> 1) & 1u, p.err, kDevTimeoutAccum) ? 1 : 0;
+        // This row of the partial tile goes to the staging tile (in the pipeline buffers, free
+        // once every MMA that read them has completed), float4 columns XOR-swizzled by row.
+        const uint32_t row_s = stage_s + static_cast<uint32_t>(row_local * BN * 4);
+        const int sw = row_local & 7;
+        if constexpr (GemmShape<BN>::kTBufs == 1) {
+            // One TMEM buffer and one chunk (the host guarantees nchunks <= 1): the accumulators
+            // stream to the staging tile 16 columns at a time, no register copy of the row.
+            static_assert(GemmShape<BN>::kNAcc == 2, "wide tiles keep two accumulators");
+            int ok = (nchunks == 1) ? 1 : 0;
+            if (lane == 0 && ok) ok = mbar_wait(&tfull_bar[0], 0, p.err, kDevTimeoutAccum) ? 1 : 0;
             ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t t_big = taddr + static_cast<uint32_t>(b * kNAcc * BN);
-#pragma unroll
+            if (ok) tc_fence_after();
+#pragma unroll 2
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 float vb[16], vs[16];
-                tmem_ld_16x2(t_big + c0, t_big + BN + c0, vb, vs);
-                if constexpr (kNAcc == 3) {
-                    float v2[16];
-                    tmem_ld_16(t_big + 2 * BN + c0, v2);
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) acc[c0 + j] += vb[j] + (vs[j] + v2[j]);
+                if (ok) {
+                    tmem_ld_16x2(taddr + c0, taddr + BN + c0, vb, vs);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) acc[c0 + j] += vb[j] + vs[j];
+                    for (int j = 0; j < 16; ++j) vb[j] = vs[j] = 0.f;
+                }
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    const int ch = c0 / 4 + g;
+                    st_shared_f4(row_s + static_cast<uint32_t>((ch ^ sw) * 16), vb[4 * g] + vs[4 * g],
+                                 vb[4 * g + 1] + vs[4 * g + 1], vb[4 * g + 2] + vs[4 * g + 2],
+                                 vb[4 * g + 3] + vs[4 * g + 3]);
                 }
             }
             tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty_bar[b]);
-        }
-        // This row of the partial tile -> the staging tile (the pipeline buffers are free: every
-        // MMA that read them has completed).
-        const uint32_t row_s = stage_s + static_cast<uint32_t>(row_local * BN * 4);
-        const int sw = row_local & 7;
+        } else {
+            float acc[BN];
 #pragma unroll
-        for (int ch = 0; ch < kChunks; ++ch)
-            st_shared_f4(row_s + static_cast<uint32_t>((ch ^ sw) * 16), acc[4 * ch], acc[4 * ch + 1],
-                         acc[4 * ch + 2], acc[4 * ch + 3]);
+            for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+            for (int c = 0; c < nchunks; ++c) {
+                const int b = c & 1;
+                int ok = 1;
+                if (lane == 0)
+                    ok = mbar_wait(&tfull_bar[b], static_cast<uint32_t>(c >> 1) & 1u, p.err, kDevTimeoutAccum) ? 1 : 0;
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t t_big = taddr + static_cast<uint32_t>(b * kNAcc * BN);
+#pragma unroll
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    float vb[16], vs[16];
+                    tmem_ld_16x2(t_big + c0, t_big + BN + c0, vb, vs);
+                    if constexpr (kNAcc == 3) {
+                        float v2[16];
+                        tmem_ld_16(t_big + 2 * BN + c0, v2);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) acc[c0 + j] += vb[j] + (vs[j] + v2[j]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) acc[c0 + j] += vb[j] + vs[j];
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty_bar[b]);
+            }
+#pragma unroll
+            for (int ch = 0; ch < kChunks; ++ch)
+                st_shared_f4(row_s + static_cast<uint32_t>((ch ^ sw) * 16), acc[4 * ch], acc[4 * ch + 1],
+                             acc[4 * ch + 2], acc[4 * ch + 3]);
+        }
         if (S > 1) fence_proxy_async_smem();  // the rows leave by bulk copy (async proxy)
     }
     __syncwarp();
@@ -691,10 +724,12 @@ size_t recv_bytes_for(int bn, int s) {
     return s > 1 ? static_cast<size_t>(s) * rows_per_for(s) * bn * 4 : 0;
 }
 
-// Two TMEM buffers, each with one accumulator of BN columns per MMA issuer.
+// Two TMEM buffers (one when two do not fit), each with one accumulator of BN columns per MMA
+// issuer.
+int tbufs_for(int bn) { return (2 * nacc_for(bn) * bn <= 512) ? 2 : 1; }
 uint32_t tmem_cols_for(int bn) {
     uint32_t cols = 32;
-    while (cols < static_cast<uint32_t>(2 * nacc_for(bn) * bn)) cols <<= 1;
+    while (cols < static_cast<uint32_t>(tbufs_for(bn) * nacc_for(bn) * bn)) cols <<= 1;
     return cols;
 }
 
@@ -720,13 +755,23 @@ GemmKernelFn kernel_for_epi(int flags) {
     }
 }
 
-constexpr int kTileWidths[] = {32, 64, 128};
+constexpr int kTileWidths[] = {32, 64, 128};  // the time model's candidates
+// 224-column tiles exist for the LM head only (143 tiles of a 32000-word vocabulary: one wave).
+constexpr int kWideTile = 224;
 
 GemmKernelFn kernel_for(int bn, int flags) {
     switch (bn) {
         case 32: return kernel_for_epi<32>(flags);
         case 64: return kernel_for_epi<64>(flags);
         case 128: return kernel_for_epi<128>(flags);
+        case kWideTile:
+            switch (flags) {
+                case kEpiSetHead: return gemm_3xtf32_kernel<kWideTile, kEpiSetHead>;
+                case kEpiSetHeadLogits: return gemm_3xtf32_kernel<kWideTile, kEpiSetHeadLogits>;
+                case kEpiSetHeadLn: return gemm_3xtf32_kernel<kWideTile, kEpiSetHeadLn>;
+                case kEpiSetHeadLogitsLn: return gemm_3xtf32_kernel<kWideTile, kEpiSetHeadLogitsLn>;
+                default: return nullptr;
+            }
         default: return nullptr;
     }
 }
@@ -743,9 +788,10 @@ cudaError_t prepare_device_attrs() {
                         kEpiSetHead,        kEpiSetHeadLogits, kEpiSetScatter,   kEpiSetStoreLn,
                         kEpiSetResidStats,  kEpiSetFfnUpLn, kEpiSetFfnDownStats, kEpiSetHeadLn,
                         kEpiSetHeadLogitsLn};
-    for (int bn : kTileWidths)
+    for (int bn : {32, 64, 128, kWideTile})
         for (int f : sets) {
             GemmKernelFn k = kernel_for(bn, f);
+            if (k == nullptr) continue;
             cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  static_cast<int>(kSmemLimit));
             if (e == cudaSuccess)
@@ -821,6 +867,7 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
     {1024, 1024, 32, 4, 4, 8},
     {4096, 1024, 128, 4, 3, 8},
     {1024, 4096, 128, 8, 3, 8},
+    {32000, 1024, kWideTile, 1, 2, 32},  // LM head: 143 tiles, one wave, one TMEM chunk
     {32000, 1024, 128, 1, 3, 8},
     // d_model 512, d_ff 2048, vocab 16000
     {1536, 512, 64, 4, 2, 4},
@@ -851,6 +898,7 @@ bool complete_plan(GemmPlan& p, int M, int N, int K) {
     p.n_tiles = (N + p.bn - 1) / p.bn;
     p.stages = std::max(1, std::min(p.stages, p.kb_per_split));
     p.chunk_kb = std::max(1, std::min(p.chunk_kb, p.kb_per_split));
+    if (tbufs_for(p.bn) == 1) p.chunk_kb = p.kb_per_split;  // one TMEM buffer: one chunk
     p.smem_bytes = std::max(smem_for(p.bn, p.splits, p.stages), tmem_bound_smem(p.bn));
     if (p.smem_bytes > kSmemLimit) return false;
     if (p.splits > 1 && max_active_clusters(p.bn, p.splits, p.smem_bytes) <= 0) return false;
@@ -875,7 +923,7 @@ GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms) {
                     break;
                 q += used;
                 if (*q == ',') ++q;
-                if (mp.n != N || mp.k != K || kernel_for(mp.bn, kEpiSetStore) == nullptr) continue;
+                if (mp.n != N || mp.k != K || kernel_for(mp.bn, flags) == nullptr) continue;
                 GemmPlan p;
                 p.bn = mp.bn;
                 p.splits = mp.splits;
@@ -890,7 +938,7 @@ GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms) {
     }
     if (m_tiles == 1 && !measured) {
         for (const MeasuredPlan& mp : kMeasuredPlans) {
-            if (mp.n != N || mp.k != K) continue;
+            if (mp.n != N || mp.k != K || kernel_for(mp.bn, flags) == nullptr) continue;
             GemmPlan p;
             p.bn = mp.bn;
             p.splits = mp.splits;
@@ -963,7 +1011,6 @@ GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms) {
     // slower per K block).
     if (!measured) best.chunk_kb = std::min(best.kb_per_split, 4);
     best.smem_bytes = std::max(best.smem_bytes, tmem_bound_smem(best.bn));
-    (void)flags;
     return best;
 }
 
@@ -981,6 +1028,7 @@ int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e
     if (kern == nullptr || plan.chunk_kb < 1 || plan.stages < 1) return cudaErrorInvalidValue;
     if (plan.splits < 1 || plan.splits > kMaxCluster || (plan.splits > 1 && kBM % plan.splits))
         return cudaErrorInvalidValue;
+    if (tbufs_for(plan.bn) == 1 && plan.chunk_kb < plan.kb_per_split) return cudaErrorInvalidValue;
     if (plan.smem_bytes > kSmemLimit ||
         plan.smem_bytes < smem_for(plan.bn, plan.splits, plan.stages))
         return cudaErrorInvalidValue;
