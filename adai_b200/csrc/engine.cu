@@ -1953,11 +1953,15 @@ void gemm_run(adai_b200_ctx* c, int m, const float* A, int lda, bool trans_a, fl
     const int rows_alloc = round_up(m, 128);
     const size_t need = static_cast<size_t>(rows_alloc) * kpad;
     const bool direct = reinterpret_cast<uintptr_t>(C) % 16 == 0 && ldc % 4 == 0;
+    // Up to two 128-row tiles of A in its own layout (rows 16-byte aligned) are split inside the
+    // GEMM: one launch. Larger, transposed, scaled or unaligned A goes through the split kernel.
+    const bool fused_split = !trans_a && alpha == 1.0f && rows_alloc <= 256 && lda % 4 == 0 &&
+                             reinterpret_cast<uintptr_t>(A) % 16 == 0;
     const int ldp = round_up(n, 4);
     const size_t need_c = direct ? 0 : static_cast<size_t>(m) * ldp;
-    if (need > c->op_a_floats || need_c > c->op_c_floats) {
+    if ((!fused_split && need > c->op_a_floats) || need_c > c->op_c_floats) {
         cuda_ok(cudaStreamSynchronize(c->stream), "sync");
-        if (need > c->op_a_floats) {
+        if (!fused_split && need > c->op_a_floats) {
             c->dfree(c->op_a_hi);
             c->dfree(c->op_a_lo);
             c->op_a_hi = c->op_a_lo = nullptr;
@@ -1974,15 +1978,27 @@ void gemm_run(adai_b200_ctx* c, int m, const float* A, int lda, bool trans_a, fl
             c->op_c_floats = need_c;
         }
     }
-    c->note("pack_split_a_kernel");
-    pack_split_a_kernel<<<blocks_for(need), 256, 0, c->stream>>>(A, lda, trans_a ? 1 : 0, m, k, alpha,
-                                                                 c->op_a_hi, c->op_a_lo, kpad, rows_alloc);
-    cuda_ok(cudaGetLastError(), "split");
     GemmEpilogue e;
     e.flags = kEpiStore;
     e.out = direct ? C : c->op_c;
     e.ldo = direct ? ldc : ldp;
-    c->gemm(acts(c->op_a_hi, c->op_a_lo, kpad, rows_alloc), m, w->w, e);
+    if (fused_split) {
+        TcActs a;
+        a.K = kpad;
+        a.rows_alloc = rows_alloc;
+        a.fp32 = A;
+        a.lda = lda;
+        a.k_valid = k;
+        a.rows = m;
+        e.flags |= kEpiAFp32;
+        c->gemm(a, m, w->w, e, "gemm_3xtf32_kernel (A split inside)");
+    } else {
+        c->note("pack_split_a_kernel");
+        pack_split_a_kernel<<<blocks_for(need), 256, 0, c->stream>>>(A, lda, trans_a ? 1 : 0, m, k, alpha,
+                                                                     c->op_a_hi, c->op_a_lo, kpad, rows_alloc);
+        cuda_ok(cudaGetLastError(), "split");
+        c->gemm(acts(c->op_a_hi, c->op_a_lo, kpad, rows_alloc), m, w->w, e);
+    }
     if (!direct)
         cuda_ok(cudaMemcpy2DAsync(C, static_cast<size_t>(ldc) * sizeof(float), c->op_c,
                                   static_cast<size_t>(ldp) * sizeof(float), static_cast<size_t>(n) * sizeof(float),

@@ -64,12 +64,13 @@ struct GemmShape {
     static constexpr int kWarps = 6 + kNAcc - 1;
     static constexpr int kThreads = 32 * kWarps;
 };
-int threads_for(int bn) {
+int threads_for(int bn, int flags = 0) {
+    const int conv = (flags & kEpiAFp32) ? 64 : 0;  // the fp32-A converter warps
     switch (bn) {
-        case 32: return GemmShape<32>::kThreads;
-        case 64: return GemmShape<64>::kThreads;
-        case 224: return GemmShape<224>::kThreads;
-        default: return GemmShape<128>::kThreads;
+        case 32: return GemmShape<32>::kThreads + conv;
+        case 64: return GemmShape<64>::kThreads + conv;
+        case 224: return GemmShape<224>::kThreads + conv;
+        default: return GemmShape<128>::kThreads + conv;
     }
 }
 int nacc_for(int bn) { return (6 * bn <= 512) ? 3 : 2; }
@@ -94,6 +95,17 @@ constexpr int kEpiSetFfnUpLn = kEpiBias | kEpiGelu | kEpiSplit | kEpiLnFold;
 constexpr int kEpiSetFfnDownStats = kEpiBias | kEpiResid | kEpiStore | kEpiSplit | kEpiRowStats;
 constexpr int kEpiSetHeadLn = kEpiBias | kEpiArgmax | kEpiLnFold;
 constexpr int kEpiSetHeadLogitsLn = kEpiBias | kEpiArgmax | kEpiStore | kEpiLnFold;
+// The op-level product with A in fp32, split inside the GEMM.
+constexpr int kEpiSetStoreAF = kEpiStore | kEpiAFp32;
+
+// Warps of a launch: the shape's, plus two converter warps when A arrives in fp32.
+template <int BN, int EPI>
+struct GemmWarps {
+    static constexpr bool kAF = (EPI & kEpiAFp32) != 0;
+    static constexpr int kConvWarps = kAF ? 2 : 0;
+    static constexpr int kWarps = GemmShape<BN>::kWarps + kConvWarps;
+    static constexpr int kThreads = 32 * kWarps;
+};
 
 struct __align__(64) GemmKParams {
     CUtensorMap a_hi, a_lo, b_hi, b_lo;
@@ -287,16 +299,19 @@ __device__ __forceinline__ void row_group_stats(float4 v, float2* dst, int lane)
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(GemmShape<BN>::kThreads, 1) gemm_3xtf32_kernel(const __grid_constant__ GemmKParams p) {
-    constexpr int kThreads = GemmShape<BN>::kThreads;
-    constexpr int kWarps = GemmShape<BN>::kWarps;
+__global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_kernel(const __grid_constant__ GemmKParams p) {
+    constexpr int kThreads = GemmWarps<BN, EPI>::kThreads;
+    constexpr int kWarps = GemmWarps<BN, EPI>::kWarps;
+    constexpr bool kAF = GemmWarps<BN, EPI>::kAF;
     constexpr int kNAcc = GemmShape<BN>::kNAcc;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     constexpr bool kArgmax = (EPI & kEpiArgmax) != 0;
     constexpr int b_tile_bytes = BN * kBK * 4;
-    constexpr int stage_bytes = 2 * kATileBytes + 2 * b_tile_bytes;
+    // kAF: a third A plane per stage holds the raw fp32 box TMA brings
+    constexpr int stage_bytes = (kAF ? 3 : 2) * kATileBytes + 2 * b_tile_bytes;
+    constexpr int raw_off = 2 * kATileBytes + 2 * b_tile_bytes;  // kAF: the raw A box in a stage
     constexpr int kChunks = BN / 4;  // float4 columns per output row
     const int stages = p.stages;
     const int S = p.splits;
@@ -318,7 +333,8 @@ __global__ void __launch_bounds__(GemmShape<BN>::kThreads, 1) gemm_3xtf32_kernel
     uint64_t* tempty_bar = tfull_bar + 2;      // [2] TMEM buffer b drained by the epilogue
     uint64_t* recv_bar = tempty_bar + 2;       // peers' partials have landed in `recv`
     uint64_t* done_bar = recv_bar + 1;         // [3] every MMA issuer i issued has completed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 3);
+    uint64_t* a_ready = done_bar + 3;          // [stages] kAF: the converters split the stage's A
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(a_ready + (kAF ? stages : 0));
     int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
     // LayerNorm mean / rstd of the tile's rows (kEpiLnFold), after the 256 bytes of barriers
     float* ln_mean = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full_bar) + 256);
@@ -337,7 +353,7 @@ __global__ void __launch_bounds__(GemmShape<BN>::kThreads, 1) gemm_3xtf32_kernel
 
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&p.a_hi);
-        tma_prefetch_desc(&p.a_lo);
+        if constexpr (!kAF) tma_prefetch_desc(&p.a_lo);
         tma_prefetch_desc(&p.b_hi);
         tma_prefetch_desc(&p.b_lo);
         for (int s = 0; s < stages; ++s) {
@@ -350,6 +366,8 @@ __global__ void __launch_bounds__(GemmShape<BN>::kThreads, 1) gemm_3xtf32_kernel
         }
         mbar_init(recv_bar, 1);
         for (int r = 0; r < 3; ++r) mbar_init(&done_bar[r], 1);
+        if constexpr (kAF)
+            for (int s = 0; s < stages; ++s) mbar_init(&a_ready[s], GemmWarps<BN, EPI>::kConvWarps);
         if (S > 1)  // the phase completes once every peer's rows have arrived
             mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>((S - 1) * rows_per * BN * 4));
         fence_barrier_init();
@@ -371,9 +389,11 @@ __global__ void __launch_bounds__(GemmShape<BN>::kThreads, 1) gemm_3xtf32_kernel
             // Weights are constant: the first stages' weight boxes are requested before waiting
             // for the preceding kernel; the activation boxes only after it.
             const int first = min(stages, nkb);
+            // kAF: one raw A box instead of the two split planes
+            constexpr uint32_t tx_bytes = (kAF ? 1 : 2) * kATileBytes + 2 * b_tile_bytes;
             for (int i = 0; i < first; ++i) {
                 uint8_t* st = smem + static_cast<size_t>(i) * stage_bytes;
-                mbar_arrive_expect_tx(&full_bar[i], static_cast<uint32_t>(stage_bytes));
+                mbar_arrive_expect_tx(&full_bar[i], tx_bytes);
                 const int kx = (kb0 + i) * kBK;
                 tma_load_2d(st + 2 * kATileBytes, &p.b_hi, &full_bar[i], kx, n0);
                 tma_load_2d(st + 2 * kATileBytes + b_tile_bytes, &p.b_lo, &full_bar[i], kx, n0);
@@ -382,8 +402,12 @@ __global__ void __launch_bounds__(GemmShape<BN>::kThreads, 1) gemm_3xtf32_kernel
             for (int i = 0; i < first; ++i) {
                 uint8_t* st = smem + static_cast<size_t>(i) * stage_bytes;
                 const int kx = (kb0 + i) * kBK;
-                tma_load_2d(st, &p.a_hi, &full_bar[i], kx, m0);
-                tma_load_2d(st + kATileBytes, &p.a_lo, &full_bar[i], kx, m0);
+                if constexpr (kAF) {
+                    tma_load_2d(st + raw_off, &p.a_hi, &full_bar[i], kx, m0);  // raw fp32 A
+                } else {
+                    tma_load_2d(st, &p.a_hi, &full_bar[i], kx, m0);
+                    tma_load_2d(st + kATileBytes, &p.a_lo, &full_bar[i], kx, m0);
+                }
             }
             int issued = first;
             for (int i = first; i < nkb; ++i) {
@@ -391,10 +415,14 @@ __global__ void __launch_bounds__(GemmShape<BN>::kThreads, 1) gemm_3xtf32_kernel
                 const uint32_t round = static_cast<uint32_t>(i / stages);
                 if (!mbar_wait(&empty_bar[s], (round & 1u) ^ 1u, p.err, kDevTimeoutSmemEmpty)) break;
                 uint8_t* st = smem + static_cast<size_t>(s) * stage_bytes;
-                mbar_arrive_expect_tx(&full_bar[s], static_cast<uint32_t>(stage_bytes));
+                mbar_arrive_expect_tx(&full_bar[s], tx_bytes);
                 const int kx = (kb0 + i) * kBK;
-                tma_load_2d(st, &p.a_hi, &full_bar[s], kx, m0);
-                tma_load_2d(st + kATileBytes, &p.a_lo, &full_bar[s], kx, m0);
+                if constexpr (kAF) {
+                    tma_load_2d(st + raw_off, &p.a_hi, &full_bar[s], kx, m0);
+                } else {
+                    tma_load_2d(st, &p.a_hi, &full_bar[s], kx, m0);
+                    tma_load_2d(st + kATileBytes, &p.a_lo, &full_bar[s], kx, m0);
+                }
                 tma_load_2d(st + 2 * kATileBytes, &p.b_hi, &full_bar[s], kx, n0);
                 tma_load_2d(st + 2 * kATileBytes + b_tile_bytes, &p.b_lo, &full_bar[s], kx, n0);
                 ++issued;
@@ -404,6 +432,40 @@ __global__ void __launch_bounds__(GemmShape<BN>::kThreads, 1) gemm_3xtf32_kernel
             for (int i = max(0, issued - stages); i < issued; ++i)
                 mbar_wait_drain(&full_bar[i % stages], static_cast<uint32_t>(i / stages) & 1u,
                                 p.err, kDevTimeoutTmaFull);
+        }
+    } else if (kAF && warp >= GemmShape<BN>::kWarps) {
+        // ---- kAF converters: the stage's raw A box (as TMA wrote it, 128-byte swizzled) ->
+        // A_hi and A_lo at the same offsets of their planes (the split is elementwise) ----
+        constexpr int kConv = GemmWarps<BN, EPI>::kConvWarps;
+        constexpr int kVec = kATileBytes / 16;
+        const int cw = warp - GemmShape<BN>::kWarps;
+        const uint32_t smem0 = smem_u32(smem);
+        int s = 0;
+        uint32_t phase = 0;
+        for (int i = 0; i < nkb; ++i) {
+            // every lane waits, so that each sees the copy's bytes
+            const bool got = mbar_wait(&full_bar[s], phase, p.err, kDevTimeoutTmaFull);
+            if (!__all_sync(0xffffffffu, got)) break;
+            const uint32_t st = smem0 + static_cast<uint32_t>(s * stage_bytes);
+#pragma unroll 4
+            for (int v = cw * 32 + lane; v < kVec; v += 32 * kConv) {
+                const uint32_t o = static_cast<uint32_t>(v * 16);
+                const float4 x = ld_shared_f4(st + raw_off + o);
+                float h0, h1, h2, h3, l0, l1, l2, l3;
+                split_tf32(x.x, h0, l0);
+                split_tf32(x.y, h1, l1);
+                split_tf32(x.z, h2, l2);
+                split_tf32(x.w, h3, l3);
+                st_shared_f4(st + o, h0, h1, h2, h3);
+                st_shared_f4(st + kATileBytes + o, l0, l1, l2, l3);
+            }
+            fence_proxy_async_smem();  // the tensor core reads both planes through the async proxy
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_ready[s]);
+            if (++s == stages) {
+                s = 0;
+                phase ^= 1u;
+            }
         }
     } else if (warp == 1 || warp >= 6) {
         // ---- MMA issuers: role 0 (warp 1), 1 (warp 6), 2 (warp 7) ----
@@ -425,7 +487,8 @@ __global__ void __launch_bounds__(GemmShape<BN>::kThreads, 1) gemm_3xtf32_kernel
                 const uint32_t t_acc = tmem_base + static_cast<uint32_t>((b * kNAcc + role) * BN);
                 const int kend = min(nkb, (c + 1) * CK);
                 for (; i < kend; ++i) {
-                    if (!mbar_wait(&full_bar[s], phase, p.err, kDevTimeoutTmaFull)) {
+                    // kAF: the converters waited for the copy and split A
+                    if (!mbar_wait(kAF ? &a_ready[s] : &full_bar[s], phase, p.err, kDevTimeoutTmaFull)) {
                         ok = false;
                         break;
                     }
@@ -698,18 +761,24 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-bool make_map(CUtensorMap* map, const float* base, int K, int rows, int box_rows) {
+// Tensor map of a row-major fp32 matrix [rows, cols] with row stride ld (floats), box 32 x box_rows,
+// 128-byte swizzle; reads past cols or rows fill with zero.
+bool make_map_ld(CUtensorMap* map, const float* base, int cols, int ld, int rows, int box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
-    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (K & 3) != 0) return false;
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 4};
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld & 3) != 0 || cols > ld) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
     cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
+}
+
+bool make_map(CUtensorMap* map, const float* base, int K, int rows, int box_rows) {
+    return make_map_ld(map, base, K, K, rows, box_rows);
 }
 
 size_t stage_bytes_for(int bn) {
@@ -751,6 +820,7 @@ GemmKernelFn kernel_for_epi(int flags) {
         case kEpiSetFfnDownStats: return gemm_3xtf32_kernel<BN, kEpiSetFfnDownStats>;
         case kEpiSetHeadLn: return gemm_3xtf32_kernel<BN, kEpiSetHeadLn>;
         case kEpiSetHeadLogitsLn: return gemm_3xtf32_kernel<BN, kEpiSetHeadLogitsLn>;
+        case kEpiSetStoreAF: return gemm_3xtf32_kernel<BN, kEpiSetStoreAF>;
         default: return nullptr;
     }
 }
@@ -787,7 +857,7 @@ cudaError_t prepare_device_attrs() {
     const int sets[] = {kEpiSetStore,       kEpiSetResid,   kEpiSetFfnUp,        kEpiSetFfnDown,
                         kEpiSetHead,        kEpiSetHeadLogits, kEpiSetScatter,   kEpiSetStoreLn,
                         kEpiSetResidStats,  kEpiSetFfnUpLn, kEpiSetFfnDownStats, kEpiSetHeadLn,
-                        kEpiSetHeadLogitsLn};
+                        kEpiSetHeadLogitsLn, kEpiSetStoreAF};
     for (int bn : {32, 64, 128, kWideTile})
         for (int f : sets) {
             GemmKernelFn k = kernel_for(bn, f);
@@ -1048,20 +1118,38 @@ int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e
          (reinterpret_cast<uintptr_t>(epi.row_stats) & 15) != 0 ||
          (reinterpret_cast<uintptr_t>(epi.ln_c1) & 15) != 0))
         return cudaErrorInvalidValue;
-    // barriers (2 per stage + 8), the TMEM slot and the ticket flag share 256 bytes
-    if ((2 * plan.stages + 8) * 8 + 8 > 256) return cudaErrorInvalidValue;
+    // fp32 A: a third A plane per stage (the raw box) and a third barrier per stage; as many
+    // stages as then fit
+    const bool af = (epi.flags & kEpiAFp32) != 0;
+    GemmPlan pl = plan;
+    if (af) {
+        if (a.fp32 == nullptr || a.k_valid <= 0 || a.k_valid > w.K || a.rows < M)
+            return cudaErrorInvalidValue;
+        auto smem_af = [&](int st) {
+            return std::max(static_cast<size_t>(st) * (stage_bytes_for(pl.bn) + kATileBytes),
+                            smem_for(pl.bn, pl.splits, 1) - kSmemReserve) + kSmemReserve;
+        };
+        while (pl.stages > 1 && (smem_af(pl.stages) > kSmemLimit || 3 * pl.stages + 8 > 31)) --pl.stages;
+        pl.smem_bytes = std::max(pl.smem_bytes, smem_af(pl.stages));
+        if (pl.smem_bytes > kSmemLimit) return cudaErrorInvalidValue;
+    }
+    // barriers (2 per stage + 8, or 3 per stage + 8), the TMEM slot and the ticket flag share 256
+    // bytes
+    if (((af ? 3 : 2) * pl.stages + 8) * 8 + 8 > 256) return cudaErrorInvalidValue;
     const int n_rows_alloc = (w.N + 255) / 256 * 256;
 
     GemmKParams p{};
-    if (!make_map(&p.a_hi, a.hi, a.K, a.rows_alloc, kBM) ||
-        !make_map(&p.a_lo, a.lo, a.K, a.rows_alloc, kBM) ||
+    const bool amaps = af ? make_map_ld(&p.a_hi, a.fp32, a.k_valid, a.lda, a.rows, kBM)
+                          : (make_map(&p.a_hi, a.hi, a.K, a.rows_alloc, kBM) &&
+                             make_map(&p.a_lo, a.lo, a.K, a.rows_alloc, kBM));
+    if (!amaps ||
         !make_map(&p.b_hi, w.hi, w.K, n_rows_alloc, plan.bn) ||
         !make_map(&p.b_lo, w.lo, w.K, n_rows_alloc, plan.bn))
         return cudaErrorInvalidValue;
     p.M = M;
     p.N = w.N;
     p.K = w.K;
-    p.stages = plan.stages;
+    p.stages = pl.stages;
     p.kb_per_split = plan.kb_per_split;
     p.splits = plan.splits;
     p.rows_per = rows_per_for(plan.splits);
@@ -1079,8 +1167,8 @@ int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e
 
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(plan.n_tiles, plan.m_tiles, plan.splits);
-    cfg.blockDim = dim3(threads_for(plan.bn));
-    cfg.dynamicSmemBytes = plan.smem_bytes;
+    cfg.blockDim = dim3(threads_for(plan.bn, epi.flags));
+    cfg.dynamicSmemBytes = pl.smem_bytes;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     int na = 0;

@@ -62,6 +62,10 @@ enum GemmFlags : int {
     // ln_c1 = column sums of diag(gamma) W and the bias holds beta W (+ the layer's own bias).
     // mean / rstd per row come from the K / 32 group statistics in row_stats.
     kEpiLnFold = 256,
+    // Not an epilogue: A arrives in fp32 (TcActs::fp32, row stride lda); TMA brings its boxes
+    // raw and two converter warps split them into tf32 hi / lo in shared memory (the op-level
+    // entry points: one launch instead of a split kernel and the GEMM).
+    kEpiAFp32 = 512,
 };
 
 struct GemmEpilogue {
@@ -104,6 +108,10 @@ struct TcActs {
     int K = 0, rows_alloc = 0;
     const float* hi = nullptr;
     const float* lo = nullptr;
+    // kEpiAFp32: A itself, [rows, k_valid] row-major with row stride lda (a multiple of 4, base
+    // 16-byte aligned); rows past `rows` and columns past k_valid read as zero
+    const float* fp32 = nullptr;
+    int lda = 0, k_valid = 0, rows = 0;
 };
 
 struct GemmPlan {

@@ -105,6 +105,32 @@ def test_gemm_odd_inner_dimension(ctx, torch_cuda):
     assert np.all(np.abs(got - exact) <= gemm_bound(A, B))
 
 
+@pytest.mark.parametrize("m,n,k,lda,off", [(64, 1536, 512, 512, 0), (200, 96, 70, 72, 0),
+                                           (1, 33, 5, 8, 0), (256, 128, 1024, 1028, 0),
+                                           (64, 96, 40, 44, 1), (257, 64, 64, 64, 0)])
+def test_gemm_split_inside_the_gemm_matches_the_split_kernel(ctx, torch_cuda, m, n, k, lda, off):
+    # Up to 256 rows of untransposed, unscaled A with 16-byte aligned rows are split into tf32 hi
+    # and lo inside the GEMM (TMA brings the fp32 box, converter warps split it); a transposed A
+    # takes the separate split kernel. Both must give the same bits: the same split, the same
+    # products. Covered: rows past M, columns past K (K not a multiple of 32), and an A that the
+    # inside split does not take (a base 4 bytes off 16-byte alignment, more than 256 rows).
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + k)
+    buf = torch.randn(m * lda + 4, device="cuda", generator=g)
+    A = buf[off:off + m * lda].view(m, lda)
+    B = torch.randn(k, n, device="cuda", generator=g)
+    C1 = torch.empty(m, n, device="cuda")
+    C2 = torch.empty(m, n, device="cuda")
+    ctx.gemm_strided(0, 0, m, n, k, 1.0, A.data_ptr(), lda, B.data_ptr(), n, C1.data_ptr(), n)
+    At = A[:, :k].t().contiguous()  # [k, m]
+    ctx.gemm_strided(1, 0, m, n, k, 1.0, At.data_ptr(), m, B.data_ptr(), n, C2.data_ptr(), n)
+    torch.cuda.synchronize()
+    assert torch.equal(C1, C2)
+    a64, b64 = A[:, :k].double().cpu().numpy(), B.double().cpu().numpy()
+    bound = 1e-5 + 1e-5 * (np.abs(a64) @ np.abs(b64))
+    assert np.all(np.abs(C1.double().cpu().numpy() - a64 @ b64) <= bound)
+
+
 # ---------------------------------------------------------------------------------------------
 def attention_case(ctx, torch, port, lens, H, cap, append, seed, dh=64):
     rng = np.random.default_rng(seed)
