@@ -1954,9 +1954,12 @@ void gemm_run(adai_b200_ctx* c, int m, const float* A, int lda, bool trans_a, fl
     const size_t need = static_cast<size_t>(rows_alloc) * kpad;
     const bool direct = reinterpret_cast<uintptr_t>(C) % 16 == 0 && ldc % 4 == 0;
     // Up to two 128-row tiles of A in its own layout (rows 16-byte aligned) are split inside the
-    // GEMM: one launch. Larger, transposed, scaled or unaligned A goes through the split kernel.
-    const bool fused_split = !trans_a && alpha == 1.0f && rows_alloc <= 256 && lda % 4 == 0 &&
-                             reinterpret_cast<uintptr_t>(A) % 16 == 0;
+    // GEMM, one launch, when N is at most 8192. Larger, transposed, scaled or unaligned A goes
+    // through the split kernel; so do wide products, where the extra shared-memory plane for the
+    // raw A box costs a pipeline stage (measured on B200: 128 x 1024 x 32000 took 91.5 us split
+    // inside against 66.2 us with the split kernel).
+    const bool fused_split = !trans_a && alpha == 1.0f && rows_alloc <= 256 && n <= 8192 &&
+                             lda % 4 == 0 && reinterpret_cast<uintptr_t>(A) % 16 == 0;
     const int ldp = round_up(n, 4);
     const size_t need_c = direct ? 0 : static_cast<size_t>(m) * ldp;
     if ((!fused_split && need > c->op_a_floats) || need_c > c->op_c_floats) {
