@@ -74,17 +74,52 @@ def dram_traffic(workload: str, kernel_class: str):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """SM clock and clock-event (throttle) reasons sampled every 10 ms while the timed region runs:
+    NVML from a thread (read-only queries), else `nvidia-smi -lms 200` (which needs a region of a
+    few hundred ms to report anything)."""
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.thread = None
+        self.stop = None
         self.lines = []
+        self.samples = []  # (sm MHz, max sm MHz, set of reason names)
+
+    def _poll_nvml(self, nvml, handle, masks):
+        while not self.stop.is_set():
+            try:
+                sm = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
+                mx = nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM)
+                r = nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                self.samples.append((float(sm), float(mx),
+                                     {n for n, m in masks.items() if r & m}))
+            except Exception:
+                pass
+            self.stop.wait(0.01)
 
     def __enter__(self):
+        try:
+            import threading
+
+            import pynvml as nvml
+            nvml.nvmlInit()
+            handle = nvml.nvmlDeviceGetHandleByIndex(self.index)
+            masks = {"hw_slowdown": nvml.nvmlClocksEventReasonHwSlowdown,
+                     "hw_thermal_slowdown": nvml.nvmlClocksEventReasonHwThermalSlowdown,
+                     "sw_thermal_slowdown": nvml.nvmlClocksEventReasonSwThermalSlowdown,
+                     "sw_power_cap": nvml.nvmlClocksEventReasonSwPowerCap}
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._poll_nvml, args=(nvml, handle, masks),
+                                           daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
@@ -95,6 +130,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -103,26 +141,27 @@ class ClockSampler:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            for ln in self.lines:
+                f = [x.strip() for x in ln.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm, mx = float(f[1]), float(f[2])
+                except ValueError:
+                    continue
+                self.samples.append((sm, mx, {n for n, v in zip(self.NAMES, f[5:9])
+                                              if v.lower() == "active"}))
 
     def summary(self):
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
+        if not self.samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
-                "reasons": sorted(reasons), "samples": len(sm)}
+        reasons = set()
+        for _, _, r in self.samples:
+            reasons |= r
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": max(s[1] for s in self.samples), "reasons": sorted(reasons),
+                "samples": len(self.samples),
+                "source": "nvml" if self.thread is not None else "nvidia-smi"}
 
 
 def dist_env():
