@@ -20,6 +20,10 @@
 //   warps 6-7 tcgen05.mma issuers of the correction terms (one warp for both at BN = 128), each
 //             into its own TMEM accumulator
 //   warps 2-5 promote finished TMEM chunks into fp32 registers (one output row per thread)
+// Two variants: 224-column tiles (the LM head, one wave of CTAs) keep a single TMEM buffer, so the
+// K slice is one chunk that the epilogue streams to shared memory 16 columns at a time; and the
+// op-level product of a small fp32 A (kEpiAFp32) lets TMA bring the raw A box into a third plane
+// of each stage, where two more warps split it into A_hi / A_lo before the MMAs read them.
 // Split-K: the S K-slices of a tile are the S CTAs of one thread-block cluster. Each CTA stages
 // its partial tile in its own shared memory and ships the rows it does not own to their owners
 // with one bulk copy per owner (cp.async.bulk shared::cta -> shared::cluster, completing on the
