@@ -985,8 +985,9 @@ GemmPlan gemm_plan(int M, int N, int K, int flags, int num_sms) {
     const int m_tiles = (M + kBM - 1) / kBM;
     const int total_kb = (K + kBK - 1) / kBK;
     bool measured = false;
-    // ADAI_B200_GEMM_PLANS="N:K:bn:splits:stages:chunk,..." replaces table entries (plan tuning).
-    if (m_tiles == 1) {
+    // ADAI_B200_GEMM_PLANS="N:K:bn:splits:stages:chunk,..." replaces the plan of every (N, K) it
+    // names, whatever M (plan tuning; the measured table below holds one-row-tile plans only).
+    {
         if (const char* env = std::getenv("ADAI_B200_GEMM_PLANS")) {
             const char* q = env;
             while (*q && !measured) {
