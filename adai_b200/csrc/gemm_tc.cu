@@ -19,7 +19,9 @@
 //   warp 1    TMEM allocator + tcgen05.mma issuer of A_hi*W_hi
 //   warps 6-7 tcgen05.mma issuers of the correction terms (one warp for both at BN = 128), each
 //             into its own TMEM accumulator
-//   warps 2-5 promote finished TMEM chunks into fp32 registers (one output row per thread)
+//   warps 2-5 promote finished TMEM chunks into fp32 registers (one output row per thread), and
+//             with two TMEM buffers four more warps after the issuers, each pair of warps on one
+//             TMEM lane quarter splitting the row's columns
 // Two variants: 224-column tiles (the LM head, one wave of CTAs) keep a single TMEM buffer, so the
 // K slice is one chunk that the epilogue streams to shared memory 16 columns at a time; and the
 // op-level product of a small fp32 A (kEpiAFp32) lets TMA bring the raw A box into a third plane
@@ -64,8 +66,12 @@ struct GemmShape {
     // TMEM buffers of the accumulators: two (chunks promoted while the next one accumulates), or
     // one for tiles too wide for two (224 columns, the LM head): the K slice is then one chunk.
     static constexpr int kTBufs = (2 * kNAcc * BN <= 512) ? 2 : 1;
-    // warp 0 TMA producer, warp 1 issuer 0, warps 2-5 epilogue, warps 6.. further issuers
-    static constexpr int kWarps = 6 + kNAcc - 1;
+    // warp 0 TMA producer, warp 1 issuer 0, warps 2-5 epilogue, warps 6 .. kIssuerEnd-1 further
+    // issuers; with two TMEM buffers four more epilogue warps follow, so that two warps share
+    // each TMEM lane quarter, each promoting half of the tile's columns.
+    static constexpr int kIssuerEnd = 6 + kNAcc - 1;
+    static constexpr int kEpiWarps = (kTBufs == 2) ? 8 : 4;
+    static constexpr int kWarps = kIssuerEnd + kEpiWarps - 4;
     static constexpr int kThreads = 32 * kWarps;
 };
 int threads_for(int bn, int flags = 0) {
@@ -366,7 +372,7 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull_bar[b], kNAcc);  // one commit per MMA issuer
-            mbar_init(&tempty_bar[b], 4);     // one arrival per epilogue warp
+            mbar_init(&tempty_bar[b], GemmShape<BN>::kEpiWarps);  // one arrival per epilogue warp
         }
         mbar_init(recv_bar, 1);
         for (int r = 0; r < 3; ++r) mbar_init(&done_bar[r], 1);
@@ -471,7 +477,7 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
                 phase ^= 1u;
             }
         }
-    } else if (warp == 1 || warp >= 6) {
+    } else if (warp == 1 || (warp >= 6 && warp < GemmShape<BN>::kIssuerEnd)) {
         // ---- MMA issuers: role 0 (warp 1), 1 (warp 6), 2 (warp 7) ----
         const int role = (warp == 1) ? 0 : warp - 5;
         if (lane == 0 && nkb > 0) {
@@ -532,17 +538,22 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
             mbar_wait_drain(&done_bar[role], 0, p.err, kDevTimeoutAccum);
         }
     } else {
-        // ---- warps 2..5: promote each finished chunk into fp32 registers, one row per thread ----
+        // ---- warps 2..5 (and kIssuerEnd..): promote each finished chunk into fp32 registers,
+        // one row per thread; with eight such warps each owns half of the row's columns ----
         pdl_wait();  // the epilogue reads and writes data of earlier kernels
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int row_local = q * 32 + lane;
+        constexpr int kCols = BN / (GemmShape<BN>::kEpiWarps / 4);  // columns one warp promotes
+        const int c_lo = (warp < 6) ? 0 : kCols;
         if constexpr ((EPI & kEpiLnFold) != 0) {
-            float mean = 0.f, rstd = 0.f;
-            if (m0 + row_local < p.M)
-                ln_row_stats(p.epi.row_stats + static_cast<size_t>(m0 + row_local) * (p.K >> 5),
-                             p.K, mean, rstd);
-            ln_mean[row_local] = mean;
-            ln_rstd[row_local] = rstd;
+            if (c_lo == 0) {  // one warp of the two per lane quarter
+                float mean = 0.f, rstd = 0.f;
+                if (m0 + row_local < p.M)
+                    ln_row_stats(p.epi.row_stats + static_cast<size_t>(m0 + row_local) * (p.K >> 5),
+                                 p.K, mean, rstd);
+                ln_mean[row_local] = mean;
+                ln_rstd[row_local] = rstd;
+            }
         }
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
         // This row of the partial tile goes to the staging tile (in the pipeline buffers, free
@@ -576,9 +587,9 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
             }
             tc_fence_before();
         } else {
-            float acc[BN];
+            float acc[kCols];
 #pragma unroll
-            for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+            for (int j = 0; j < kCols; ++j) acc[j] = 0.f;
             for (int c = 0; c < nchunks; ++c) {
                 const int b = c & 1;
                 int ok = 1;
@@ -587,9 +598,9 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t t_big = taddr + static_cast<uint32_t>(b * kNAcc * BN);
+                const uint32_t t_big = taddr + static_cast<uint32_t>(b * kNAcc * BN + c_lo);
 #pragma unroll
-                for (int c0 = 0; c0 < BN; c0 += 16) {
+                for (int c0 = 0; c0 < kCols; c0 += 16) {
                     float vb[16], vs[16];
                     tmem_ld_16x2(t_big + c0, t_big + BN + c0, vb, vs);
                     if constexpr (kNAcc == 3) {
@@ -607,9 +618,9 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
                 if (lane == 0) mbar_arrive(&tempty_bar[b]);
             }
 #pragma unroll
-            for (int ch = 0; ch < kChunks; ++ch)
-                st_shared_f4(row_s + static_cast<uint32_t>((ch ^ sw) * 16), acc[4 * ch], acc[4 * ch + 1],
-                             acc[4 * ch + 2], acc[4 * ch + 3]);
+            for (int ch = 0; ch < kCols / 4; ++ch)
+                st_shared_f4(row_s + static_cast<uint32_t>(((c_lo / 4 + ch) ^ sw) * 16), acc[4 * ch],
+                             acc[4 * ch + 1], acc[4 * ch + 2], acc[4 * ch + 3]);
         }
         if (S > 1) fence_proxy_async_smem();  // the rows leave by bulk copy (async proxy)
     }
