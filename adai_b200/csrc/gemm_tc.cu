@@ -121,6 +121,7 @@ struct __align__(64) GemmKParams {
     CUtensorMap a_hi, a_lo, b_hi, b_lo;
     int M, N, K;
     int stages, kb_per_split, splits, n_tiles, m_tiles, total_kb, chunk_kb, rows_per;
+    int pair_commit;  // 1: the MMA issuers free the stages two at a time (even stage counts)
     uint32_t idesc, tmem_cols;
     GemmEpilogue epi;
     int* tickets;
@@ -423,7 +424,10 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
             for (int i = first; i < nkb; ++i) {
                 const int s = i % stages;
                 const uint32_t round = static_cast<uint32_t>(i / stages);
-                if (!mbar_wait(&empty_bar[s], (round & 1u) ^ 1u, p.err, kDevTimeoutSmemEmpty)) break;
+                // Stage s last held K block i - stages; with paired commits an even block's stage
+                // is freed by the commit of the odd block after it (the next stage, same round).
+                const int se = (p.pair_commit && !(s & 1)) ? s + 1 : s;
+                if (!mbar_wait(&empty_bar[se], (round & 1u) ^ 1u, p.err, kDevTimeoutSmemEmpty)) break;
                 uint8_t* st = smem + static_cast<size_t>(s) * stage_bytes;
                 mbar_arrive_expect_tx(&full_bar[s], tx_bytes);
                 const int kx = (kb0 + i) * kBK;
@@ -524,7 +528,8 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
                             mma_tf32(t_acc, d_ahi + o, d_blo + o, p.idesc, acc);
                         }
                     }
-                    mma_commit(&empty_bar[s]);
+                    // one commit per two K blocks with paired commits: it tracks both blocks' MMAs
+                    if (!p.pair_commit || (i & 1)) mma_commit(&empty_bar[s]);
                     if (++s == stages) {
                         s = 0;
                         phase ^= 1u;
@@ -1166,6 +1171,7 @@ int gemm_launch(const TcActs& a, int M, const TcWeight& w, const GemmEpilogue& e
     p.N = w.N;
     p.K = w.K;
     p.stages = pl.stages;
+    p.pair_commit = (pl.stages % 2 == 0 && pl.stages >= 4) ? 1 : 0;
     p.kb_per_split = plan.kb_per_split;
     p.splits = plan.splits;
     p.rows_per = rows_per_for(plan.splits);
