@@ -131,6 +131,26 @@ def test_gemm_split_inside_the_gemm_matches_the_split_kernel(ctx, torch_cuda, m,
     assert np.all(np.abs(C1.double().cpu().numpy() - a64 @ b64) <= bound)
 
 
+@pytest.mark.parametrize("m", [64, 300])
+@pytest.mark.parametrize("n,k,plan", [
+    (96, 224, "96:224:32:1:4:2"),      # 7 K blocks (odd) over 4 stages, 2-block chunks
+    (128, 470, "128:470:64:2:4:4"),    # 2-way split-K, 8 + 7 K blocks, ragged last K block
+    (64, 1024, "64:1024:32:1:4:8"),    # 32 K blocks: every stage refilled 7 times
+])
+def test_gemm_forced_pipeline_plans(ctx, torch_cuda, monkeypatch, m, n, k, plan):
+    # Plans with four stages, where the MMA issuers free the stages two at a time, forced through
+    # ADAI_B200_GEMM_PLANS (read at each call): odd K-block counts per split leave an even last
+    # block with no commit of its own. 64 rows take the in-GEMM split of an fp32 A (converter
+    # warps), 300 rows the separate split kernel.
+    monkeypatch.setenv("ADAI_B200_GEMM_PLANS", plan)
+    rng = np.random.default_rng(m + n + k)
+    A = rng.standard_normal((m, k)).astype(np.float32)
+    B = rng.standard_normal((k, n)).astype(np.float32)
+    got = gemm_gpu(ctx, torch_cuda, A, B)
+    exact = A.astype(np.float64) @ B.astype(np.float64)
+    assert np.all(np.abs(got - exact) <= gemm_bound(A, B))
+
+
 # ---------------------------------------------------------------------------------------------
 def attention_case(ctx, torch, port, lens, H, cap, append, seed, dh=64):
     rng = np.random.default_rng(seed)
