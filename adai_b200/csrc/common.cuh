@@ -125,6 +125,11 @@ __device__ __forceinline__ void cluster_sync_all() {
 __device__ __forceinline__ void cluster_arrive_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
+// Arrival of one thread on the cluster barrier, from divergent code: each thread of every CTA
+// of the cluster arrives once (here or with cluster_arrive_all) before it waits.
+__device__ __forceinline__ void cluster_arrive_one() {
+    asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_wait_all() {
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }

@@ -447,6 +447,7 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
                 mbar_wait_drain(&full_bar[i % stages], static_cast<uint32_t>(i / stages) & 1u,
                                 p.err, kDevTimeoutTmaFull);
         }
+        if (S > 1) cluster_arrive_one();  // no copy of this CTA lands in its pipeline any more
     } else if (kAF && warp >= GemmShape<BN>::kWarps) {
         // ---- kAF converters: the stage's raw A box (as TMA wrote it, 128-byte swizzled) ->
         // A_hi and A_lo at the same offsets of their planes (the split is elementwise) ----
@@ -481,6 +482,7 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
                 phase ^= 1u;
             }
         }
+        if (S > 1) cluster_arrive_one();  // done with the raw A planes
     } else if (warp == 1 || (warp >= 6 && warp < GemmShape<BN>::kIssuerEnd)) {
         // ---- MMA issuers: role 0 (warp 1), 1 (warp 6), 2 (warp 7) ----
         const int role = (warp == 1) ? 0 : warp - 5;
@@ -542,9 +544,13 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
             mma_commit(&done_bar[role]);
             mbar_wait_drain(&done_bar[role], 0, p.err, kDevTimeoutAccum);
         }
+        if (S > 1) cluster_arrive_one();  // every MMA of this issuer has read its operands
     } else {
         // ---- warps 2..5 (and kIssuerEnd..): promote each finished chunk into fp32 registers,
         // one row per thread; with eight such warps each owns half of the row's columns ----
+        // These warps write only the staging tile, which the peers' partials do not overlap, so
+        // they arrive on the cluster barrier at once.
+        if (S > 1) cluster_arrive_one();
         pdl_wait();  // the epilogue reads and writes data of earlier kernels
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int row_local = q * 32 + lane;
@@ -636,9 +642,10 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
         tmem_dealloc(tmem_base, p.tmem_cols);
     }
     if (S > 1) {
-        // This CTA's pipeline is drained and its receive barrier initialised: peers may write
-        // into its buffers once every CTA of the cluster has passed this point.
-        cluster_arrive_all();
+        // Peers may write into this CTA's buffers once every thread of the cluster has arrived:
+        // each thread arrived when its role was done with the pipeline buffers (the TMA loads
+        // landed, the MMAs completed, the converters finished), after the receive barrier's
+        // initialisation.
         cluster_wait_all();
         if (threadIdx.x == 0) {
             // rows [o*rows_per, (o+1)*rows_per) of this partial go to rank o, slot `rank`
