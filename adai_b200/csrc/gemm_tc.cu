@@ -361,6 +361,9 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
     const int nkb = max(0, kb1 - kb0);
     const int CK = p.chunk_kb;
     const int nchunks = (nkb + CK - 1) / CK;
+    const int n_first = min(stages, nkb);  // stages filled before the first wait for an empty one
+    // kAF: one raw A box instead of the two split planes
+    constexpr uint32_t tx_bytes = (kAF ? 1 : 2) * kATileBytes + 2 * b_tile_bytes;
 
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&p.a_hi);
@@ -382,6 +385,16 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
         if (S > 1)  // the phase completes once every peer's rows have arrived
             mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>((S - 1) * rows_per * BN * 4));
         fence_barrier_init();
+        // Weights are constant: the first stages' weight boxes are requested as soon as their
+        // barriers exist (before the tensor-memory allocation and the CTA barrier), the
+        // activation boxes only after the wait for the preceding kernel.
+        for (int i = 0; i < n_first; ++i) {
+            uint8_t* st = smem + static_cast<size_t>(i) * stage_bytes;
+            mbar_arrive_expect_tx(&full_bar[i], tx_bytes);
+            const int kx = (kb0 + i) * kBK;
+            tma_load_2d(st + 2 * kATileBytes, &p.b_hi, &full_bar[i], kx, n0);
+            tma_load_2d(st + 2 * kATileBytes + b_tile_bytes, &p.b_lo, &full_bar[i], kx, n0);
+        }
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, p.tmem_cols);
@@ -397,20 +410,9 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
 
     if (warp == 0) {
         if (lane == 0 && nkb > 0) {
-            // Weights are constant: the first stages' weight boxes are requested before waiting
-            // for the preceding kernel; the activation boxes only after it.
-            const int first = min(stages, nkb);
-            // kAF: one raw A box instead of the two split planes
-            constexpr uint32_t tx_bytes = (kAF ? 1 : 2) * kATileBytes + 2 * b_tile_bytes;
-            for (int i = 0; i < first; ++i) {
-                uint8_t* st = smem + static_cast<size_t>(i) * stage_bytes;
-                mbar_arrive_expect_tx(&full_bar[i], tx_bytes);
-                const int kx = (kb0 + i) * kBK;
-                tma_load_2d(st + 2 * kATileBytes, &p.b_hi, &full_bar[i], kx, n0);
-                tma_load_2d(st + 2 * kATileBytes + b_tile_bytes, &p.b_lo, &full_bar[i], kx, n0);
-            }
+            // (the first stages' weight boxes are on their way: see the barrier set-up)
             pdl_wait();
-            for (int i = 0; i < first; ++i) {
+            for (int i = 0; i < n_first; ++i) {
                 uint8_t* st = smem + static_cast<size_t>(i) * stage_bytes;
                 const int kx = (kb0 + i) * kBK;
                 if constexpr (kAF) {
@@ -420,8 +422,8 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
                     tma_load_2d(st + kATileBytes, &p.a_lo, &full_bar[i], kx, m0);
                 }
             }
-            int issued = first;
-            for (int i = first; i < nkb; ++i) {
+            int issued = n_first;
+            for (int i = n_first; i < nkb; ++i) {
                 const int s = i % stages;
                 const uint32_t round = static_cast<uint32_t>(i / stages);
                 // Stage s last held K block i - stages; with paired commits an even block's stage
