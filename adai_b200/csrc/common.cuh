@@ -195,6 +195,10 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
 
 // ---------------------------------------------------------------------------------------------
 // TMA (tiled tensor copies, no multicast)
+// Request the 128-byte line holding `ptr` into L1 (no register result, no wait).
+__device__ __forceinline__ void prefetch_l1(const void* ptr) {
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<uint64_t>(ptr)));
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -661,6 +661,20 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
             }
             bulk_commit();
         }
+        if constexpr ((EPI & kEpiResid) != 0) {
+            // The epilogue's residual rows (written by earlier kernels: every thread is past the
+            // CTA barrier that follows the epilogue warps' wait for them) are requested into L1
+            // while the peers' partials travel.
+            constexpr int kLines = (BN * 4 + 127) / 128;
+            const int rl0 = rank * rows_per;
+            const int rn = max(0, min(kBM, rl0 + rows_per) - rl0);
+            for (int it = threadIdx.x; it < rn * kLines; it += kThreads) {
+                const int row = m0 + rl0 + it / kLines;
+                const int col = n0 + (it % kLines) * 32;
+                if (row < p.M && col < p.N)
+                    prefetch_l1(p.epi.resid + static_cast<size_t>(row) * p.epi.ldr + col);
+            }
+        }
         // Peers' rows of this rank are here. After an abort elsewhere still drain: no copy may
         // land in this CTA's memory after it exits.
         if (!mbar_wait(recv_bar, 0, p.err, kDevTimeoutAccum))
