@@ -402,8 +402,6 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
     }
     __syncthreads();
     tc_fence_after();
-    // The next kernel in the stream may begin its own prologue (it waits before touching data).
-    pdl_trigger();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t stage_s = smem_u32(stage_out);
     const uint32_t recv_s = smem_u32(recv);
@@ -639,6 +637,8 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
     }
     __syncwarp();
     __syncthreads();  // staging tile complete
+    // The next kernel in the stream may begin its own prologue (it waits before touching data).
+    pdl_trigger();
     if (warp == 1) {  // accumulators drained: give the tensor memory back early
         tc_fence_after();
         tmem_dealloc(tmem_base, p.tmem_cols);
