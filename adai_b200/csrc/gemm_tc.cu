@@ -638,6 +638,8 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
     __syncwarp();
     __syncthreads();  // staging tile complete
     // The next kernel in the stream may begin its own prologue (it waits before touching data).
+    // Not earlier: an attention kernel's CTAs fit beside this one and would start streaming their
+    // cached rows while the K loop still needs the memory system (measured slower).
     pdl_trigger();
     if (warp == 1) {  // accumulators drained: give the tensor memory back early
         tc_fence_after();
