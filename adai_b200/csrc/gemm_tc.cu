@@ -362,6 +362,8 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
     const int CK = p.chunk_kb;
     const int nchunks = (nkb + CK - 1) / CK;
     const int n_first = min(stages, nkb);  // stages filled before the first wait for an empty one
+    // Each weight box is read by one CTA once: its lines go first when L2 needs room.
+    const uint64_t w_policy = (warp == 0 && lane == 0) ? l2_policy_evict_first() : 0;
     // kAF: one raw A box instead of the two split planes
     constexpr uint32_t tx_bytes = (kAF ? 1 : 2) * kATileBytes + 2 * b_tile_bytes;
 
@@ -392,8 +394,8 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
             uint8_t* st = smem + static_cast<size_t>(i) * stage_bytes;
             mbar_arrive_expect_tx(&full_bar[i], tx_bytes);
             const int kx = (kb0 + i) * kBK;
-            tma_load_2d(st + 2 * kATileBytes, &p.b_hi, &full_bar[i], kx, n0);
-            tma_load_2d(st + 2 * kATileBytes + b_tile_bytes, &p.b_lo, &full_bar[i], kx, n0);
+            tma_load_2d_hint(st + 2 * kATileBytes, &p.b_hi, &full_bar[i], kx, n0, w_policy);
+            tma_load_2d_hint(st + 2 * kATileBytes + b_tile_bytes, &p.b_lo, &full_bar[i], kx, n0, w_policy);
         }
     }
     if (warp == 1) {
@@ -437,8 +439,8 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
                     tma_load_2d(st, &p.a_hi, &full_bar[s], kx, m0);
                     tma_load_2d(st + kATileBytes, &p.a_lo, &full_bar[s], kx, m0);
                 }
-                tma_load_2d(st + 2 * kATileBytes, &p.b_hi, &full_bar[s], kx, n0);
-                tma_load_2d(st + 2 * kATileBytes + b_tile_bytes, &p.b_lo, &full_bar[s], kx, n0);
+                tma_load_2d_hint(st + 2 * kATileBytes, &p.b_hi, &full_bar[s], kx, n0, w_policy);
+                tma_load_2d_hint(st + 2 * kATileBytes + b_tile_bytes, &p.b_lo, &full_bar[s], kx, n0, w_policy);
                 ++issued;
             }
             // No copy may still be landing in shared memory when the CTA moves on, also after an
