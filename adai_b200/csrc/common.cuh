@@ -225,6 +225,12 @@ __device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorM
 }
 
 // An L2 policy under which the lines a load brings in are the first to be evicted (data read once).
+// An L2 policy under which the lines a load brings in are kept longest (data read many times).
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t policy;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));

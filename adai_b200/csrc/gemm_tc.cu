@@ -364,6 +364,8 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
     const int n_first = min(stages, nkb);  // stages filled before the first wait for an empty one
     // Each weight box is read by one CTA once: its lines go first when L2 needs room.
     const uint64_t w_policy = (warp == 0 && lane == 0) ? l2_policy_evict_first() : 0;
+    // The activation boxes are read by every N tile's CTA: kept longest.
+    const uint64_t a_policy = (warp == 0 && lane == 0) ? l2_policy_evict_last() : 0;
     // kAF: one raw A box instead of the two split planes
     constexpr uint32_t tx_bytes = (kAF ? 1 : 2) * kATileBytes + 2 * b_tile_bytes;
 
@@ -418,8 +420,8 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
                 if constexpr (kAF) {
                     tma_load_2d(st + raw_off, &p.a_hi, &full_bar[i], kx, m0);  // raw fp32 A
                 } else {
-                    tma_load_2d(st, &p.a_hi, &full_bar[i], kx, m0);
-                    tma_load_2d(st + kATileBytes, &p.a_lo, &full_bar[i], kx, m0);
+                    tma_load_2d_hint(st, &p.a_hi, &full_bar[i], kx, m0, a_policy);
+                    tma_load_2d_hint(st + kATileBytes, &p.a_lo, &full_bar[i], kx, m0, a_policy);
                 }
             }
             int issued = n_first;
@@ -436,8 +438,8 @@ __global__ void __launch_bounds__(GemmWarps<BN, EPI>::kThreads, 1) gemm_3xtf32_k
                 if constexpr (kAF) {
                     tma_load_2d(st + raw_off, &p.a_hi, &full_bar[s], kx, m0);
                 } else {
-                    tma_load_2d(st, &p.a_hi, &full_bar[s], kx, m0);
-                    tma_load_2d(st + kATileBytes, &p.a_lo, &full_bar[s], kx, m0);
+                    tma_load_2d_hint(st, &p.a_hi, &full_bar[s], kx, m0, a_policy);
+                    tma_load_2d_hint(st + kATileBytes, &p.a_lo, &full_bar[s], kx, m0, a_policy);
                 }
                 tma_load_2d_hint(st + 2 * kATileBytes, &p.b_hi, &full_bar[s], kx, n0, w_policy);
                 tma_load_2d_hint(st + 2 * kATileBytes + b_tile_bytes, &p.b_lo, &full_bar[s], kx, n0, w_policy);
